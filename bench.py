@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Benchmark of the BF16X fused decode+GEMV hot path.
+
+One step = one pass of the fused decode+GEMV over the four benchmark weight
+shapes ([out x in] = 4096x4096, 14336x4096, 4096x14336, 128256x4096) at the
+chosen batch (default 1), weights resident in HBM in the kernel layout,
+activations bf16 N(0,1).  ~950 MB of compressed weights per step, far larger
+than the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Multi-GPU (launched by torchrun, one rank per GPU): weights are sharded by
+output rows with no collective on the data path.  Default weak scaling: each
+rank holds a [out x in] row shard of a [N*out x in] weight, so per-GPU work
+is fixed; --scaling strong splits the [out x in] weights N ways instead.
+
+Rank 0 prints one JSON line.  `value` is the whole-job compressed-byte
+throughput (resident layout + patch table + activations + outputs, summed
+over ranks, divided by the max-over-ranks device time of K steps).
+`--impl reference` times the reference's CPU decode+matmul path (the C
+oracle port, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode+GEMV GB/s (frac of 8 TB/s) & tok/s; decode+GEMM prefill TFLOPS"
+SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--shapes", default="", help="e.g. 4096x4096,128256x4096 (default: all four)")
+    ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def shapes_of(args):
+    if not args.shapes:
+        return SHAPES
+    return [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
+
+
+def workload_name(args, shapes):
+    return ("configs[1] fused decode+GEMV sweep: " + ", ".join(f"{o}x{i}" for o, i in shapes) +
+            f" at batch {args.batch}")
+
+
+def peak_hbm():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_from_profile(kernel_key):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d.get(kernel_key)
+    except Exception:
+        return None
+
+
+# --------------------------------------------------------------------------- #
+# CPU side (reference arm and cpu_baseline): the C oracle port                 #
+# --------------------------------------------------------------------------- #
+def cpu_sample(batch: int, seconds: float):
+    """Time the CPU decode+matmul (oracle port of BF16XLinear.forward) on a
+    4096x4096 sample; returns (bytes per pass, seconds per pass, cores, passes)."""
+    import numpy as np
+    import torch
+
+    from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
+    from oracle import oracle
+
+    out_f, in_f = 4096, 4096
+    w = synthetic_weight(out_f, in_f, seed=0)
+    bits = w.view(torch.int16).numpy().view(np.uint16)
+    p = oracle.quantize(bits, out_f, in_f)
+    x = synthetic_activation(batch, in_f, seed=1).float().numpy()
+    n_patch = int((p["delta_ovf_val"] > 7).sum())
+    nbytes = workload_bytes(out_f, in_f, n_patch, batch)
+    oracle.linear(p, x)   # warm
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        oracle.linear(p, x)
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return nbytes, el / passes, oracle.num_threads(), passes
+
+
+def workload_bytes(rows, in_f, n_patch, batch, y_bytes=2):
+    """Bytes one fused decode+GEMV launch must move: resident layout + patch
+    table + patch offsets + activations + outputs."""
+    row_bytes = (in_f + 255) // 256 * 368
+    return rows * row_bytes + 4 * n_patch + 4 * (rows + 1) + 2 * batch * in_f + y_bytes * batch * rows
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps, warmup = args.steps, args.warmup
+    import numpy as np
+    import torch
+
+    from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
+    from oracle import oracle
+
+    shapes = shapes_of(args)
+    w = synthetic_weight(4096, 4096, seed=0)
+    bits = w.view(torch.int16).numpy().view(np.uint16)
+    p = oracle.quantize(bits, 4096, 4096)
+    x = synthetic_activation(args.batch, 4096, seed=1).float().numpy()
+    nbytes = workload_bytes(4096, 4096, int((p["delta_ovf_val"] > 7).sum()), args.batch)
+    for _ in range(warmup):
+        oracle.linear(p, x)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.linear(p, x)
+    el = time.perf_counter() - t0
+    v = nbytes * steps / el / 1e9
+    sample = ("one 4096x4096 BF16X weight (same synthetic distribution) per step: CPU oracle port of "
+              "BF16XLinear.forward (opqk_linear.py:390-404), tile decode + fp32 matmul, batch %d" % args.batch)
+    line = {
+        "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warmup, "ms_per_step": round(el / steps * 1e3, 3),
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights with 0.5% x 2^U{4..8} outliers, bf16 N(0,1) activations)",
+        "config": {"workload": workload_name(args, shapes), "batch": args.batch},
+        "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": oracle.num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- #
+# GPU side                                                                     #
+# --------------------------------------------------------------------------- #
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.strip().split(", ") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except Exception:
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    from bfloat16x_b200 import _lib
+    from bfloat16x_b200.opqk_linear import bf16x_quantize
+    from bfloat16x_b200.resident import ResidentWeight
+    from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
+
+    B = args.batch
+    shapes = shapes_of(args)
+    layers = []
+    for si, (out_f, in_f) in enumerate(shapes):
+        if args.scaling == "weak":
+            rows = out_f
+        else:
+            base = out_f // world
+            rows = base + (out_f % world if rank == world - 1 else 0)
+        w = synthetic_weight(rows, in_f, seed=1000 * si + rank, device=dev)
+        p = bf16x_quantize(w, device=dev)
+        rw = ResidentWeight.from_packed(p, device=dev)
+        del p
+        wb = None if args.no_cublas else w
+        del w
+        x = synthetic_activation(B, in_f, seed=si + 1, device=dev)
+        y = torch.empty((B, rows), dtype=torch.bfloat16, device=dev)
+        layers.append(dict(rw=rw, x=x, y=y, w=wb, rows=rows, in_f=in_f,
+                           nbytes=workload_bytes(rows, in_f, rw.n_patches, B)))
+    torch.cuda.synchronize()
+
+    def step():
+        for L in layers:
+            L["rw"].gemv(L["x"], out=L["y"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # ---------------- device-resident timing (value) --------------------------
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    clock = ClockSampler(local)
+    clock.start()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in layers for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    t_start.record()
+    k = 0
+    for _ in range(args.steps):
+        for L in layers:
+            ev[k][0].record()
+            L["rw"].gemv(L["x"], out=L["y"])
+            ev[k][1].record()
+            k += 1
+    t_end.record()
+    barrier()
+    clocks = clock.stop()
+    el_ms = t_start.elapsed_time(t_end)
+    per_layer_ms = [0.0] * len(layers)
+    k = 0
+    for _ in range(args.steps):
+        for i in range(len(layers)):
+            per_layer_ms[i] += ev[k][0].elapsed_time(ev[k][1])
+            k += 1
+    per_layer_ms = [v / args.steps for v in per_layer_ms]
+    el_max = max_over_ranks(el_ms)
+    step_bytes = sum(L["nbytes"] for L in layers)
+    total_bytes = sum_over_ranks(step_bytes * args.steps)
+    value = total_bytes / (el_max / 1e3) / 1e9
+    _lib.check_device_status(local)
+
+    # dominant kernel: the launch with the largest share of device time
+    dom = max(range(len(layers)), key=lambda i: per_layer_ms[i])
+    Ld = layers[dom]
+    achieved = Ld["nbytes"] / (per_layer_ms[dom] / 1e3) / 1e9
+    peak, peak_kind = peak_hbm()
+    kernel_key = f"gemv_b{B}_{Ld['rows']}x{Ld['in_f']}"
+
+    # ---------------- end-to-end through the public API, host buffers ---------
+    e2e = None
+    if not args.no_e2e:
+        hx = [L["x"].cpu().pin_memory() for L in layers]
+        hy = [torch.empty((B, L["rows"]), dtype=torch.bfloat16).pin_memory() for L in layers]
+        dx = [torch.empty_like(L["x"]) for L in layers]
+
+        def e2e_step():
+            for i, L in enumerate(layers):
+                dx[i].copy_(hx[i], non_blocking=True)
+                L["rw"].gemv(dx[i], out=L["y"])
+                hy[i].copy_(L["y"], non_blocking=True)
+
+        for _ in range(max(args.warmup, 3)):
+            e2e_step()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            e2e_step()
+        b.record()
+        barrier()
+        e_max = max_over_ranks(a.elapsed_time(b))
+        e2e = {"value": round(total_bytes / (e_max / 1e3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": sum(t.numel() * 2 for t in hx) * world,
+               "d2h_bytes_per_step": sum(t.numel() * 2 for t in hy) * world,
+               "path": "ResidentWeight.gemv (module forward path): pinned x -> H2D, fused kernel, D2H y",
+               "ms_per_step": round(e_max / args.steps, 4)}
+
+    # ---------------- cuBLAS bf16 GEMV on the same shapes ----------------------
+    cublas = None
+    if not args.no_cublas:
+        import torch.nn.functional as F
+        for _ in range(3):
+            for L in layers:
+                F.linear(L["x"], L["w"])
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            for L in layers:
+                F.linear(L["x"], L["w"])
+        b.record()
+        barrier()
+        c_ms = max_over_ranks(a.elapsed_time(b)) / args.steps
+        cublas = {"ms_per_step": round(c_ms, 4), "speedup_vs_cublas_bf16": round(c_ms / (el_max / args.steps), 3),
+                  "bf16_bytes_per_step": sum(L["rows"] * L["in_f"] * 2 for L in layers)}
+
+    # ---------------- CPU baseline (rank 0, N=1) ---------------------------------
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        nb, sec, cores, passes = cpu_sample(B, args.cpu_seconds)
+        cpu = {"value": round(nb / sec / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"4096x4096 batch-{B} decode+matmul with the C oracle port of BF16XLinear.forward "
+                         f"(OpenMP, {cores} threads), {passes} passes in {sec * passes:.1f} s"}
+
+    if rank == 0:
+        ms_step = el_max / args.steps
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights with 0.5% x 2^U{4..8} outliers, bf16 N(0,1) activations)",
+            "config": {"workload": workload_name(args, shapes), "batch": B,
+                       "parallelism": f"row-shard x{world} ({args.scaling})",
+                       "l2": "inputs larger than L2 (%.0f MB of weights per step per GPU)" % (step_bytes / 1e6),
+                       "resident_bpw": round(8 * sum(L['rw'].nbytes() for L in layers) /
+                                             sum(L['rows'] * L['in_f'] for L in layers), 3)},
+            "frac_of_8TBs": round(value / world / 8000.0, 4),
+            "tok_s": round(B / (ms_step / 1e3), 1),
+            "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per_layer_ms[i], 4) for i, L in enumerate(layers)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "kernel": f"gemv_kernel (fused decode+GEMV) {Ld['rows']}x{Ld['in_f']} batch {B}",
+                         "traffic": traffic_from_profile(kernel_key)},
+            "gpu_launches": args.steps * len(layers),
+            "clocks": clocks,
+            "e2e": e2e,
+            "cublas_bf16": cublas,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,171 @@
+"""Device-resident BF16X weights in the kernel layout.
+
+``ResidentWeight`` is what the fused Linear modules hold: the weight rows in
+the resident layout (chunks of 256 columns, 368 bytes each: sign|mant bytes,
+pair-aligned 3-bit deltas, row-local emax -- 11.5 bits per weight) plus a
+per-row CSR of exact-delta patches for the ~3% of weights whose exponent is
+more than 7 below their sub-block maximum.  It is built once from a
+bf16x_quantize dict by the ``bf16x_repack_count`` / ``bf16x_repack`` kernels
+(the counterpart of the reference modules' device preparation,
+bf16x_fused.py:154-192 and bf16x_gemm_fused.py:163-184) and can hold a row
+range only (tensor-parallel shards by output rows).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import BF16X_DTYPE_BF16, BF16X_DTYPE_F32, CHUNK_BYTES, CHUNK_ELEMS, call, ptr
+
+_FLAT = ("sign_packed", "mant_packed", "delta_packed", "emax", "delta_ovf_idx", "delta_ovf_val")
+
+GEMV_MAX_BATCH = 8
+
+
+def _as_dev(t: torch.Tensor, dtype, dev) -> torch.Tensor:
+    return t.to(device=dev, dtype=dtype, non_blocking=True).contiguous()
+
+
+def flat_on_device(p: dict, dev) -> dict:
+    """The dict's streams as contiguous device tensors of the C-ABI dtypes."""
+    out = {
+        "sign_packed": _as_dev(p["sign_packed"], torch.int32, dev),
+        "mant_packed": _as_dev(p["mant_packed"], torch.int32, dev),
+        "delta_packed": _as_dev(p["delta_packed"], torch.int32, dev),
+        "emax": _as_dev(p["emax"], torch.uint8, dev),
+        "delta_ovf_idx": _as_dev(p["delta_ovf_idx"], torch.int32, dev),
+        "delta_ovf_val": _as_dev(p["delta_ovf_val"], torch.uint8, dev),
+    }
+    return out
+
+
+def flat_args(f: dict):
+    """Positional stream arguments of the flat-stream C entry points."""
+    n_ovf = f["delta_ovf_idx"].numel()
+    return (ptr(f["sign_packed"]), f["sign_packed"].numel(), ptr(f["mant_packed"]), f["mant_packed"].numel(),
+            ptr(f["delta_packed"]), f["delta_packed"].numel(), ptr(f["emax"]), f["emax"].numel(),
+            ptr(f["delta_ovf_idx"]) if n_ovf else None, ptr(f["delta_ovf_val"]) if n_ovf else None, n_ovf)
+
+
+class ResidentWeight:
+    """Rows [row0, row1) of a BF16X weight in the resident kernel layout."""
+
+    def __init__(self, layout: torch.Tensor, patch_off: torch.Tensor, patches: torch.Tensor,
+                 rows: int, in_f: int, out_f: int | None = None, row0: int = 0):
+        self.layout = layout
+        self.patch_off = patch_off
+        self.patches = patches
+        self.rows = int(rows)
+        self.in_f = int(in_f)
+        self.out_f = int(out_f if out_f is not None else rows)
+        self.row0 = int(row0)
+
+    # ------------------------------------------------------------------ build
+    @classmethod
+    @torch.no_grad()
+    def from_packed(cls, p: dict, device=None, row_range: tuple | None = None) -> "ResidentWeight":
+        out_f, in_f = int(p["out_f"]), int(p["in_f"])
+        if int(p.get("sub", 16)) != 16:
+            raise ValueError("only sub=16 dicts are supported")
+        if device is None:
+            device = p["sign_packed"].device if p["sign_packed"].is_cuda else torch.device(
+                "cuda", torch.cuda.current_device())
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            raise _lib.Bf16xError("ResidentWeight lives on a CUDA device")
+        r0, r1 = (0, out_f) if row_range is None else (int(row_range[0]), int(row_range[1]))
+        rows = r1 - r0
+        f = flat_on_device(p, dev)
+        row_bytes = int(_lib.lib().bf16x_resident_row_bytes(in_f))
+        with torch.cuda.device(dev):
+            st = torch.cuda.current_stream(dev).cuda_stream
+            patch_off = torch.empty(rows + 1, dtype=torch.int32, device=dev)
+            call("bf16x_repack_count", *flat_args(f), out_f, in_f, r0, r1, ptr(patch_off), st)
+            n_patch = int(patch_off[rows].item())
+            layout = torch.empty((rows, row_bytes), dtype=torch.uint8, device=dev)
+            patches = torch.empty(max(n_patch, 1), dtype=torch.int32, device=dev)
+            call("bf16x_repack", *flat_args(f), out_f, in_f, r0, r1, ptr(patch_off), ptr(layout),
+                 ptr(patches), st)
+            _lib.check_device_status(dev.index)
+        return cls(layout, patch_off, patches, rows, in_f, out_f=out_f, row0=r0)
+
+    # ------------------------------------------------------------ properties
+    @property
+    def device(self) -> torch.device:
+        return self.layout.device
+
+    @property
+    def in_pad(self) -> int:
+        return (self.in_f + CHUNK_ELEMS - 1) // CHUNK_ELEMS * CHUNK_ELEMS
+
+    @property
+    def row_bytes(self) -> int:
+        return self.layout.shape[1]
+
+    @property
+    def n_patches(self) -> int:
+        return int(self.patch_off[-1].item())
+
+    def nbytes(self) -> int:
+        """Bytes the fused kernels stream per full pass: layout + patch table + offsets."""
+        return self.layout.numel() + 4 * self.n_patches + 4 * self.patch_off.numel()
+
+    def bits_per_weight(self) -> float:
+        return 8.0 * self.nbytes() / max(1, self.rows * self.in_f)
+
+    # -------------------------------------------------------------- compute
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def decode(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Exact bf16 weight rows [rows, in_f]."""
+        if out is None:
+            out = torch.empty((self.rows, self.in_f), dtype=torch.bfloat16, device=self.device)
+        with torch.cuda.device(self.device):
+            call("bf16x_resident_decode", ptr(self.layout), ptr(self.patch_off), ptr(self.patches),
+                 self.rows, self.in_f, ptr(out), out.stride(0), self._stream())
+        return out
+
+    def _prep_x(self, x2: torch.Tensor) -> torch.Tensor:
+        """bf16 activations with a row pitch covering the padded columns (zeros)."""
+        x2 = x2.to(torch.bfloat16)
+        if (self.in_f % CHUNK_ELEMS == 0 and x2.is_contiguous() and x2.data_ptr() % 16 == 0):
+            return x2
+        xp = torch.zeros((x2.shape[0], self.in_pad), dtype=torch.bfloat16, device=self.device)
+        xp[:, : self.in_f] = x2
+        return xp
+
+    def gemv(self, x: torch.Tensor, bias: torch.Tensor | None = None,
+             out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y[b, n] = sum_k W[n, k] x[b, k] (+ bias) for a batch of <= 8 rows."""
+        _lib.require_cuda(x, "x")
+        x2 = x.reshape(-1, self.in_f)
+        B = x2.shape[0]
+        if B < 1 or B > GEMV_MAX_BATCH:
+            raise ValueError(f"gemv takes 1..{GEMV_MAX_BATCH} rows of activations, got {B}")
+        xp = self._prep_x(x2)
+        if out is None:
+            out = torch.empty((B, self.rows), dtype=out_dtype, device=self.device)
+        ydt = {torch.bfloat16: BF16X_DTYPE_BF16, torch.float32: BF16X_DTYPE_F32}[out.dtype]
+        b = None
+        if bias is not None:
+            b = bias.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        with torch.cuda.device(self.device):
+            call("bf16x_gemv", ptr(self.layout), ptr(self.patch_off), ptr(self.patches), self.rows, self.in_f,
+                 ptr(xp), B, xp.stride(0), ptr(b), ptr(out), ydt, out.stride(0), self._stream())
+        return out
+
+    def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None,
+               out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        """x[..., in_f] -> [..., rows] with the fused kernels."""
+        od = out_dtype or (x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.bfloat16)
+        x2 = x.reshape(-1, self.in_f)
+        M = x2.shape[0]
+        y = torch.empty((M, self.rows), dtype=od, device=self.device)
+        for m0 in range(0, M, GEMV_MAX_BATCH):
+            m1 = min(M, m0 + GEMV_MAX_BATCH)
+            self.gemv(x2[m0:m1], bias, out=y[m0:m1])
+        return y.reshape(*x.shape[:-1], self.rows)
+
+
+__all__ = ["ResidentWeight", "flat_on_device", "flat_args", "GEMV_MAX_BATCH"]

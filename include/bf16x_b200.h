@@ -1,0 +1,141 @@
+/*
+ * bf16x_b200.h -- C ABI of the B200-native BF16X hot path.
+ *
+ * Plain pointers and sizes, no framework types.  All pointers are device
+ * pointers unless stated otherwise; `stream` is a cudaStream_t.  Every
+ * function returns BF16X_OK (0) or a negative status; bf16x_last_error()
+ * returns the message of the last failure on the calling host thread.
+ * Nothing allocates device memory except where a function says so.
+ *
+ * The reference (dfytensor/bfloat16x) has no C ABI: its boundary is a Python
+ * API.  Each entry point below names the reference function it replaces
+ * (file:line within the reference project); the Python package
+ * bfloat16x_b200 mirrors those Python functions on top of this ABI.
+ *
+ * Formats
+ *   flat streams   : the bf16x_quantize dict (opqk_linear.py:291-324): LSB-first
+ *                    int32 bit streams sign (1 b/elt), mant (7 b), delta (3 b,
+ *                    7 = saturated), emax (u8 per 16 flat elements), overflow
+ *                    table idx (int32 ascending flat positions) + val (u8 true
+ *                    delta, >= 7).
+ *   resident layout: the kernel layout built once per weight by bf16x_repack:
+ *                    rows of ceil(in_f/256) chunks of 368 bytes
+ *                    ([256 B sign|mant bytes][96 B pair-aligned deltas][16 B emax]),
+ *                    i.e. the same 11.5 bits per weight, plus a per-row CSR of
+ *                    patches for exponent deltas > 7 (u32 entries:
+ *                    col | true_delta << 16 | sign_mant << 24).
+ *   GGUF blocks    : 46-byte blocks of 32 weights (bf16x_gguf_block.py:6-17).
+ */
+#ifndef BF16X_B200_H
+#define BF16X_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BF16X_OK               0
+#define BF16X_ERR_INVALID     -1   /* bad argument (size, alignment, dtype) */
+#define BF16X_ERR_CUDA        -2   /* CUDA runtime error */
+#define BF16X_ERR_UNSUPPORTED -3   /* shape or device not supported */
+#define BF16X_ERR_DEVICE      -4   /* a kernel reported a device-side error */
+
+#define BF16X_DTYPE_BF16 0
+#define BF16X_DTYPE_F32  1
+
+#define BF16X_CHUNK_ELEMS 256
+#define BF16X_CHUNK_BYTES 368
+
+/* ---- library ----------------------------------------------------------- */
+int bf16x_version(void);
+const char *bf16x_last_error(void);
+
+/* Read and clear the device-side status bits that kernels of this library
+ * set on `device` (wait timeouts, malformed overflow tables).  Synchronises
+ * the device.  *flags == 0 means no error was recorded. */
+int bf16x_device_status(int device, uint32_t *flags);
+
+/* ---- flat-stream decode ------------------------------------------------ */
+/* Replaces bf16x_decode_triton (bf16x_triton_test.py:80-108): base decode and
+ * overflow fix in ONE kernel.  out: bf16 bits [out_f * in_f].  Stream word
+ * counts may be the exact dict lengths or padded ones; nothing past them is
+ * read.  ovf_idx/ovf_val are device arrays (n_ovf may be 0).  Semantics are
+ * those of BF16XLinear._decode_tile (opqk_linear.py:360-377) for well-formed
+ * tables: exponent = (emax - d) & 0xFF with d the true delta of listed
+ * elements.  sub must be 16. */
+int bf16x_decode(const uint32_t *sign, int64_t n_sign_words,
+                 const uint32_t *mant, int64_t n_mant_words,
+                 const uint32_t *delta, int64_t n_delta_words,
+                 const uint8_t *emax, int64_t n_emax,
+                 const int32_t *ovf_idx, const uint8_t *ovf_val, int64_t n_ovf,
+                 int64_t out_f, int64_t in_f, int sub,
+                 uint16_t *out, void *stream);
+
+/* ---- GPU packer --------------------------------------------------------- */
+/* Replaces bf16x_quantize (opqk_linear.py:291-324) on the device.  Two calls:
+ * bf16x_quantize_count writes the number of overflow entries (delta >= 7) to
+ * *n_ovf_dev (device int64) using `scratch` (bf16x_quantize_scratch_bytes(n)
+ * bytes, device); bf16x_quantize then fills the streams, whose lengths follow
+ * the reference's pack_bits_stream rule (opqk_linear.py:53-64), and the
+ * overflow table (capacity entries at most).  w: bf16 bits [n]. */
+int64_t bf16x_stream_words(int64_t n, int bits);
+int64_t bf16x_quantize_scratch_bytes(int64_t n);
+int bf16x_quantize_count(const uint16_t *w, int64_t n, int sub, void *scratch,
+                         int64_t *n_ovf_dev, void *stream);
+int bf16x_quantize(const uint16_t *w, int64_t n, int sub, const void *scratch,
+                   uint8_t *emax, uint32_t *sign, uint32_t *mant, uint32_t *delta,
+                   int32_t *ovf_idx, uint8_t *ovf_val, int64_t capacity, void *stream);
+
+/* ---- resident layout ---------------------------------------------------- */
+/* Replaces the per-layer device preparation of Bf16xFused.__init__
+ * (bf16x_fused.py:154-192: _pad1 + CSR build) and Bf16xGemmLinear.__init__
+ * (bf16x_gemm_fused.py:163-184).  Rows [row0, row1) of the flat dict are
+ * decoded exactly (overflow applied) and re-encoded into the resident layout.
+ *   bf16x_resident_row_bytes: bytes per row of the layout.
+ *   bf16x_repack_count: patch counts -> patch_off[0..rows] (exclusive scan,
+ *                       device int32, rows+1 entries); patch_off[rows] is the
+ *                       total.
+ *   bf16x_repack: writes layout [rows][row_bytes] and patches (u32).
+ * in_f must be <= 65536. */
+int64_t bf16x_resident_row_bytes(int64_t in_f);
+int bf16x_repack_count(const uint32_t *sign, int64_t n_sign_words,
+                       const uint32_t *mant, int64_t n_mant_words,
+                       const uint32_t *delta, int64_t n_delta_words,
+                       const uint8_t *emax, int64_t n_emax,
+                       const int32_t *ovf_idx, const uint8_t *ovf_val, int64_t n_ovf,
+                       int64_t out_f, int64_t in_f, int64_t row0, int64_t row1,
+                       int32_t *patch_off, void *stream);
+int bf16x_repack(const uint32_t *sign, int64_t n_sign_words,
+                 const uint32_t *mant, int64_t n_mant_words,
+                 const uint32_t *delta, int64_t n_delta_words,
+                 const uint8_t *emax, int64_t n_emax,
+                 const int32_t *ovf_idx, const uint8_t *ovf_val, int64_t n_ovf,
+                 int64_t out_f, int64_t in_f, int64_t row0, int64_t row1,
+                 const int32_t *patch_off, uint8_t *layout, uint32_t *patches,
+                 void *stream);
+
+/* Resident layout -> bf16 bits [rows][in_f] (bit-exact, patches applied).
+ * Used by the two-segment path (Bf16xFused 'opt' mode, bf16x_fused.py:194-205). */
+int bf16x_resident_decode(const uint8_t *layout, const int32_t *patch_off,
+                          const uint32_t *patches, int64_t rows, int64_t in_f,
+                          uint16_t *out, int64_t ld_out, void *stream);
+
+/* ---- fused decode + GEMV (batch 1..8) ----------------------------------- */
+/* Replaces bf16x_fused_gemv / _bf16x_gemv_fused_kernel (bf16x_fused.py:32-127):
+ * y[b][n] = sum_k W[n][k] * x[b][k] (+ bias[n]) for b < batch <= 8, with W
+ * read from the resident layout and decoded in registers, patches applied
+ * exactly, fp32 accumulation.  x: bf16 [batch][ldx], ldx >= ceil(in_f/256)*256
+ * elements with zeros past in_f, rows 16-byte aligned.  bias: bf16 [rows] or
+ * NULL.  y: [batch][ldy] of y_dtype (BF16X_DTYPE_BF16 or _F32). */
+int bf16x_gemv(const uint8_t *layout, const int32_t *patch_off, const uint32_t *patches,
+               int64_t rows, int64_t in_f,
+               const uint16_t *x, int64_t batch, int64_t ldx,
+               const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
+               void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BF16X_B200_H */
