@@ -281,33 +281,51 @@ def run_ours(args):
         return float(t.item())
 
     # ---------------- device-resident timing (value) --------------------------
+    # One step (the four launches) is captured once in a CUDA graph and
+    # replayed: what is timed is device work, not Python launch overhead.
     for _ in range(max(args.warmup, 3)):
         step()
     barrier()
+    gstream = torch.cuda.Stream(device=dev)
+    gstream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(gstream):
+        step()                                   # per-stream scratch for the capture stream
+        torch.cuda.synchronize(dev)
+        g_step = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step, stream=gstream):
+            step()
+        g_layer = []
+        for L in layers:
+            gl = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gl, stream=gstream):
+                L["rw"].gemv(L["x"], out=L["y"])
+            g_layer.append(gl)
+    torch.cuda.synchronize(dev)
+    for _ in range(max(args.warmup, 3)):
+        g_step.replay()
+    barrier()
     clock = ClockSampler(local)
     clock.start()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in layers for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     t_start.record()
-    k = 0
     for _ in range(args.steps):
-        for L in layers:
-            ev[k][0].record()
-            L["rw"].gemv(L["x"], out=L["y"])
-            ev[k][1].record()
-            k += 1
+        g_step.replay()
     t_end.record()
     barrier()
     clocks = clock.stop()
     el_ms = t_start.elapsed_time(t_end)
-    per_layer_ms = [0.0] * len(layers)
-    k = 0
-    for _ in range(args.steps):
-        for i in range(len(layers)):
-            per_layer_ms[i] += ev[k][0].elapsed_time(ev[k][1])
-            k += 1
-    per_layer_ms = [v / args.steps for v in per_layer_ms]
+    # per-launch device time of each layer (the same launch replayed back to back)
+    per_layer_ms = []
+    for gl in g_layer:
+        gl.replay()
+        a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_ev.record()
+        for _ in range(args.steps):
+            gl.replay()
+        b_ev.record()
+        torch.cuda.synchronize(dev)
+        per_layer_ms.append(a_ev.elapsed_time(b_ev) / args.steps)
     el_max = max_over_ranks(el_ms)
     step_bytes = sum(L["nbytes"] for L in layers)
     total_bytes = sum_over_ranks(step_bytes * args.steps)
@@ -354,20 +372,27 @@ def run_ours(args):
     cublas = None
     if not args.no_cublas:
         import torch.nn.functional as F
-        for _ in range(3):
+        with torch.cuda.stream(gstream):
             for L in layers:
                 F.linear(L["x"], L["w"])
+            torch.cuda.synchronize(dev)
+            gc = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gc, stream=gstream):
+                for L in layers:
+                    F.linear(L["x"], L["w"])
+        for _ in range(3):
+            gc.replay()
         barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(args.steps):
-            for L in layers:
-                F.linear(L["x"], L["w"])
+            gc.replay()
         b.record()
         barrier()
         c_ms = max_over_ranks(a.elapsed_time(b)) / args.steps
         cublas = {"ms_per_step": round(c_ms, 4), "speedup_vs_cublas_bf16": round(c_ms / (el_max / args.steps), 3),
-                  "bf16_bytes_per_step": sum(L["rows"] * L["in_f"] * 2 for L in layers)}
+                  "bf16_bytes_per_step": sum(L["rows"] * L["in_f"] * 2 for L in layers),
+                  "note": "torch F.linear (cuBLAS) on the uncompressed bf16 weights, same shapes, CUDA graph"}
 
     # ---------------- CPU baseline (rank 0, N=1) ---------------------------------
     cpu = None
@@ -397,6 +422,7 @@ def run_ours(args):
                          "kernel": f"gemv_kernel (fused decode+GEMV) {Ld['rows']}x{Ld['in_f']} batch {B}",
                          "traffic": traffic_from_profile(kernel_key)},
             "gpu_launches": args.steps * len(layers),
+            "timing": "CUDA-graph replay of the step; per_shape_ms from the same launch replayed back to back",
             "clocks": clocks,
             "e2e": e2e,
             "cublas_bf16": cublas,

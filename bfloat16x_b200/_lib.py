@@ -11,12 +11,14 @@ import os
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libbf16x_b200.so")
+# BF16X_LIB points at another build of the same library (e.g. a tuned variant)
+LIB_PATH = os.environ.get("BF16X_LIB") or os.path.join(_HERE, "libbf16x_b200.so")
 
 BF16X_DTYPE_BF16 = 0
 BF16X_DTYPE_F32 = 1
 CHUNK_ELEMS = 256
 CHUNK_BYTES = 368
+TILE_ROWS = 16
 
 
 class Bf16xError(RuntimeError):
@@ -41,7 +43,8 @@ _SIGS = {
     "bf16x_repack": (_i32, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64,
                             _p, _p, _p, _p]),
     "bf16x_resident_decode": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _p]),
-    "bf16x_gemv": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p]),
+    "bf16x_gemv_scratch_bytes": (_i64, [_i64, _i64]),
+    "bf16x_gemv": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p, _p, _i64, _p]),
 }
 
 _lib = None
@@ -89,6 +92,8 @@ def device_status(device: int | None = None) -> int:
 def check_device_status(device: int | None = None) -> None:
     f = device_status(device)
     if f:
+        from .resident import reset_workspaces
+        reset_workspaces()
         names = {1: "wait timeout", 2: "overflow index not ascending", 4: "overflow index out of range",
                  8: "bad resident layout"}
         what = ", ".join(v for k, v in names.items() if f & k) or hex(f)

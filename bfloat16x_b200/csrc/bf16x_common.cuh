@@ -55,12 +55,14 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting warp sleeps (up to the hint)
+// instead of spinning, so it does not take issue slots from working warps.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
                  "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+                 : "=r"(ok) : "r"(bar), "r"(parity), "r"(1000000u) : "memory");
     return ok != 0;
 }
 
@@ -73,7 +75,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(a, parity)) return true;
-        if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+        if ((i & 7u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
             atomicOr(status, kErrWaitTimeout);
             return false;
         }
@@ -110,6 +112,29 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits_rn(float f) {
 template <int SH>
 __device__ __forceinline__ uint32_t shl_signed(uint32_t v) {
     if constexpr (SH >= 0) return v << SH; else return v >> (-SH);
+}
+
+}  // namespace bf16x
+
+// ------------------------------------------------------- tensor-map copies
+namespace bf16x {
+
+// Tiled TMA loads (no multicast) into shared memory, completion counted on an
+// mbarrier.  `map` is the address of a __grid_constant__ kernel parameter.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *map, int c0, int c1, int c2, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        :: "r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const void *map) {
+    asm volatile("prefetch.tensormap [%0];" :: "l"(map) : "memory");
 }
 
 }  // namespace bf16x

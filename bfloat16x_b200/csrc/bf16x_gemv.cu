@@ -4,53 +4,85 @@
 // and generalises it from batch 1 to batch <= 8.
 //
 // Design (HBM-bound: the only large stream is the compressed weight):
-//   * persistent CTAs, one per SM; a CTA walks tiles of 16 weight rows;
-//   * one producer warp streams each tile's compressed rows (368-byte chunks
-//     of the resident layout) and the matching activation slice into a ring
-//     of shared-memory stages with 1-D bulk copies (the TMA engine), completion
-//     counted on mbarriers; consumer warps release stages through a second
-//     set of mbarriers;
-//   * each consumer warp owns one 256-column chunk per stage; a lane decodes
-//     two 32-column groups (rows g and g+8 of the tile) straight into bf16x2
-//     registers and feeds them as the A operand of mma.m16n8k16 (rows x k),
-//     with the activations as the B operand (k x batch).  The tensor core does
-//     the multiply-accumulate, so the CUDA cores only decode: about five
-//     integer ops per pair of weights;
-//   * at the end of a tile the warps' fp32 partials are summed in a fixed
-//     order in shared memory and the exact-delta patches (delta > 7, ~3% of
-//     weights) are added as (w_exact - w_saturated) * x by 2*NW lanes per row
-//     with a shuffle reduction, so results are deterministic;
+//   * work items are (16-row tile, 256-column chunk) pairs in tile-major
+//     order; persistent CTAs of 8 warps split them stream-K style, every warp
+//     a contiguous, equal range, so every SM streams the same number of bytes
+//     whatever the shape;
+//   * each warp feeds itself: a ring of shared-memory slots filled by 1-D bulk
+//     copies (the TMA engine) -- 16 weight rows x 368 bytes, the activation
+//     slice, and the (tile, chunk) patch record -- completion counted on one
+//     mbarrier per slot; a slot is refilled right after it is consumed, so
+//     S items per warp are always in flight and no warp waits for another;
+//   * a lane decodes two 32-column groups (rows g and g+8) into bf16x2 pairs
+//     (about five integer ops per pair) and stores them, in mma fragment
+//     order, to a 4 KB per-warp buffer; the exact-delta patches of the item
+//     (delta > 7, ~3% of weights) are then scattered into that buffer as exact
+//     bf16 values, round-robin over all 32 lanes, and the fragments go to
+//     mma.m16n8k16 (rows x k) with the activations as the B operand
+//     (k x batch).  The tensor core does the multiply-accumulate, patches cost
+//     one 2-byte store each whatever the batch;
+//   * a tile split between warps is finished by whichever warp arrives last
+//     (an atomic counter per tile in the workspace), summing the pieces in a
+//     fixed order, so results are deterministic and no warp ever waits;
 //   * every mbarrier wait is bounded (bf16x_common.cuh) and reports a timeout
 //     through the device status word instead of hanging.
+#include <algorithm>
+#include <mutex>
+
 #include <cuda_runtime.h>
 
 #include "bf16x_common.cuh"
 #include "bf16x_resident.cuh"
 #include "bf16x_status.cuh"
+#include "bf16x_tmap.h"
 
 namespace bf16x {
 
-constexpr int kGemvRows = 16;
+constexpr int kPcapWords = 192;      // patch-record words staged per slot (larger records: tail from L2)
+constexpr int kFragBytes = 8 * 32 * 16;   // one half chunk: 8 mma steps x 32 lanes x 4 registers
+constexpr int kXRowBytes = kChunkElems * 2;
 
-template <int NW, int BMAX>
+// Configuration per (batch bound, warps per CTA): ring depth per warp and
+// whether both half chunks are decoded before the patches and the mma (two
+// fragment buffers).  Long weights run 12 warps per SM with 2-slot rings;
+// short ones 8 warps with 3-slot rings (more bytes in flight per warp).
+#ifndef BF16X_GEMV_DUAL
+#define BF16X_GEMV_DUAL 0
+#endif
+
+template <int BMAX, int NW>
 struct GemvCfg {
-    static constexpr int kPadR = (16 - (NW * kChunkBytes) % 128 + 128) % 128;
-    static constexpr int kRowStride = NW * kChunkBytes + kPadR;   // == 16 (mod 128): conflict-free 16-B loads
-    static constexpr int kXStride = NW * kChunkElems * 2 + 16;
-    static constexpr int kXOff = kGemvRows * kRowStride;
-    static constexpr int kStageBytes = (kXOff + BMAX * kXStride + 127) / 128 * 128;
-    static constexpr int kStages = (200 * 1024 / kStageBytes) < 8 ? (200 * 1024 / kStageBytes) : 8;
-    static constexpr int kRedBytes = NW * kGemvRows * 8 * 4;
-    static constexpr int kSmem = kStages * kStageBytes + kRedBytes + 2 * kStages * 8;
-    static_assert(kStages >= 2, "stage too large");
+    static constexpr bool kDual = BF16X_GEMV_DUAL != 0;
+    static constexpr int kWBytes = kTileRows * kChunkBytes;                 // 5888
+    static constexpr int kXOff = kWBytes;
+    static constexpr int kPOff = kXOff + BMAX * kXRowBytes;
+    static constexpr int kSlot = (kPOff + kPcapWords * 4 + 127) / 128 * 128;
+    static constexpr int kFrag = (kDual ? 2 : 1) * kFragBytes;
+    static constexpr int kBudget = 220 * 1024 - 1024;
+    static constexpr int kWarpsFit = kBudget / (2 * kSlot + kFrag);
+    static constexpr int kWarps = NW < kWarpsFit ? NW : kWarpsFit;
+    static constexpr int kStagesFit = (kBudget / kWarps - kFrag) / kSlot;
+    static constexpr int kStages = kStagesFit < 3 ? kStagesFit : 3;
+    static constexpr int kWarpBytes = kStages * kSlot + kFrag;
+    static constexpr int kZeroOff = kWarps * kWarpBytes;                    // 512 zero bytes
+    static constexpr int kRecOff = kZeroOff + 512;                          // per slot record offset
+    static constexpr int kBarOff = kRecOff + kWarps * kStages * 8;
+    static constexpr int kSmem = kBarOff + kWarps * kStages * 8;
+    static_assert(kStages >= 2, "ring too shallow for this configuration");
+    static_assert(kSlot % 128 == 0 && kXOff % 128 == 0 && kPOff % 16 == 0, "slot alignment");
+    static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct GemvParams {
+    CUtensorMap wmap;   // resident layout as [rows][chunks][92 words], box 16 rows x 1 chunk
+    CUtensorMap xmap;   // activations [batch][in_pad] bf16, box BMAX rows x 256 columns
     const uint8_t *layout;
-    const int32_t *patch_off;
-    const uint32_t *patches;
-    int64_t rows, in_f, row_bytes;
+    const int32_t *ptile_off;
+    const uint32_t *precs;
+    int64_t rows, row_bytes;
     int nch, n_tiles;
+    int64_t T;          // items = n_tiles * nch
+    int64_t W;          // warps taking part in the partition (<= T)
     const uint16_t *x;
     int64_t ldx;
     int batch;
@@ -58,6 +90,8 @@ struct GemvParams {
     void *y;
     int y_f32;
     int64_t ldy;
+    int32_t *tile_cnt;  // n_tiles counters, zero between launches
+    float *partials;    // scratch: W x 2 x [16][8]
 };
 
 __device__ __forceinline__ void mma_bf16_16816(float &c0, float &c1, float &c2, float &c3, uint32_t a0, uint32_t a1,
@@ -69,203 +103,350 @@ __device__ __forceinline__ void mma_bf16_16816(float &c0, float &c1, float &c2, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// mma step J of one group: k-slots (2t, 2t+1 | 2t+8, 2t+9) carry the group's
-// columns 4J..4J+3, i.e. pairs 2J (a0/a1) and 2J+1 (a2/a3) for rows g and g+8.
-// The B operand of lane (g, t) is x[g][group + 4J .. +3]: one 8-byte load.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Decode step J of one group: k-slots (2t, 2t+1 | 2t+8, 2t+9) of mma step J
+// carry the group's columns 4J..4J+3, i.e. pairs 2J (a0/a1) and 2J+1 (a2/a3)
+// of rows g (a0/a2) and g+8 (a1/a3).  The lane stores them as one 16-byte
+// fragment at frag[J][lane].
 template <int J>
-__device__ __forceinline__ void group_mma(const uint32_t (&smA)[8], const uint32_t (&dA)[3], uint32_t eAlo,
-                                          uint32_t eAhi, const uint32_t (&smB)[8], const uint32_t (&dB)[3],
-                                          uint32_t eBlo, uint32_t eBhi, const uint16_t *xq, bool xv, float &c0,
-                                          float &c1, float &c2, float &c3) {
+__device__ __forceinline__ void group_to_frag(const uint32_t (&smA)[8], const uint32_t (&dA)[3], uint32_t eAlo,
+                                              uint32_t eAhi, const uint32_t (&smB)[8], const uint32_t (&dB)[3],
+                                              uint32_t eBlo, uint32_t eBhi, uint4 *frag, int lane) {
     const uint32_t eA = J < 4 ? eAlo : eAhi, eB = J < 4 ? eBlo : eBhi;
-    const uint32_t a0 = decode_pair<2 * J>(smA, dA, eA);
-    const uint32_t a1 = decode_pair<2 * J>(smB, dB, eB);
-    const uint32_t a2 = decode_pair<2 * J + 1>(smA, dA, eA);
-    const uint32_t a3 = decode_pair<2 * J + 1>(smB, dB, eB);
-    uint2 b = make_uint2(0u, 0u);
-    if (xv) b = *reinterpret_cast<const uint2 *>(xq + 4 * J);
-    mma_bf16_16816(c0, c1, c2, c3, a0, a1, a2, a3, b.x, b.y);
-    if constexpr (J + 1 < 8)
-        group_mma<J + 1>(smA, dA, eAlo, eAhi, smB, dB, eBlo, eBhi, xq, xv, c0, c1, c2, c3);
+    frag[J * 32 + lane] = make_uint4(decode_pair<2 * J>(smA, dA, eA), decode_pair<2 * J>(smB, dB, eB),
+                                     decode_pair<2 * J + 1>(smA, dA, eA), decode_pair<2 * J + 1>(smB, dB, eB));
+    if constexpr (J + 1 < 8) group_to_frag<J + 1>(smA, dA, eAlo, eAhi, smB, dB, eBlo, eBhi, frag, lane);
 }
 
-__device__ __forceinline__ void chunk_mma(const uint8_t *rowA, const uint8_t *rowB, const uint16_t *xg, bool xv,
-                                          int t, float &c0, float &c1, float &c2, float &c3) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int q = 4 * h + t;
-        uint32_t smA[8], dA[3], eAlo, eAhi, smB[8], dB[3], eBlo, eBhi;
-        load_group(rowA, q, smA, dA, eAlo, eAhi);
-        load_group(rowB, q, smB, dB, eBlo, eBhi);
-        group_mma<0>(smA, dA, eAlo, eAhi, smB, dB, eBlo, eBhi, xg + 32 * q, xv, c0, c1, c2, c3);
-    }
+// mma steps of one half chunk: A from the fragment buffer, B = x[g][group +
+// 4J .. +3] (one 8-byte load).  Even and odd steps accumulate separately: two
+// independent mma chains.
+template <int J>
+__device__ __forceinline__ void frag_mma(const uint4 *frag, int lane, const uint16_t *xq, float (&ce)[4],
+                                         float (&co)[4]) {
+    const uint4 a = frag[J * 32 + lane];
+    const uint2 b = *reinterpret_cast<const uint2 *>(xq + 4 * J);
+    float(&c)[4] = (J & 1) ? co : ce;
+    mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, b.x, b.y);
+    if constexpr (J + 1 < 8) frag_mma<J + 1>(frag, lane, xq, ce, co);
 }
 
-__device__ __forceinline__ void named_bar(int id, int nthreads) {
-    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
-}
+// Warp w of the partition owns items [T*w/W, T*(w+1)/W); item i belongs to
+// warp floor(((i+1)*W - 1) / T).
+__device__ __forceinline__ int64_t item_lo(int64_t w, int64_t T, int64_t W) { return T * w / W; }
+__device__ __forceinline__ int64_t item_owner(int64_t i, int64_t T, int64_t W) { return ((i + 1) * W - 1) / T; }
 
-template <int NW, int BMAX>
-__global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_kernel(const GemvParams p) {
-    using C = GemvCfg<NW, BMAX>;
+template <int BMAX, int NW>
+__global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+    using C = GemvCfg<BMAX, NW>;
     constexpr int S = C::kStages;
     extern __shared__ __align__(128) uint8_t smem[];
-    float *red = reinterpret_cast<float *>(smem + S * C::kStageBytes);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * C::kStageBytes + C::kRedBytes);
-    uint64_t *empty = full + S;
-
-    // abort[0]: set by any warp whose bounded wait gave up; abort[1]: the
-    // consumers' per-tile decision, read by all of them after a barrier.
-    __shared__ volatile int abort_flag[2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        abort_flag[0] = 0;
-        abort_flag[1] = 0;
-        for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NW);
-        }
-        fence_mbar_init();
-    }
+
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff) + warp * S;
+    int64_t *rec_of = reinterpret_cast<int64_t *>(smem + C::kRecOff) + warp * S;
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) reinterpret_cast<uint32_t *>(smem + C::kZeroOff)[i] = 0u;
+    if (lane == 0)
+        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
     __syncthreads();
 
-    const int spt = (p.nch + NW - 1) / NW;   // stages per tile
-    int slot = 0;
-    uint32_t ph = 0;
-
-    if (warp == NW) {
-        // ------------------------------------------------------------ producer
-        for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-            const int64_t row0 = (int64_t)tile * kGemvRows;
-            const int rv = (int)(p.rows - row0 < kGemvRows ? p.rows - row0 : kGemvRows);
-            for (int s = 0; s < spt; ++s) {
-                const int c0 = s * NW;
-                const int nch = min(NW, p.nch - c0);
-                int ok = 1;
-                if (lane == 0) ok = !abort_flag[0] && mbar_wait(&empty[slot], ph ^ 1u, &g_status);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) {
-                    if (lane == 0) abort_flag[0] = 1;
-                    return;
-                }
-                uint8_t *st = smem + slot * C::kStageBytes;
-                if (lane == 0)
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t)(rv * nch * kChunkBytes + p.batch * nch * kChunkElems * 2));
-                __syncwarp();
-                if (lane < rv) {
-                    bulk_g2s(st + lane * C::kRowStride,
-                             p.layout + (row0 + lane) * p.row_bytes + (int64_t)c0 * kChunkBytes,
-                             (uint32_t)(nch * kChunkBytes), &full[slot]);
-                } else if (lane >= kGemvRows && lane - kGemvRows < p.batch) {
-                    const int b = lane - kGemvRows;
-                    bulk_g2s(st + C::kXOff + b * C::kXStride, p.x + b * p.ldx + (int64_t)c0 * kChunkElems,
-                             (uint32_t)(nch * kChunkElems * 2), &full[slot]);
-                }
-                if (++slot == S) { slot = 0; ph ^= 1u; }
-            }
-        }
-        return;
+    const int64_t gw = (int64_t)blockIdx.x * C::kWarps + warp;
+    if (gw >= p.W) return;
+    if (lane == 0) {
+        prefetch_tensormap(&p.wmap);
+        prefetch_tensormap(&p.xmap);
     }
+    const int64_t lo = item_lo(gw, p.T, p.W), hi = item_lo(gw + 1, p.T, p.W);
+    const int64_t first_tile = lo / p.nch;
+    uint8_t *wsm = smem + warp * C::kWarpBytes;
+    uint4 *frag = reinterpret_cast<uint4 *>(wsm + S * C::kSlot);
+    const uint16_t *zero_x = reinterpret_cast<const uint16_t *>(smem + C::kZeroOff);
 
-    // -------------------------------------------------------------- consumers
+    // ---- issue the copies of item (tile, c) into slot `s`: lane 0 alone,
+    // three TMA operations (16 weight rows, the activation slice, the record)
+    auto issue = [&](int64_t tile, int c, int s, int32_t r_off, int32_t r_end) {
+        if (lane == 0) {
+            const int staged = min(r_end - r_off, kPcapWords);
+            uint8_t *slot = wsm + s * C::kSlot;
+            rec_of[s] = r_off;
+            mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + BMAX * kXRowBytes + staged * 4));
+            tma_load_3d(slot, &p.wmap, 0, c, (int)(tile * kTileRows), &bars[s]);
+            tma_load_2d(slot + C::kXOff, &p.xmap, c * kChunkElems, 0, &bars[s]);
+            bulk_g2s(slot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
+        }
+    };
+
+    // issue cursor: the next item to be copied, as (tile, chunk) and index;
+    // its record bounds are loaded one refill ahead of their use
+    int64_t i_it = lo, i_tile = first_tile;
+    int i_c = (int)(lo - first_tile * p.nch);
+    int32_t nxt_off = 0, nxt_end = 0;
+    auto load_rec = [&]() {
+        if (i_it < hi) {
+            nxt_off = __ldg(p.ptile_off + i_it);
+            nxt_end = __ldg(p.ptile_off + i_it + 1);
+        }
+    };
+    auto advance_issue = [&]() {
+        ++i_it;
+        if (++i_c == p.nch) { i_c = 0; ++i_tile; }
+    };
+    for (int s = 0; s < S && i_it < hi; ++s) {
+        load_rec();
+        issue(i_tile, i_c, s, nxt_off, nxt_end);
+        advance_issue();
+    }
+    load_rec();
+
     const int g = lane >> 2, t = lane & 3;
-    const bool xv = g < p.batch;
-    constexpr int TPR = 2 * NW;                 // threads per row in the epilogue
-    const int ctid = warp * 32 + lane;
-    const int erow = ctid / TPR, esl = ctid % TPR;
+    float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
+    int64_t tile = first_tile;
+    int c = (int)(lo - first_tile * p.nch);
+    int tile_c0 = c;                                // first chunk of the current tile in this range
+    int s = 0;
+    uint32_t parity = 0;
 
-    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-        const int64_t row0 = (int64_t)tile * kGemvRows;
-        float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
-        bool failed = false;
-        for (int s = 0; s < spt; ++s) {
-            const int nch = min(NW, p.nch - s * NW);
-            if (!failed && (abort_flag[0] || !mbar_wait(&full[slot], ph, &g_status))) {
-                failed = true;
-                abort_flag[0] = 1;
+    for (int64_t it = lo; it < hi; ++it) {
+        if (!mbar_wait(&bars[s], parity, &g_status)) return;
+        const uint8_t *slot = wsm + s * C::kSlot;
+        const uint16_t *xs = reinterpret_cast<const uint16_t *>(slot + C::kXOff);
+
+        // ---- per half chunk: decode to fragments, patch, multiply
+        {
+            const uint32_t *rec = reinterpret_cast<const uint32_t *>(slot + C::kPOff);
+            const uint32_t hdr = rec[0];
+            const uint8_t *rowA = slot + g * kChunkBytes;
+            const uint8_t *rowB = rowA + 8 * kChunkBytes;
+            const uint16_t *xg = g < BMAX ? xs + g * kChunkElems : zero_x;
+            // both halves' compressed groups are read up front, so the
+            // shared-memory latency overlaps the first half's decode
+            uint32_t smA[2][8], dA[2][3], eAlo[2], eAhi[2], smB[2][8], dB[2][3], eBlo[2], eBhi[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                load_group(rowA, 4 * h + t, smA[h], dA[h], eAlo[h], eAhi[h]);
+                load_group(rowB, 4 * h + t, smB[h], dB[h], eBlo[h], eBhi[h]);
             }
-            if (!failed && warp < nch) {
-                const uint8_t *st = smem + slot * C::kStageBytes;
-                const uint8_t *rowA = st + g * C::kRowStride + warp * kChunkBytes;
-                const uint8_t *rowB = rowA + 8 * C::kRowStride;
-                const uint16_t *xg = reinterpret_cast<const uint16_t *>(st + C::kXOff + g * C::kXStride) +
-                                     warp * kChunkElems;
-                chunk_mma(rowA, rowB, xg, xv, t, c0, c1, c2, c3);
+            if constexpr (!C::kDual) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int q = 4 * h + t;
+                    group_to_frag<0>(smA[h], dA[h], eAlo[h], eAhi[h], smB[h], dB[h], eBlo[h], eBhi[h], frag, lane);
+                    __syncwarp();
+                    // exact values of the patched weights of this half, stored
+                    // over their saturated decode: each entry carries its slot
+                    const int jlo = h ? (int)(hdr & 0xFFFFu) : 0;
+                    const int jhi = h ? (int)(hdr >> 16) : (int)(hdr & 0xFFFFu);
+                    uint16_t *frag16 = reinterpret_cast<uint16_t *>(frag);
+                    for (int j = jlo + lane; j < jhi; j += 32) {
+                        const uint32_t ent = (kRecHdrWords + j < kPcapWords)
+                                                 ? rec[kRecHdrWords + j]
+                                                 : __ldg(p.precs + rec_of[s] + kRecHdrWords + j);
+                        frag16[ent & 0x7FFu] = (uint16_t)(ent >> 16);
+                    }
+                    __syncwarp();
+                    frag_mma<0>(frag, lane, xg + 32 * q, ce, co);
+                    __syncwarp();
+                }
+            } else {
+                // both halves decoded first: 64 independent pairs per lane
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    group_to_frag<0>(smA[h], dA[h], eAlo[h], eAhi[h], smB[h], dB[h], eBlo[h], eBhi[h],
+                                     frag + h * (kFragBytes / 16), lane);
+                __syncwarp();
+                const int jhi = (int)(hdr >> 16);
+                uint16_t *frag16 = reinterpret_cast<uint16_t *>(frag);
+                for (int j = lane; j < jhi; j += 32) {
+                    const uint32_t ent = (kRecHdrWords + j < kPcapWords)
+                                             ? rec[kRecHdrWords + j]
+                                             : __ldg(p.precs + rec_of[s] + kRecHdrWords + j);
+                    frag16[ent & 0xFFFu] = (uint16_t)(ent >> 16);   // bit 11 = half selects the buffer
+                }
+                __syncwarp();
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    frag_mma<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), ce, co);
+                __syncwarp();
             }
-            __syncwarp();
-            if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
-            if (++slot == S) { slot = 0; ph ^= 1u; }
         }
 
-        // ---- epilogue: fixed-order reduction + exact-delta patches
-        float *rw = red + warp * kGemvRows * 8;
-        rw[g * 8 + 2 * t] = c0;
-        rw[g * 8 + 2 * t + 1] = c1;
-        rw[(g + 8) * 8 + 2 * t] = c2;
-        rw[(g + 8) * 8 + 2 * t + 1] = c3;
-        named_bar(1, NW * 32);
+        // ---- refill this slot S items ahead
+        __syncwarp();
+        if (i_it < hi) {
+            fence_proxy_async_smem();
+            issue(i_tile, i_c, s, nxt_off, nxt_end);
+            advance_issue();
+            load_rec();
+        }
 
-        const int64_t grow = row0 + erow;
-        float corr[BMAX];
+        // ---- tile finished (or range ends inside it)
+        if (c == p.nch - 1 || it == hi - 1) {
+            const float c0 = ce[0] + co[0], c1 = ce[1] + co[1], c2 = ce[2] + co[2], c3 = ce[3] + co[3];
+            const int64_t row0 = tile * kTileRows;
+            const bool whole = tile_c0 == 0 && c == p.nch - 1;
+            if (whole) {
+                const float v[4] = {c0, c1, c2, c3};
 #pragma unroll
-        for (int b = 0; b < BMAX; ++b) corr[b] = 0.f;
-        if (grow < p.rows) {
-            const int32_t lo = __ldg(p.patch_off + grow), hi = __ldg(p.patch_off + grow + 1);
-            const uint8_t *lrow = p.layout + grow * p.row_bytes;
-            for (int32_t j = lo + esl; j < hi; j += TPR) {
-                const uint32_t ent = __ldg(p.patches + j);
-                const uint32_t col = ent & 0xFFFFu;
-                const uint32_t em = __ldg(lrow + (col >> 8) * kChunkBytes + kEOff + ((col & 255u) >> 4));
-                const float dw = bf16_bits_to_f32(patch_bits(ent, em)) - bf16_bits_to_f32(saturated_bits(ent, em));
+                for (int k = 0; k < 4; ++k) {
+                    const int64_t row = row0 + g + 8 * (k >> 1);
+                    const int b = 2 * t + (k & 1);
+                    if (b < p.batch && row < p.rows) {
+                        float o = v[k];
+                        if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
+                        if (p.y_f32) reinterpret_cast<float *>(p.y)[b * p.ldy + row] = o;
+                        else reinterpret_cast<uint16_t *>(p.y)[b * p.ldy + row] = f32_to_bf16_bits_rn(o);
+                    }
+                }
+            } else {
+                // partial tile: publish this piece, the last arriving warp reduces
+                const int pslot = tile == first_tile ? 0 : 1;
+                float *mine = p.partials + (gw * 2 + pslot) * 128;
+                mine[g * 8 + 2 * t] = c0;
+                mine[g * 8 + 2 * t + 1] = c1;
+                mine[(g + 8) * 8 + 2 * t] = c2;
+                mine[(g + 8) * 8 + 2 * t + 1] = c3;
+                __threadfence();
+                __syncwarp();
+                const int64_t w_first = item_owner(tile * p.nch, p.T, p.W);
+                const int64_t w_last = item_owner(tile * p.nch + p.nch - 1, p.T, p.W);
+                int last = 0;
+                if (lane == 0) last = atomicAdd(p.tile_cnt + tile, 1) == (int)(w_last - w_first);
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
 #pragma unroll
-                for (int b = 0; b < BMAX; ++b)
-                    if (b < p.batch) corr[b] = fmaf(dw, bf16_bits_to_f32(__ldg(p.x + b * p.ldx + col)), corr[b]);
-            }
-        }
-#pragma unroll
-        for (int b = 0; b < BMAX; ++b) {
-#pragma unroll
-            for (int o = TPR / 2; o; o >>= 1) corr[b] += __shfl_xor_sync(0xffffffffu, corr[b], o);
-        }
-        if (grow < p.rows && !abort_flag[0]) {
-            const float bias = p.bias ? bf16_bits_to_f32(__ldg(p.bias + grow)) : 0.f;
-#pragma unroll
-            for (int b = 0; b < BMAX; ++b) {
-                if (b < p.batch && (b % TPR) == esl) {
-                    float v = 0.f;
-#pragma unroll
-                    for (int w = 0; w < NW; ++w) v += red[(w * kGemvRows + erow) * 8 + b];
-                    v += corr[b];
-                    v += bias;
-                    if (p.y_f32)
-                        reinterpret_cast<float *>(p.y)[b * p.ldy + grow] = v;
-                    else
-                        reinterpret_cast<uint16_t *>(p.y)[b * p.ldy + grow] = f32_to_bf16_bits_rn(v);
+                    for (int k = 0; k < 4; ++k) {
+                        const int idx = lane + 32 * k;
+                        const int rr = idx >> 3, b = idx & 7;
+                        float o = 0.f;
+                        for (int64_t w2 = w_first; w2 <= w_last; ++w2) {
+                            const int sl2 = (tile == item_lo(w2, p.T, p.W) / p.nch) ? 0 : 1;
+                            o += __ldcg(p.partials + (w2 * 2 + sl2) * 128 + idx);
+                        }
+                        const int64_t row = row0 + rr;
+                        if (b < p.batch && row < p.rows) {
+                            if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
+                            if (p.y_f32) reinterpret_cast<float *>(p.y)[b * p.ldy + row] = o;
+                            else reinterpret_cast<uint16_t *>(p.y)[b * p.ldy + row] = f32_to_bf16_bits_rn(o);
+                        }
+                    }
+                    if (lane == 0) p.tile_cnt[tile] = 0;
                 }
             }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ce[k] = co[k] = 0.f;
+            tile_c0 = 0;
         }
-        if (ctid == 0) abort_flag[1] = abort_flag[0];
-        named_bar(1, NW * 32);
-        if (abort_flag[1]) return;
+        if (++s == S) { s = 0; parity ^= 1u; }
+        if (++c == p.nch) { c = 0; ++tile; }
     }
 }
 
-template <int NW, int BMAX>
-static int launch_gemv(const GemvParams &p, cudaStream_t st) {
-    using C = GemvCfg<NW, BMAX>;
+struct GemvLaunch {
+    int grid;
+    int64_t W, T;
+    int n_tiles, nch;
+};
+
+static int device_sms() {
+    static int cache[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
-    static int attr_set[64] = {0};
-    static int sms[64] = {0};
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = sms > 0 ? sms : 1;
+    }
+    return cache[dev];
+}
+
+// Small cache of encoded tensor maps: encoding is host work that would be
+// repeated on every call for the same weight and activation buffers.
+struct MapKey {
+    const void *ptr;
+    int64_t a, b, c;
+    int dev;
+    bool operator==(const MapKey &o) const { return ptr == o.ptr && a == o.a && b == o.b && c == o.c && dev == o.dev; }
+};
+
+static bool cached_map(CUtensorMap *out, const MapKey &key, bool (*make)(CUtensorMap *, const MapKey &)) {
+    constexpr int kSlots = 256;
+    static MapKey keys[kSlots];
+    static CUtensorMap maps[kSlots];
+    static bool used[kSlots] = {false};
+    static std::mutex mu;
+    const size_t h = (reinterpret_cast<uintptr_t>(key.ptr) >> 8) ^ (size_t)(key.a * 31 + key.b * 7 + key.c + key.dev);
+    const int slot = (int)(h % kSlots);
+    std::lock_guard<std::mutex> lk(mu);
+    if (used[slot] && keys[slot] == key) {
+        *out = maps[slot];
+        return true;
+    }
+    if (!make(out, key)) return false;
+    keys[slot] = key;
+    maps[slot] = *out;
+    used[slot] = true;
+    return true;
+}
+
+static bool make_wmap(CUtensorMap *m, const MapKey &k) {   // a = rows, b = in_f
+    const int64_t nch = (k.b + kChunkElems - 1) / kChunkElems;
+    const cuuint64_t dims[3] = {(cuuint64_t)(kChunkBytes / 4), (cuuint64_t)nch, (cuuint64_t)k.a};
+    const cuuint64_t strides[2] = {(cuuint64_t)kChunkBytes, (cuuint64_t)resident_row_bytes(k.b)};
+    const cuuint32_t box[3] = {(cuuint32_t)(kChunkBytes / 4), 1u, (cuuint32_t)kTileRows};
+    return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, k.ptr, dims, strides, box);
+}
+
+static bool make_xmap(CUtensorMap *m, const MapKey &k) {   // a = in_pad, b = batch, c = ldx | bmax << 40
+    const int64_t ldx = k.c & ((1ll << 40) - 1), bmax = k.c >> 40;
+    const cuuint64_t dims[2] = {(cuuint64_t)k.a, (cuuint64_t)k.b};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kChunkElems, (cuuint32_t)bmax};
+    return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, k.ptr, dims, strides, box);
+}
+
+static GemvLaunch plan_gemv(int64_t rows, int64_t in_f, int nw) {
+    GemvLaunch L;
+    L.nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
+    L.n_tiles = (int)((rows + kTileRows - 1) / kTileRows);
+    L.T = (int64_t)L.n_tiles * L.nch;
+    const int64_t want = (L.T + nw - 1) / nw;
+    L.grid = (int)std::max<int64_t>(1, std::min<int64_t>(device_sms(), want));
+    L.W = std::min<int64_t>((int64_t)L.grid * nw, L.T);
+    return L;
+}
+
+// Warps per CTA for a launch: 12 when every warp gets many items (long
+// weights), else 8.
+static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
+    const int64_t T = (rows + kTileRows - 1) / kTileRows * ((in_f + kChunkElems - 1) / kChunkElems);
+    const bool wide = T >= (int64_t)device_sms() * 12 * 48;
+    if (batch == 1) return wide ? GemvCfg<1, 12>::kWarps : GemvCfg<1, 8>::kWarps;
+    if (batch == 2) return wide ? GemvCfg<2, 12>::kWarps : GemvCfg<2, 8>::kWarps;
+    if (batch <= 4) return GemvCfg<4, 8>::kWarps;
+    return GemvCfg<8, 8>::kWarps;
+}
+
+static int64_t scratch_need(const GemvLaunch &L) { return L.W * 2 * 128 * 4; }
+
+template <int BMAX, int NW>
+static int launch_gemv(const GemvParams &p, const GemvLaunch &L, cudaStream_t st) {
+    using C = GemvCfg<BMAX, NW>;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool attr_set[64] = {false};
     if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv: device index %d", dev);
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NW, BMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BMAX, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
         if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: smem attribute: %s", cudaGetErrorString(e));
-        cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        attr_set[dev] = 1;
+        attr_set[dev] = true;
     }
-    const int grid = min(p.n_tiles, max(sms[dev], 1));
-    gemv_kernel<NW, BMAX><<<grid, (NW + 1) * 32, C::kSmem, st>>>(p);
+    gemv_kernel<BMAX, NW><<<L.grid, C::kWarps * 32, C::kSmem, st>>>(p);
     return check_launch("bf16x_gemv");
 }
 
@@ -273,32 +454,57 @@ static int launch_gemv(const GemvParams &p, cudaStream_t st) {
 
 using namespace bf16x;
 
-extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *patch_off, const uint32_t *patches,
+extern "C" int64_t bf16x_gemv_scratch_bytes(int64_t rows, int64_t in_f) {
+    if (rows <= 0 || in_f <= 0) return 0;
+    int64_t need = 0;
+    for (int b : {1, 2, 4, 8}) need = std::max(need, scratch_need(plan_gemv(rows, in_f, warps_for(b, rows, in_f))));
+    return need;
+}
+
+extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
                           int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
-                          const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream) {
+                          const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
+                          int32_t *tile_counters, void *scratch, int64_t scratch_bytes, void *stream) {
     if (rows < 0 || in_f <= 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: bad shape");
     if (in_f > 65536) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv: in_f > 65536");
     if (batch < 1 || batch > 8) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: batch must be 1..8 (got %lld)", (long long)batch);
     if (y_dtype != BF16X_DTYPE_BF16 && y_dtype != BF16X_DTYPE_F32)
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: bad y_dtype");
     if (rows == 0) return BF16X_OK;
-    if (!layout || !patch_off || !x || !y) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: null pointer");
+    if (!layout || !ptile_off || !precs || !x || !y) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: null pointer");
     const int64_t in_pad = (in_f + kChunkElems - 1) / kChunkElems * kChunkElems;
     if (ldx < in_pad || (ldx % 8) != 0)
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: ldx must be a multiple of 8 and >= %lld (zero padded)", (long long)in_pad);
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(layout)) & 15u)
-        return set_error(BF16X_ERR_INVALID, "bf16x_gemv: x and layout must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(layout) | reinterpret_cast<uintptr_t>(precs)) & 15u)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv: x, layout and records must be 16-byte aligned");
     if (ldy < rows) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: ldy < rows");
+    const int nw = warps_for(batch, rows, in_f);
+    const GemvLaunch L = plan_gemv(rows, in_f, nw);
+    if (!tile_counters) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: tile_counters (ceil(rows/16) zeroed int32) missing");
+    if (!scratch || scratch_bytes < scratch_need(L))
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv: scratch of %lld bytes needed", (long long)scratch_need(L));
+    if (reinterpret_cast<uintptr_t>(scratch) & 15u)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv: scratch must be 16-byte aligned");
     GemvParams p;
-    p.layout = layout; p.patch_off = patch_off; p.patches = patches;
-    p.rows = rows; p.in_f = in_f; p.row_bytes = resident_row_bytes(in_f);
-    p.nch = (int)(in_pad / kChunkElems);
-    p.n_tiles = (int)((rows + kGemvRows - 1) / kGemvRows);
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int64_t bmax = batch == 1 ? 1 : batch == 2 ? 2 : batch <= 4 ? 4 : 8;
+        if (!cached_map(&p.wmap, MapKey{layout, rows, in_f, 0, dev}, make_wmap))
+            return set_error(BF16X_ERR_CUDA, "bf16x_gemv: weight tensor map");
+        if (!cached_map(&p.xmap, MapKey{x, in_pad, batch, ldx | (bmax << 40), dev}, make_xmap))
+            return set_error(BF16X_ERR_CUDA, "bf16x_gemv: activation tensor map");
+    }
+    p.layout = layout; p.ptile_off = ptile_off; p.precs = precs;
+    p.rows = rows; p.row_bytes = resident_row_bytes(in_f);
+    p.nch = L.nch; p.n_tiles = L.n_tiles; p.T = L.T; p.W = L.W;
     p.x = x; p.ldx = ldx; p.batch = (int)batch;
     p.bias = bias; p.y = y; p.y_f32 = y_dtype == BF16X_DTYPE_F32; p.ldy = ldy;
+    p.tile_cnt = tile_counters;
+    p.partials = static_cast<float *>(scratch);
     cudaStream_t st = (cudaStream_t)stream;
-    if (batch == 1) return launch_gemv<4, 1>(p, st);
-    if (batch == 2) return launch_gemv<4, 2>(p, st);
-    if (batch <= 4) return launch_gemv<4, 4>(p, st);
-    return launch_gemv<4, 8>(p, st);
+    if (batch == 1) return nw > 8 ? launch_gemv<1, 12>(p, L, st) : launch_gemv<1, 8>(p, L, st);
+    if (batch == 2) return nw > 8 ? launch_gemv<2, 12>(p, L, st) : launch_gemv<2, 8>(p, L, st);
+    if (batch <= 4) return launch_gemv<4, 8>(p, L, st);
+    return launch_gemv<8, 8>(p, L, st);
 }

@@ -9,9 +9,9 @@
 // re-encoded with row-local 16-column sub-blocks, so any in_f works (the flat
 // sub-blocks of the dict may straddle rows when in_f % 16 != 0).
 //
-//   repack_count_kernel : warp per row, counts patches (exact delta > 7)
-//   scan_kernel         : exclusive scan of the counts into patch_off
-//   repack_write_kernel : warp per row, writes chunks and ordered patches
+//   repack_count_kernel : CTA per 16-row tile, record sizes per (tile, chunk)
+//   scan_kernel         : exclusive scan of the sizes into ptile_off
+//   repack_write_kernel : CTA per 16-row tile, writes chunks and records
 #include "bf16x_common.cuh"
 #include "bf16x_flat.cuh"
 #include "bf16x_resident.cuh"
@@ -19,7 +19,6 @@
 
 namespace bf16x {
 
-constexpr int kRepackWarps = 8;
 
 struct RowSlice {
     int64_t lo, hi;
@@ -77,25 +76,6 @@ __device__ __forceinline__ Enc8 encode8(const FlatStreams &f, int64_t pos0, int6
     return r;
 }
 
-__global__ void __launch_bounds__(kRepackWarps * 32)
-repack_count_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int32_t *counts) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r = row0 + (int64_t)blockIdx.x * kRepackWarps + warp;
-    if (r >= row1) return;
-    const int64_t pos0 = r * in_f;
-    const RowSlice s = row_ovf_slice(f, pos0, in_f);
-    const int nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
-    int total = 0;
-    for (int c = 0; c < nch; ++c) {
-        const Enc8 e = encode8(f, pos0, in_f, c, s);
-        int n = __popc(e.pmask);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
-        total += n;
-    }
-    if (lane == 0) counts[r - row0] = total;
-}
-
 // Exclusive scan of a[0..n) in place, a[n] = total (one CTA).
 __global__ void __launch_bounds__(1024) scan_kernel(int32_t *a, int64_t n) {
     __shared__ int32_t warp_sums[32];
@@ -134,28 +114,80 @@ __global__ void __launch_bounds__(1024) scan_kernel(int32_t *a, int64_t n) {
     if (tid == 0) a[n] = carry_s;
 }
 
-__global__ void __launch_bounds__(kRepackWarps * 32)
-repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1,
-                    const int32_t *__restrict__ patch_off, uint8_t *__restrict__ layout,
-                    uint32_t *__restrict__ patches) {
+// One CTA per 16-row tile, one warp per row.  Counts the patches (exact delta
+// > 7) of every (tile, chunk) and writes the record sizes in words.
+__global__ void __launch_bounds__(kTileRows * 32)
+repack_count_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int nch, int32_t *rec_sizes) {
+    extern __shared__ int cnt[];   // [nch]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r = row0 + (int64_t)blockIdx.x * kRepackWarps + warp;
-    if (r >= row1) return;
+    for (int c = threadIdx.x; c < nch; c += blockDim.x) cnt[c] = 0;
+    __syncthreads();
+    const int64_t r = row0 + (int64_t)blockIdx.x * kTileRows + warp;
+    if (r < row1) {
+        const int64_t pos0 = r * in_f;
+        const RowSlice s = row_ovf_slice(f, pos0, in_f);
+        for (int c = 0; c < nch; ++c) {
+            const Enc8 e = encode8(f, pos0, in_f, c, s);
+            int n = __popc(e.pmask);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+            if (lane == 0 && n) atomicAdd(&cnt[c], n);
+        }
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < nch; c += blockDim.x)
+        rec_sizes[(int64_t)blockIdx.x * nch + c] = (int32_t)rec_words(cnt[c]);
+}
+
+// One CTA per 16-row tile: pass A counts each row's patches per chunk and
+// half (columns < 128 / >= 128), pass B writes the resident chunks, the
+// record headers and the entries sorted by (half, row, column).
+__global__ void __launch_bounds__(kTileRows * 32)
+repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int nch,
+                    const int32_t *__restrict__ ptile_off, uint8_t *__restrict__ layout,
+                    uint32_t *__restrict__ precs) {
+    extern __shared__ uint16_t rc[];   // [16][nch][2]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t tile = blockIdx.x;
+    const int64_t r = row0 + tile * kTileRows + warp;
+    const bool valid = r < row1;
     const int64_t pos0 = r * in_f;
-    const RowSlice s = row_ovf_slice(f, pos0, in_f);
-    const int nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
+    const RowSlice s = valid ? row_ovf_slice(f, pos0, in_f) : RowSlice{0, 0};
+    const int half = lane >> 4;        // lanes 0..15: columns 0..127, 16..31: 128..255
+    for (int c = 0; c < nch; ++c) {
+        int n = 0;
+        if (valid) {
+            const Enc8 e = encode8(f, pos0, in_f, c, s);
+            n = __popc(e.pmask);
+#pragma unroll
+            for (int o = 8; o; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);   // sum within the half
+        }
+        if ((lane & 15) == 0) rc[(warp * nch + c) * 2 + half] = (uint16_t)n;
+    }
+    __syncthreads();
     const int64_t row_bytes = resident_row_bytes(in_f);
     uint8_t *row = layout + (r - row0) * row_bytes;
-    int32_t out_pos = patch_off[r - row0];
     for (int c = 0; c < nch; ++c) {
+        int n_low = 0, start_low = 0, start_high = 0, n_all = 0;
+        for (int q = 0; q < kTileRows; ++q) {
+            const int v0 = rc[(q * nch + c) * 2], v1 = rc[(q * nch + c) * 2 + 1];
+            if (q < warp) { start_low += v0; start_high += v1; }
+            n_low += v0;
+            n_all += v0 + v1;
+        }
+        uint32_t *rec = precs + ptile_off[tile * nch + c];
+        if (warp == 0 && lane == 0) rec[0] = (uint32_t)n_low | ((uint32_t)n_all << 16);
+        if (warp == kTileRows - 1) {
+            const int64_t used = kRecHdrWords + n_all, words = rec_words(n_all);
+            for (int64_t w = used + lane; w < words; w += 32) rec[w] = 0u;
+        }
+        if (!valid) continue;
         const Enc8 e = encode8(f, pos0, in_f, c, s);
         uint8_t *chunk = row + (int64_t)c * kChunkBytes;
-        // sign|mant bytes, natural order: 8 per lane
         uint2 smv;
         smv.x = e.sm[0] | (e.sm[1] << 8) | (e.sm[2] << 16) | (e.sm[3] << 24);
         smv.y = e.sm[4] | (e.sm[5] << 8) | (e.sm[6] << 16) | (e.sm[7] << 24);
         *reinterpret_cast<uint2 *>(chunk + kSmOff + 8 * lane) = smv;
-        // delta words of group q = lane / 4; this lane holds pairs 4*(lane&3) .. +3
         uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
         for (int pp = 0; pp < 4; ++pp) {
@@ -182,23 +214,24 @@ repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1,
             dp[0] = w0; dp[1] = w1; dp[2] = w2;
         }
         if ((lane & 1) == 0) chunk[kEOff + (lane >> 1)] = (uint8_t)e.emax;
-        // ordered patches: exclusive prefix of the per-lane counts
+        // ordered entries: exclusive prefix of the per-lane counts within the half
         const int n = __popc(e.pmask);
         int x = n;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
+        for (int o = 1; o < 16; o <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, x, o);
-            if (lane >= o) x += y;
+            if ((lane & 15) >= o) x += y;
         }
-        int wpos = out_pos + x - n;
+        const int base = half ? n_low + start_high : start_low;
+        uint32_t *dst = rec + kRecHdrWords + base + (x - n);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if (e.pmask & (1u << i)) {
-                const uint32_t col = (uint32_t)(c * kChunkElems + 8 * lane + i);
-                patches[wpos++] = col | (e.d[i] << 16) | (e.sm[i] << 24);
+                const uint32_t col = (uint32_t)(8 * lane + i);
+                const uint32_t bits = ((e.sm[i] & 0x80u) << 8) | (((e.emax - e.d[i]) & 0xFFu) << 7) | (e.sm[i] & 0x7Fu);
+                *dst++ = frag_index((uint32_t)warp, col) | ((col >> 7) << 11) | (bits << 16);
             }
         }
-        out_pos += __shfl_sync(0xffffffffu, x, 31);
     }
 }
 
@@ -212,44 +245,50 @@ __global__ void validate_ovf_kernel(const int32_t *idx, int64_t n_ovf, int64_t n
     }
 }
 
-// Resident layout -> bf16 bits.  Lane = one 32-column group: lanes 8u..8u+7
-// cover chunk 4*it + u.  Patches are applied by the same warp after its row
-// is written.
-__global__ void __launch_bounds__(kRepackWarps * 32)
-resident_decode_kernel(const uint8_t *__restrict__ layout, const int32_t *__restrict__ patch_off,
-                       const uint32_t *__restrict__ patches, int64_t rows, int64_t in_f,
+// Resident layout -> bf16 bits.  One CTA per 16-row tile: warp w decodes row
+// w (lane = one 32-column group, lanes 8u..8u+7 cover chunk 4*it + u), then
+// the CTA applies the tile's patch records.
+__global__ void __launch_bounds__(kTileRows * 32)
+resident_decode_kernel(const uint8_t *__restrict__ layout, const int32_t *__restrict__ ptile_off,
+                       const uint32_t *__restrict__ precs, int64_t rows, int64_t in_f,
                        uint16_t *__restrict__ out, int64_t ld_out, bool vec_ok) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r = (int64_t)blockIdx.x * kRepackWarps + warp;
-    if (r >= rows) return;
+    const int64_t tile = blockIdx.x;
+    const int64_t r = tile * kTileRows + warp;
     const int64_t row_bytes = resident_row_bytes(in_f);
-    const uint8_t *row = layout + r * row_bytes;
-    uint16_t *orow = out + r * ld_out;
     const int nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
-    for (int c = lane >> 3; c < nch; c += 4) {
-        const int q = lane & 7;
-        uint32_t sm[8], dw[3], e2lo, e2hi;
-        load_group(row + (int64_t)c * kChunkBytes, q, sm, dw, e2lo, e2hi);
-        GroupPairs g;
-        decode_pairs_from<0>(g, sm, dw, e2lo, e2hi);
-        const int64_t k0 = (int64_t)c * kChunkElems + 32 * q;
-        if (k0 + 32 <= in_f && vec_ok) {
-            uint4 *dst = reinterpret_cast<uint4 *>(orow + k0);
+    if (r < rows) {
+        const uint8_t *row = layout + r * row_bytes;
+        uint16_t *orow = out + r * ld_out;
+        for (int c = lane >> 3; c < nch; c += 4) {
+            const int q = lane & 7;
+            uint32_t sm[8], dw[3], e2lo, e2hi;
+            load_group(row + (int64_t)c * kChunkBytes, q, sm, dw, e2lo, e2hi);
+            GroupPairs g;
+            decode_pairs_from<0>(g, sm, dw, e2lo, e2hi);
+            const int64_t k0 = (int64_t)c * kChunkElems + 32 * q;
+            if (k0 + 32 <= in_f && vec_ok) {
+                uint4 *dst = reinterpret_cast<uint4 *>(orow + k0);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(g.w[4 * i], g.w[4 * i + 1], g.w[4 * i + 2], g.w[4 * i + 3]);
-        } else {
+                for (int i = 0; i < 4; ++i)
+                    dst[i] = make_uint4(g.w[4 * i], g.w[4 * i + 1], g.w[4 * i + 2], g.w[4 * i + 3]);
+            } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (k0 + i < in_f) orow[k0 + i] = (uint16_t)(g.w[i >> 1] >> (16 * (i & 1)));
+                for (int i = 0; i < 32; ++i)
+                    if (k0 + i < in_f) orow[k0 + i] = (uint16_t)(g.w[i >> 1] >> (16 * (i & 1)));
+            }
         }
     }
-    __syncwarp();
-    const int32_t lo = patch_off[r], hi = patch_off[r + 1];
-    for (int32_t j = lo + lane; j < hi; j += 32) {
-        const uint32_t ent = patches[j];
-        const uint32_t col = ent & 0xFFFFu;
-        const uint32_t em = row[(col >> 8) * kChunkBytes + kEOff + ((col & 255u) >> 4)];
-        orow[col] = (uint16_t)patch_bits(ent, em);
+    __syncthreads();
+    for (int c = 0; c < nch; ++c) {
+        const uint32_t *rec = precs + ptile_off[tile * nch + c];
+        const int n_all = (int)(rec[0] >> 16);
+        for (int j = threadIdx.x; j < n_all; j += blockDim.x) {
+            const uint32_t ent = rec[kRecHdrWords + j];
+            uint32_t rt, cc;
+            frag_position(ent, rt, cc);
+            out[(tile * kTileRows + rt) * ld_out + (int64_t)c * kChunkElems + cc] = (uint16_t)(ent >> 16);
+        }
     }
 }
 
@@ -280,25 +319,27 @@ extern "C" int bf16x_repack_count(const uint32_t *sign, int64_t n_sign_words,
                                   const uint8_t *emax, int64_t n_emax,
                                   const int32_t *ovf_idx, const uint8_t *ovf_val, int64_t n_ovf,
                                   int64_t out_f, int64_t in_f, int64_t row0, int64_t row1,
-                                  int32_t *patch_off, void *stream) {
+                                  int32_t *ptile_off, void *stream) {
     int rc = check_flat_args("bf16x_repack_count", sign, n_sign_words, mant, n_mant_words, delta, n_delta_words,
                              emax, n_emax, ovf_idx, ovf_val, n_ovf, out_f, in_f, row0, row1);
     if (rc) return rc;
-    if (!patch_off) return set_error(BF16X_ERR_INVALID, "bf16x_repack_count: null patch_off");
+    if (!ptile_off) return set_error(BF16X_ERR_INVALID, "bf16x_repack_count: null ptile_off");
     cudaStream_t st = (cudaStream_t)stream;
     FlatStreams f{sign, n_sign_words, mant, n_mant_words, delta, n_delta_words,
                   emax, n_emax, ovf_idx, ovf_val, n_ovf, out_f * in_f};
     const int64_t rows = row1 - row0;
+    const int nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
+    const int64_t n_tiles = (rows + kTileRows - 1) / kTileRows;
     if (n_ovf > 0) {
         validate_ovf_kernel<<<(unsigned)std::min<int64_t>((n_ovf + 255) / 256, 4096), 256, 0, st>>>(ovf_idx, n_ovf, f.n);
         if ((rc = check_launch("validate_ovf_kernel"))) return rc;
     }
-    if (rows > 0) {
-        repack_count_kernel<<<(unsigned)((rows + kRepackWarps - 1) / kRepackWarps), kRepackWarps * 32, 0, st>>>(
-            f, in_f, row0, row1, patch_off);
+    if (n_tiles > 0) {
+        repack_count_kernel<<<(unsigned)n_tiles, kTileRows * 32, nch * sizeof(int), st>>>(
+            f, in_f, row0, row1, nch, ptile_off);
         if ((rc = check_launch("repack_count_kernel"))) return rc;
     }
-    scan_kernel<<<1, 1024, 0, st>>>(patch_off, rows);
+    scan_kernel<<<1, 1024, 0, st>>>(ptile_off, n_tiles * nch);
     return check_launch("scan_kernel");
 }
 
@@ -308,34 +349,37 @@ extern "C" int bf16x_repack(const uint32_t *sign, int64_t n_sign_words,
                             const uint8_t *emax, int64_t n_emax,
                             const int32_t *ovf_idx, const uint8_t *ovf_val, int64_t n_ovf,
                             int64_t out_f, int64_t in_f, int64_t row0, int64_t row1,
-                            const int32_t *patch_off, uint8_t *layout, uint32_t *patches,
+                            const int32_t *ptile_off, uint8_t *layout, uint32_t *precs,
                             void *stream) {
     int rc = check_flat_args("bf16x_repack", sign, n_sign_words, mant, n_mant_words, delta, n_delta_words,
                              emax, n_emax, ovf_idx, ovf_val, n_ovf, out_f, in_f, row0, row1);
     if (rc) return rc;
-    if (!patch_off || !layout) return set_error(BF16X_ERR_INVALID, "bf16x_repack: null output");
-    if (reinterpret_cast<uintptr_t>(layout) & 15u)
-        return set_error(BF16X_ERR_INVALID, "bf16x_repack: layout must be 16-byte aligned");
+    if (!ptile_off || !layout || !precs) return set_error(BF16X_ERR_INVALID, "bf16x_repack: null output");
+    if ((reinterpret_cast<uintptr_t>(layout) | reinterpret_cast<uintptr_t>(precs)) & 15u)
+        return set_error(BF16X_ERR_INVALID, "bf16x_repack: layout and records must be 16-byte aligned");
     const int64_t rows = row1 - row0;
     if (rows == 0) return BF16X_OK;
     FlatStreams f{sign, n_sign_words, mant, n_mant_words, delta, n_delta_words,
                   emax, n_emax, ovf_idx, ovf_val, n_ovf, out_f * in_f};
-    repack_write_kernel<<<(unsigned)((rows + kRepackWarps - 1) / kRepackWarps), kRepackWarps * 32, 0,
-                          (cudaStream_t)stream>>>(f, in_f, row0, row1, patch_off, layout, patches);
+    const int nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
+    const int64_t n_tiles = (rows + kTileRows - 1) / kTileRows;
+    repack_write_kernel<<<(unsigned)n_tiles, kTileRows * 32, 2 * kTileRows * nch * sizeof(uint16_t),
+                          (cudaStream_t)stream>>>(f, in_f, row0, row1, nch, ptile_off, layout, precs);
     return check_launch("repack_write_kernel");
 }
 
-extern "C" int bf16x_resident_decode(const uint8_t *layout, const int32_t *patch_off,
-                                     const uint32_t *patches, int64_t rows, int64_t in_f,
+extern "C" int bf16x_resident_decode(const uint8_t *layout, const int32_t *ptile_off,
+                                     const uint32_t *precs, int64_t rows, int64_t in_f,
                                      uint16_t *out, int64_t ld_out, void *stream) {
     if (rows < 0 || in_f <= 0 || ld_out < in_f)
         return set_error(BF16X_ERR_INVALID, "bf16x_resident_decode: bad shape");
     if (rows == 0) return BF16X_OK;
-    if (!layout || !patch_off || !out) return set_error(BF16X_ERR_INVALID, "bf16x_resident_decode: null pointer");
+    if (!layout || !ptile_off || !precs || !out)
+        return set_error(BF16X_ERR_INVALID, "bf16x_resident_decode: null pointer");
     if (reinterpret_cast<uintptr_t>(layout) & 15u)
         return set_error(BF16X_ERR_INVALID, "bf16x_resident_decode: layout must be 16-byte aligned");
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15u) == 0) && (ld_out % 8 == 0);
-    resident_decode_kernel<<<(unsigned)((rows + kRepackWarps - 1) / kRepackWarps), kRepackWarps * 32, 0,
-                             (cudaStream_t)stream>>>(layout, patch_off, patches, rows, in_f, out, ld_out, vec_ok);
+    resident_decode_kernel<<<(unsigned)((rows + kTileRows - 1) / kTileRows), kTileRows * 32, 0,
+                             (cudaStream_t)stream>>>(layout, ptile_off, precs, rows, in_f, out, ld_out, vec_ok);
     return check_launch("resident_decode_kernel");
 }

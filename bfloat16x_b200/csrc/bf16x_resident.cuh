@@ -23,7 +23,20 @@
 //
 // The subtraction never borrows across fields because delta <= emax.  Weights
 // whose exact delta exceeds 7 decode to emax - 7 here and are corrected from
-// the per-row patch table (u32: col | delta << 16 | sign_mant << 24).
+// the patch records.
+//
+// Patch records: rows are grouped in tiles of 16; for every (tile, chunk)
+// there is one record of 16-byte-aligned words at precs + ptile_off[tile *
+// nchunks + chunk]:
+//   word 0       n_low (bits 0..15): entries in columns 0..127 of the chunk,
+//                n_all (bits 16..31): all entries
+//   words 1..    entries sorted by (column >= 128, row, column), u32 each:
+//                frag (bits 0..10) | half (bit 11) | exact bf16 bits << 16
+//                where half = column >= 128 and frag is the element's 16-bit
+//                slot in the mma fragment order of its half chunk (see
+//                frag_index): the GEMV stores the value there directly.
+//   zero padding to a multiple of 4 words.
+// ptile_off has n_tiles * nchunks + 1 entries; the last one is the total.
 #pragma once
 
 #include "bf16x_common.cuh"
@@ -35,6 +48,12 @@ constexpr int kChunkBytes = 368;
 constexpr int kSmOff = 0;
 constexpr int kDOff = 256;
 constexpr int kEOff = 352;
+constexpr int kTileRows = 16;
+constexpr int kRecHdrWords = 1;
+
+__host__ __device__ inline int64_t rec_words(int64_t n_entries) {
+    return (kRecHdrWords + n_entries + 3) / 4 * 4;
+}
 
 __host__ __device__ inline int64_t resident_row_bytes(int64_t in_f) {
     return (in_f + kChunkElems - 1) / kChunkElems * kChunkBytes;
@@ -87,7 +106,28 @@ __device__ __forceinline__ void load_group(const uint8_t *chunk, int q, uint32_t
     e2hi = (e >> 8) * 0x00800080u;
 }
 
-// Exact bf16 bits of a patched element.
+// Position of element (row, col) of a 16-row x 256-column chunk inside the
+// mma.m16n8k16 A-fragment buffer of its half (128 columns): 8 steps x 32
+// lanes x 4 registers x 2 halves of 16 bits.  Lane (g, t) holds rows g and
+// g+8 of the 32-column group t; step J carries group columns 4J..4J+3 as
+// pairs 2J (registers 0/1: rows g/g+8) and 2J+1 (registers 2/3).
+__host__ __device__ inline uint32_t frag_index(uint32_t row, uint32_t col) {
+    const uint32_t kk = col & 127u;
+    const uint32_t owner = 4u * (row & 7u) + (kk >> 5);
+    const uint32_t step = (kk >> 2) & 7u;
+    const uint32_t reg = (row >> 3) + 2u * ((kk >> 1) & 1u);
+    return (step * 32u + owner) * 8u + reg * 2u + (kk & 1u);
+}
+
+// Inverse of frag_index: (row, col) from a patch entry.
+__host__ __device__ inline void frag_position(uint32_t entry, uint32_t &row, uint32_t &col) {
+    const uint32_t idx = entry & 0x7FFu, half = (entry >> 11) & 1u;
+    const uint32_t hw = idx & 1u, reg = (idx >> 1) & 3u, owner = (idx >> 3) & 31u, step = idx >> 8;
+    row = (owner >> 2) + 8u * (reg & 1u);
+    col = 128u * half + 32u * (owner & 3u) + 4u * step + 2u * (reg >> 1) + hw;
+}
+
+// Exact bf16 bits of a patched element (flat-entry form: delta, sign|mant).
 __device__ __forceinline__ uint32_t patch_bits(uint32_t entry, uint32_t emax) {
     const uint32_t val = (entry >> 16) & 0xFFu, sm = entry >> 24;
     return ((sm & 0x80u) << 8) | (((emax - val) & 0xFFu) << 7) | (sm & 0x7Fu);

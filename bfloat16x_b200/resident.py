@@ -3,8 +3,8 @@
 ``ResidentWeight`` is what the fused Linear modules hold: the weight rows in
 the resident layout (chunks of 256 columns, 368 bytes each: sign|mant bytes,
 pair-aligned 3-bit deltas, row-local emax -- 11.5 bits per weight) plus a
-per-row CSR of exact-delta patches for the ~3% of weights whose exponent is
-more than 7 below their sub-block maximum.  It is built once from a
+patch record per (16-row tile, 256-column chunk) for the ~3% of weights whose
+exponent is more than 7 below their sub-block maximum.  It is built once from a
 bf16x_quantize dict by the ``bf16x_repack_count`` / ``bf16x_repack`` kernels
 (the counterpart of the reference modules' device preparation,
 bf16x_fused.py:154-192 and bf16x_gemm_fused.py:163-184) and can hold a row
@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import BF16X_DTYPE_BF16, BF16X_DTYPE_F32, CHUNK_BYTES, CHUNK_ELEMS, call, ptr
+from ._lib import BF16X_DTYPE_BF16, BF16X_DTYPE_F32, CHUNK_BYTES, CHUNK_ELEMS, TILE_ROWS, call, ptr
 
 _FLAT = ("sign_packed", "mant_packed", "delta_packed", "emax", "delta_ovf_idx", "delta_ovf_val")
 
@@ -47,18 +47,52 @@ def flat_args(f: dict):
             ptr(f["delta_ovf_idx"]) if n_ovf else None, ptr(f["delta_ovf_val"]) if n_ovf else None, n_ovf)
 
 
+_SCRATCH: dict = {}
+
+
+def gemv_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
+    """GEMV partial-sum scratch for (device, current stream), grown on demand.
+    Its contents never need initialising."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream)
+    ws = _SCRATCH.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _SCRATCH[key] = ws
+    return ws
+
+
+_ALL_COUNTERS: list = []
+
+
+def reset_workspaces() -> None:
+    """Re-zero the tile counters of every weight (after a kernel reported an
+    error, a counter may have been left non-zero)."""
+    for ref in list(_ALL_COUNTERS):
+        t = ref()
+        if t is not None:
+            t.zero_()
+
+
 class ResidentWeight:
     """Rows [row0, row1) of a BF16X weight in the resident kernel layout."""
 
-    def __init__(self, layout: torch.Tensor, patch_off: torch.Tensor, patches: torch.Tensor,
+    def __init__(self, layout: torch.Tensor, ptile_off: torch.Tensor, precs: torch.Tensor,
                  rows: int, in_f: int, out_f: int | None = None, row0: int = 0):
         self.layout = layout
-        self.patch_off = patch_off
-        self.patches = patches
+        self.ptile_off = ptile_off
+        self.precs = precs
         self.rows = int(rows)
         self.in_f = int(in_f)
         self.out_f = int(out_f if out_f is not None else rows)
         self.row0 = int(row0)
+        self._n_patches = None
+        self._scratch_need = None
+        # one zeroed counter per 16-row tile, reset by the kernel after use
+        self.tile_counters = torch.zeros((self.rows + TILE_ROWS - 1) // TILE_ROWS + 1, dtype=torch.int32,
+                                         device=layout.device)
+        import weakref
+        _ALL_COUNTERS.append(weakref.ref(self.tile_counters))
 
     # ------------------------------------------------------------------ build
     @classmethod
@@ -73,21 +107,25 @@ class ResidentWeight:
         dev = torch.device(device)
         if dev.type != "cuda":
             raise _lib.Bf16xError("ResidentWeight lives on a CUDA device")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
         r0, r1 = (0, out_f) if row_range is None else (int(row_range[0]), int(row_range[1]))
         rows = r1 - r0
         f = flat_on_device(p, dev)
         row_bytes = int(_lib.lib().bf16x_resident_row_bytes(in_f))
+        nch = (in_f + CHUNK_ELEMS - 1) // CHUNK_ELEMS
+        n_rec = (rows + TILE_ROWS - 1) // TILE_ROWS * nch
         with torch.cuda.device(dev):
             st = torch.cuda.current_stream(dev).cuda_stream
-            patch_off = torch.empty(rows + 1, dtype=torch.int32, device=dev)
-            call("bf16x_repack_count", *flat_args(f), out_f, in_f, r0, r1, ptr(patch_off), st)
-            n_patch = int(patch_off[rows].item())
+            ptile_off = torch.empty(n_rec + 1, dtype=torch.int32, device=dev)
+            call("bf16x_repack_count", *flat_args(f), out_f, in_f, r0, r1, ptile_off.data_ptr(), st)
+            words = int(ptile_off[n_rec].item())
             layout = torch.empty((rows, row_bytes), dtype=torch.uint8, device=dev)
-            patches = torch.empty(max(n_patch, 1), dtype=torch.int32, device=dev)
-            call("bf16x_repack", *flat_args(f), out_f, in_f, r0, r1, ptr(patch_off), ptr(layout),
-                 ptr(patches), st)
+            precs = torch.zeros(max(words, 4), dtype=torch.int32, device=dev)
+            call("bf16x_repack", *flat_args(f), out_f, in_f, r0, r1, ptile_off.data_ptr(), ptr(layout),
+                 ptr(precs), st)
             _lib.check_device_status(dev.index)
-        return cls(layout, patch_off, patches, rows, in_f, out_f=out_f, row0=r0)
+        return cls(layout, ptile_off, precs, rows, in_f, out_f=out_f, row0=r0)
 
     # ------------------------------------------------------------ properties
     @property
@@ -104,11 +142,16 @@ class ResidentWeight:
 
     @property
     def n_patches(self) -> int:
-        return int(self.patch_off[-1].item())
+        """Number of exact-delta patches (entries of all records)."""
+        if self._n_patches is None:
+            offs = self.ptile_off[:-1].long()
+            n_all = self.precs.view(torch.int16)[offs * 2 + 1].to(torch.int32) & 0xFFFF
+            self._n_patches = int(n_all.sum().item())
+        return self._n_patches
 
     def nbytes(self) -> int:
-        """Bytes the fused kernels stream per full pass: layout + patch table + offsets."""
-        return self.layout.numel() + 4 * self.n_patches + 4 * self.patch_off.numel()
+        """Bytes the fused kernels stream per full pass: layout + patch records + record offsets."""
+        return self.layout.numel() + 4 * int(self.ptile_off[-1].item()) + 4 * self.ptile_off.numel()
 
     def bits_per_weight(self) -> float:
         return 8.0 * self.nbytes() / max(1, self.rows * self.in_f)
@@ -122,7 +165,7 @@ class ResidentWeight:
         if out is None:
             out = torch.empty((self.rows, self.in_f), dtype=torch.bfloat16, device=self.device)
         with torch.cuda.device(self.device):
-            call("bf16x_resident_decode", ptr(self.layout), ptr(self.patch_off), ptr(self.patches),
+            call("bf16x_resident_decode", ptr(self.layout), ptr(self.ptile_off), ptr(self.precs),
                  self.rows, self.in_f, ptr(out), out.stride(0), self._stream())
         return out
 
@@ -151,8 +194,13 @@ class ResidentWeight:
         if bias is not None:
             b = bias.to(device=self.device, dtype=torch.bfloat16).contiguous()
         with torch.cuda.device(self.device):
-            call("bf16x_gemv", ptr(self.layout), ptr(self.patch_off), ptr(self.patches), self.rows, self.in_f,
-                 ptr(xp), B, xp.stride(0), ptr(b), ptr(out), ydt, out.stride(0), self._stream())
+            if self._scratch_need is None:
+                self._scratch_need = int(_lib.lib().bf16x_gemv_scratch_bytes(self.rows, self.in_f))
+            ws = gemv_scratch(self.device, self._scratch_need)
+            call("bf16x_gemv", ptr(self.layout), ptr(self.ptile_off), ptr(self.precs), self.rows, self.in_f,
+                 ptr(xp), B, xp.stride(0), ptr(b), ptr(out), ydt, out.stride(0), ptr(self.tile_counters),
+                 ptr(ws), ws.numel(),
+                 self._stream())
         return out
 
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None,
@@ -168,4 +216,4 @@ class ResidentWeight:
         return y.reshape(*x.shape[:-1], self.rows)
 
 
-__all__ = ["ResidentWeight", "flat_on_device", "flat_args", "GEMV_MAX_BATCH"]
+__all__ = ["ResidentWeight", "flat_on_device", "flat_args", "gemv_scratch", "reset_workspaces", "GEMV_MAX_BATCH"]

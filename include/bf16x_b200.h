@@ -21,9 +21,10 @@
  *   resident layout: the kernel layout built once per weight by bf16x_repack:
  *                    rows of ceil(in_f/256) chunks of 368 bytes
  *                    ([256 B sign|mant bytes][96 B pair-aligned deltas][16 B emax]),
- *                    i.e. the same 11.5 bits per weight, plus a per-row CSR of
- *                    patches for exponent deltas > 7 (u32 entries:
- *                    col | true_delta << 16 | sign_mant << 24).
+ *                    i.e. the same 11.5 bits per weight, plus one patch record
+ *                    per (16-row tile, 256-column chunk) for the weights whose
+ *                    exact exponent delta exceeds 7 (u32 entries:
+ *                    col_in_chunk | row_in_tile << 8 | delta << 16 | sign_mant << 24).
  *   GGUF blocks    : 46-byte blocks of 32 weights (bf16x_gguf_block.py:6-17).
  */
 #ifndef BF16X_B200_H
@@ -91,12 +92,14 @@ int bf16x_quantize(const uint16_t *w, int64_t n, int sub, const void *scratch,
 /* Replaces the per-layer device preparation of Bf16xFused.__init__
  * (bf16x_fused.py:154-192: _pad1 + CSR build) and Bf16xGemmLinear.__init__
  * (bf16x_gemm_fused.py:163-184).  Rows [row0, row1) of the flat dict are
- * decoded exactly (overflow applied) and re-encoded into the resident layout.
+ * decoded exactly (overflow applied) and re-encoded into the resident layout:
+ * row-major chunks of 368 bytes, and one patch record per (16-row tile,
+ * 256-column chunk) holding the weights whose exact exponent delta exceeds 7.
  *   bf16x_resident_row_bytes: bytes per row of the layout.
- *   bf16x_repack_count: patch counts -> patch_off[0..rows] (exclusive scan,
- *                       device int32, rows+1 entries); patch_off[rows] is the
- *                       total.
- *   bf16x_repack: writes layout [rows][row_bytes] and patches (u32).
+ *   bf16x_repack_count: record sizes -> ptile_off[0..n_tiles*n_chunks]
+ *                       (device int32, exclusive scan in words; the last
+ *                       entry is the total record words).
+ *   bf16x_repack: writes layout [rows][row_bytes] and the records (u32).
  * in_f must be <= 65536. */
 int64_t bf16x_resident_row_bytes(int64_t in_f);
 int bf16x_repack_count(const uint32_t *sign, int64_t n_sign_words,
@@ -105,34 +108,40 @@ int bf16x_repack_count(const uint32_t *sign, int64_t n_sign_words,
                        const uint8_t *emax, int64_t n_emax,
                        const int32_t *ovf_idx, const uint8_t *ovf_val, int64_t n_ovf,
                        int64_t out_f, int64_t in_f, int64_t row0, int64_t row1,
-                       int32_t *patch_off, void *stream);
+                       int32_t *ptile_off, void *stream);
 int bf16x_repack(const uint32_t *sign, int64_t n_sign_words,
                  const uint32_t *mant, int64_t n_mant_words,
                  const uint32_t *delta, int64_t n_delta_words,
                  const uint8_t *emax, int64_t n_emax,
                  const int32_t *ovf_idx, const uint8_t *ovf_val, int64_t n_ovf,
                  int64_t out_f, int64_t in_f, int64_t row0, int64_t row1,
-                 const int32_t *patch_off, uint8_t *layout, uint32_t *patches,
+                 const int32_t *ptile_off, uint8_t *layout, uint32_t *precs,
                  void *stream);
 
-/* Resident layout -> bf16 bits [rows][in_f] (bit-exact, patches applied).
+/* Resident layout -> bf16 bits [rows][ld_out] (bit-exact, patches applied).
  * Used by the two-segment path (Bf16xFused 'opt' mode, bf16x_fused.py:194-205). */
-int bf16x_resident_decode(const uint8_t *layout, const int32_t *patch_off,
-                          const uint32_t *patches, int64_t rows, int64_t in_f,
+int bf16x_resident_decode(const uint8_t *layout, const int32_t *ptile_off,
+                          const uint32_t *precs, int64_t rows, int64_t in_f,
                           uint16_t *out, int64_t ld_out, void *stream);
 
 /* ---- fused decode + GEMV (batch 1..8) ----------------------------------- */
 /* Replaces bf16x_fused_gemv / _bf16x_gemv_fused_kernel (bf16x_fused.py:32-127):
  * y[b][n] = sum_k W[n][k] * x[b][k] (+ bias[n]) for b < batch <= 8, with W
  * read from the resident layout and decoded in registers, patches applied
- * exactly, fp32 accumulation.  x: bf16 [batch][ldx], ldx >= ceil(in_f/256)*256
- * elements with zeros past in_f, rows 16-byte aligned.  bias: bf16 [rows] or
- * NULL.  y: [batch][ldy] of y_dtype (BF16X_DTYPE_BF16 or _F32). */
-int bf16x_gemv(const uint8_t *layout, const int32_t *patch_off, const uint32_t *patches,
+ * exactly, fp32 accumulation, deterministic.  x: bf16 [batch][ldx],
+ * ldx >= ceil(in_f/256)*256 elements with zeros past in_f, rows 16-byte
+ * aligned.  bias: bf16 [rows] or NULL.  y: [batch][ldy] of y_dtype.
+ * tile_counters: ceil(rows/16) int32 owned by the weight, zero-filled once;
+ * every successful call leaves them zero.  scratch: bf16x_gemv_scratch_bytes
+ * (rows, in_f) bytes of device memory (for the current device) holding the
+ * partial sums of tiles that several warps share; no initialisation needed.
+ * Calls that may overlap on the GPU need their own counters and scratch. */
+int64_t bf16x_gemv_scratch_bytes(int64_t rows, int64_t in_f);
+int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
                int64_t rows, int64_t in_f,
                const uint16_t *x, int64_t batch, int64_t ldx,
                const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
-               void *stream);
+               int32_t *tile_counters, void *scratch, int64_t scratch_bytes, void *stream);
 
 #ifdef __cplusplus
 }

@@ -57,11 +57,11 @@ def _err(L):
 
 def test_invalid_arguments_rejected_on_host(L):
     # batch out of range
-    rc = L.bf16x_gemv(None, None, None, 16, 256, None, 9, 256, None, None, 0, 16, None)
+    rc = L.bf16x_gemv(None, None, None, 16, 256, None, 9, 256, None, None, 0, 16, None, None, 0, None)
     assert rc == -1
     assert "batch" in _err(L)
     # in_f too large for the resident layout
-    assert L.bf16x_gemv(None, None, None, 16, 70000, None, 1, 70144, None, None, 0, 16, None) < 0
+    assert L.bf16x_gemv(None, None, None, 16, 70000, None, 1, 70144, None, None, 0, 16, None, None, 0, None) < 0
     assert "65536" in _err(L)
     # unsupported sub-block size
     assert L.bf16x_decode(None, 1, None, 7, None, 3, None, 2, None, None, 0, 1, 32, 8, None, None) < 0
@@ -74,6 +74,14 @@ def test_invalid_arguments_rejected_on_host(L):
     assert L.bf16x_decode(None, 0, None, 0, None, 0, None, 0, None, None, 0, 0, 16, 16, None, None) == 0
 
 
+def test_gemv_missing_counters_and_scratch(L):
+    # counters and scratch are checked on the host before any launch
+    assert L.bf16x_gemv_scratch_bytes(0, 256) == 0
+    v = ctypes.c_void_p(256)
+    assert L.bf16x_gemv(v, v, v, 16, 256, v, 1, 256, None, v, 0, 16, None, v, 1 << 30, None) < 0
+    assert "tile_counters" in _err(L)
+
+
 def test_error_raises_python_exception():
     with pytest.raises(_lib.Bf16xError, match="batch"):
-        _lib.call("bf16x_gemv", None, None, None, 16, 256, None, 0, 256, None, None, 0, 16, None)
+        _lib.call("bf16x_gemv", None, None, None, 16, 256, None, 0, 256, None, None, 0, 16, None, None, 0, None)

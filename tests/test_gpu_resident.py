@@ -63,8 +63,11 @@ def _gemv_check(w_bits, x_bf16, rw, bias=None):
 @pytest.mark.parametrize("b", [1, 3, 8])
 def test_gemv_matches_reference(case, b):
     yref = FLAT[f"{case}/y{b}"]
-    if not np.isfinite(yref).all():
-        pytest.skip("fp32 overflow in the reference result")
+    if not np.isfinite(yref).all() or np.abs(yref).max() > 1e37:
+        # sums within a factor ~30 of FLT_MAX overflow or not depending on the
+        # fp32 summation order; the decoded weights themselves are checked bit
+        # for bit by test_repack_decode_matches_reference
+        pytest.skip("result at the fp32 overflow threshold")
     p = dict_from_npz(FLAT, case)
     rw = ResidentWeight.from_packed(p, device="cuda")
     x = bf16_from_bits(FLAT[f"{case}/x{b}"], "cuda")
@@ -91,8 +94,23 @@ def test_gemv_bias_and_determinism():
     bias = torch.randn(777).to(torch.bfloat16)
     _gemv_check(wb, x, rw, bias=bias)
     a = rw.gemv(x.cuda(), bias=bias.cuda(), out_dtype=torch.float32)
-    b = rw.gemv(x.cuda(), bias=bias.cuda(), out_dtype=torch.float32)
-    assert torch.equal(a, b)
+    for _ in range(5):
+        b = rw.gemv(x.cuda(), bias=bias.cuda(), out_dtype=torch.float32)
+        assert torch.equal(a, b)
+    assert int(rw.tile_counters.abs().sum()) == 0   # split-tile counters left at zero
+
+
+def test_gemv_interleaved_shapes_share_scratch():
+    # weights of different shapes share the per-stream scratch; each keeps its own counters
+    ws = []
+    for shape in [(4096, 4096), (1000, 1536), (4096, 4096), (64, 14336)]:
+        w = synthetic_weight(*shape, seed=41)
+        wb = bits_of(w)
+        ws.append((wb, ResidentWeight.from_packed(oracle_dict(wb), device="cuda")))
+    for rep in range(2):
+        for wb, rw in ws:
+            for b in (1, 2, 8):
+                _gemv_check(wb, synthetic_activation(b, wb.shape[1], seed=b + rep), rw)
 
 
 @pytest.mark.parametrize("shape", [(14336, 4096), (4096, 14336)])
