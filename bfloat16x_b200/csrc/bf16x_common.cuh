@@ -133,6 +133,12 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *map, int c0, 
         :: "r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)) : "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory accesses with later
+// async-proxy ones (TMA writes, tensor-core reads) of the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const void *map) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(map) : "memory");
 }

@@ -1,0 +1,473 @@
+// bf16x_gemm.cu -- fused BF16X decode + GEMM on the 5th-generation tensor
+// cores (tcgen05 / TMEM), sm_100a.
+//
+// Replaces _bf16x_gemm_fused_kernel / bf16x_fused_gemm
+// (bf16x_gemm_fused.py:31-114), and unlike it applies the exact-delta
+// patches, so the product equals the matmul with the exact bf16 weights.
+//
+//   y[m][n] = sum_k x[m][k] * W[n][k] (+ bias[n])
+//
+// One persistent CTA per SM walks output tiles of 128 weight rows x BN tokens.
+// The MMA is D[128 rows][BN tokens] += A[128][64] * B[BN][64]^T per k-block of
+// 64 columns: A = the decoded weights, B = the activations, both K-major
+// 128-byte-swizzled in shared memory, D in tensor memory.
+//
+// Warp roles (15 warps):
+//   0      W producer: one TMA per 256-column chunk (128 rows x 368 bytes of
+//          the resident layout) + the eight 16-row patch records of the chunk
+//   1      B producer: one swizzled TMA per k-block (BN rows x 64 columns)
+//   2      MMA issuer: TMEM allocation, 4 x tcgen05.mma (K=16) per k-block,
+//          tcgen05.commit to release the A and B slots and to publish a tile
+//   3..10  decoders: each k-block (128 x 64 weights) is decoded from the
+//          compressed chunk into the swizzled A slot (five integer ops per
+//          pair), patched with the exact values, fenced for the async proxy
+//   11..14 epilogue: tcgen05.ld of the fp32 accumulator (each warp its TMEM
+//          lane quarter = 32 weight rows), bias, coalesced transposed stores
+// The accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of one tile overlaps the MMAs of the next.  Every wait is bounded;
+// a role that gives up raises the shared abort flag, every role then leaves
+// its loop, and TMEM is released before the kernel returns.
+#include <algorithm>
+#include <mutex>
+
+#include <cuda_runtime.h>
+
+#include "bf16x_common.cuh"
+#include "bf16x_resident.cuh"
+#include "bf16x_status.cuh"
+#include "bf16x_tmap.h"
+
+namespace bf16x {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 15 * 32;
+constexpr int kGemmRecCap = 192;                     // record words staged per 16-row sub-tile
+constexpr int kGemmWStage = kGemmBM * kChunkBytes;   // 47104
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int kWStages = 2;
+    static constexpr int kAStages = 3;
+    static constexpr int kBStages = BN >= 256 ? 2 : 3;
+    static constexpr int kAStage = kGemmBM * 128;     // 16 KB
+    static constexpr int kBStage = BN * 128;
+    static constexpr int kRecStage = 8 * kGemmRecCap * 4;
+    static constexpr int kAOff = 0;                                       // 1024-aligned slots first
+    static constexpr int kBOff = kAOff + kAStages * kAStage;
+    static constexpr int kWOff = kBOff + kBStages * kBStage;
+    static constexpr int kROff = kWOff + kWStages * kGemmWStage;
+    static constexpr int kBarOff = kROff + kWStages * kRecStage;
+    // barriers: w_full, w_empty (2 each), a_full, a_empty (3), b_full, b_empty, acc_full, acc_empty (2)
+    static constexpr int kNumBars = 2 * kWStages + 2 * kAStages + 2 * kBStages + 4;
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;               // tmem base, abort flag, decoder flag
+    static constexpr int kSmem = kMiscOff + 16 + 1024;                    // + alignment slack
+    static constexpr int kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+    static_assert(kSmem <= 227 * 1024, "shared memory");
+};
+
+struct GemmParams {
+    CUtensorMap wmap;    // resident layout [rows][chunks][92 words], box 128 rows x 1 chunk
+    CUtensorMap xmap;    // activations [M][in_f] bf16, box BN rows x 64 columns, 128B swizzle
+    const int32_t *ptile_off;
+    const uint32_t *precs;
+    int64_t rows, M;
+    int nch, n_tiles16;
+    int tiles_n, tiles_total;
+    const uint16_t *bias;
+    void *y;
+    int y_f32;
+    int64_t ldy;
+};
+
+// ------------------------------------------------------------- tcgen05 glue
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+    // K-major, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes apart
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);          // start address
+    d |= (uint64_t)1u << 16;                               // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024u >> 4) << 32;                     // stride byte offset
+    d |= (uint64_t)1u << 46;                               // descriptor version (sm100)
+    d |= (uint64_t)2u << 61;                               // layout: SWIZZLE_128B
+    return d;
+}
+
+template <int BN>
+__host__ __device__ constexpr uint32_t umma_idesc_bf16() {
+    return (1u << 4)                       // D: f32
+         | (1u << 7)                       // A: bf16
+         | (1u << 10)                      // B: bf16
+         | ((uint32_t)(BN >> 3) << 17)     // N
+         | ((uint32_t)(kGemmBM >> 4) << 24);   // M = 128
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory");
+}
+
+// Byte offset of element (row, col) inside a 128-row x 64-column K-major
+// 128-byte-swizzled tile (16-byte chunk index XOR row % 8).
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
+    return row * 128u + ((((col >> 3) ^ row) & 7u) << 4) + ((col & 7u) << 1);
+}
+
+// Bounded wait used by every role; on timeout (or if another role already
+// gave up) the abort flag is raised and false is returned.
+__device__ __forceinline__ bool role_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    if (*abort_flag) return false;
+    if (mbar_wait(bar, parity, &g_status)) return true;
+    *abort_flag = 1;
+    return false;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+    using C = GemmCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled operand slots
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
+    uint64_t *w_full = bars, *w_empty = w_full + C::kWStages;
+    uint64_t *a_full = w_empty + C::kWStages, *a_empty = a_full + C::kAStages;
+    uint64_t *b_full = a_empty + C::kAStages, *b_empty = b_full + C::kBStages;
+    uint64_t *acc_full = b_empty + C::kBStages, *acc_empty = acc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kWStages; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], 1); }
+        for (int s = 0; s < C::kAStages; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
+        for (int s = 0; s < C::kBStages; ++s) { mbar_init(&b_full[s], 1); mbar_init(&b_empty[s], 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
+        abort_flag[0] = 0;
+        abort_flag[1] = 0;
+        fence_mbar_init();
+    }
+    if (warp == 2) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(tmem_slot)), "r"(C::kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int nkb = p.nch * 4;                     // k-blocks per tile
+
+    if (warp == 0) {
+        // ------------------------------------------------------- W producer
+        if (lane == 0) {
+            prefetch_tensormap(&p.wmap);
+            int ws = 0;
+            uint32_t wph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
+                const int rt = t / p.tiles_n;
+                for (int c = 0; c < p.nch && ok; ++c) {
+                    int32_t off[8], len[8];
+                    int total = 0;
+#pragma unroll
+                    for (int sub = 0; sub < 8; ++sub) {
+                        const int64_t t16 = (int64_t)rt * 8 + sub;
+                        if (t16 < p.n_tiles16) {
+                            const int64_t i = t16 * p.nch + c;
+                            off[sub] = __ldg(p.ptile_off + i);
+                            len[sub] = min(__ldg(p.ptile_off + i + 1) - off[sub], kGemmRecCap);
+                        } else {
+                            off[sub] = 0;
+                            len[sub] = 0;
+                        }
+                        total += len[sub];
+                    }
+                    if (!role_wait(&w_empty[ws], wph ^ 1u, abort_flag)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(kGemmWStage + total * 4));
+                    tma_load_3d(smem + C::kWOff + ws * kGemmWStage, &p.wmap, 0, c, rt * kGemmBM, &w_full[ws]);
+                    uint8_t *rec = smem + C::kROff + ws * C::kRecStage;
+#pragma unroll
+                    for (int sub = 0; sub < 8; ++sub)
+                        if (len[sub] > 0)
+                            bulk_g2s(rec + sub * kGemmRecCap * 4, p.precs + off[sub], (uint32_t)len[sub] * 4, &w_full[ws]);
+                    if (++ws == C::kWStages) { ws = 0; wph ^= 1u; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- B producer
+        if (lane == 0) {
+            prefetch_tensormap(&p.xmap);
+            int bs = 0;
+            uint32_t bph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
+                const int nt = t % p.tiles_n;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!role_wait(&b_empty[bs], bph ^ 1u, abort_flag)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&b_full[bs], (uint32_t)C::kBStage);
+                    tma_load_2d(smem + C::kBOff + bs * C::kBStage, &p.xmap, kb * kGemmBK, nt * BN, &b_full[bs]);
+                    if (++bs == C::kBStages) { bs = 0; bph ^= 1u; }
+                }
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16<BN>();
+            int as = 0, bs = 0, ac = 0;
+            uint32_t aph = 0, bph = 0, acph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
+                if (!role_wait(&acc_empty[ac], acph ^ 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(ac * BN);
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!role_wait(&a_full[as], aph, abort_flag) || !role_wait(&b_full[bs], bph, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = umma_desc_sw128(smem_u32(smem + C::kAOff + as * C::kAStage));
+                    const uint64_t bd = umma_desc_sw128(smem_u32(smem + C::kBOff + bs * C::kBStage));
+#pragma unroll
+                    for (int k16 = 0; k16 < kGemmBK / 16; ++k16)   // 32 bytes along K per step
+                        umma_bf16(d_tmem, ad + 2u * k16, bd + 2u * k16, idesc, (kb | k16) != 0);
+                    umma_commit(&a_empty[as]);
+                    umma_commit(&b_empty[bs]);
+                    if (++as == C::kAStages) { as = 0; aph ^= 1u; }
+                    if (++bs == C::kBStages) { bs = 0; bph ^= 1u; }
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[ac]);
+                if (++ac == 2) { ac = 0; acph ^= 1u; }
+            }
+        }
+    } else if (warp <= 10) {
+        // ------------------------------------------------------- decoders
+        // One thread waits on the pipeline barriers and publishes the
+        // outcome through the named barrier, so the 256 decoder threads
+        // always agree on whether to continue (no thread is left alone at a
+        // bar.sync after a timeout).
+        volatile int *dec_ok = abort_flag + 1;
+        const int dt = (warp - 3) * 32 + lane;        // 0..255
+        const int row = dt >> 1, hh = dt & 1;         // weight row, 32-column half of the k-block
+        int ws = 0, as = 0;
+        uint32_t wph = 0, aph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
+            const int rt = t / p.tiles_n;
+            const int nsub = (int)(p.n_tiles16 - (int64_t)rt * 8 < 8 ? p.n_tiles16 - (int64_t)rt * 8 : 8);
+            for (int c = 0; c < p.nch && ok; ++c) {
+                const uint8_t *wst = smem + C::kWOff + ws * kGemmWStage;
+                const uint32_t *rec = reinterpret_cast<const uint32_t *>(smem + C::kROff + ws * C::kRecStage);
+                for (int kq = 0; kq < 4; ++kq) {
+                    if (dt == 0) {
+                        bool w = true;
+                        if (kq == 0) w = role_wait(&w_full[ws], wph, abort_flag);
+                        w = w && role_wait(&a_empty[as], aph ^ 1u, abort_flag);
+                        *dec_ok = w ? 1 : 0;
+                    }
+                    named_bar_sync(1, 256);
+                    if (!*dec_ok) { ok = false; break; }
+                    uint8_t *ast = smem + C::kAOff + as * C::kAStage;
+                    {
+                        // row `row`, columns 64*kq + 32*hh .. +31 of the chunk
+                        uint32_t sm[8], dw[3], e2lo, e2hi;
+                        load_group(wst + row * kChunkBytes, 2 * kq + hh, sm, dw, e2lo, e2hi);
+                        GroupPairs gp;
+                        decode_pairs_from<0>(gp, sm, dw, e2lo, e2hi);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t col = 32u * hh + 8u * i;
+                            *reinterpret_cast<uint4 *>(ast + sw128_offset((uint32_t)row, col)) =
+                                make_uint4(gp.w[4 * i], gp.w[4 * i + 1], gp.w[4 * i + 2], gp.w[4 * i + 3]);
+                        }
+                    }
+                    named_bar_sync(1, 256);
+                    // exact values of the patched weights of this k-block
+                    const int half = kq >> 1;
+                    int base = 0;
+                    for (int sub = 0; sub < nsub; ++sub) {
+                        const uint32_t *r = rec + sub * kGemmRecCap;
+                        const uint32_t hdr = r[0];
+                        const int lo = half ? (int)(hdr & 0xFFFFu) : 0;
+                        const int hi = half ? (int)(hdr >> 16) : (int)(hdr & 0xFFFFu);
+                        for (int j = lo + ((dt - base) & 255); j < hi; j += 256) {
+                            const uint32_t ent = (kRecHdrWords + j < kGemmRecCap)
+                                                     ? r[kRecHdrWords + j]
+                                                     : __ldg(p.precs + __ldg(p.ptile_off + ((int64_t)rt * 8 + sub) * p.nch + c) +
+                                                             kRecHdrWords + j);
+                            uint32_t rr, cc;
+                            frag_position(ent, rr, cc);
+                            if ((cc >> 6) == (uint32_t)kq) {
+                                *reinterpret_cast<uint16_t *>(ast + sw128_offset(16u * sub + rr, cc & 63u)) =
+                                    (uint16_t)(ent >> 16);
+                            }
+                        }
+                        base += hi - lo;
+                    }
+                    fence_proxy_async_smem();
+                    named_bar_sync(1, 256);
+                    if (dt == 0) mbar_arrive(&a_full[as]);
+                    if (++as == C::kAStages) { as = 0; aph ^= 1u; }
+                }
+                if (!ok) break;
+                if (dt == 0) mbar_arrive(&w_empty[ws]);
+                if (++ws == C::kWStages) { ws = 0; wph ^= 1u; }
+            }
+        }
+    } else {
+        // ------------------------------------------------------- epilogue
+        const int qd = warp & 3;                       // TMEM lane quarter
+        int ac = 0;
+        uint32_t acph = 0;
+        for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x) {
+            if (!role_wait(&acc_full[ac], acph, abort_flag)) break;
+            tc_fence_after();
+            const int rt = t / p.tiles_n, nt = t % p.tiles_n;
+            const int64_t row = (int64_t)rt * kGemmBM + 32 * qd + lane;
+            const float bias = (p.bias && row < p.rows) ? bf16_bits_to_f32(__ldg(p.bias + row)) : 0.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem_base + ((uint32_t)(32 * qd) << 16) + (uint32_t)(ac * BN + c0), v);
+                if (row < p.rows) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int64_t n = (int64_t)nt * BN + c0 + i;
+                        if (n < p.M) {
+                            const float o = __uint_as_float(v[i]) + bias;
+                            if (p.y_f32) reinterpret_cast<float *>(p.y)[n * p.ldy + row] = o;
+                            else reinterpret_cast<uint16_t *>(p.y)[n * p.ldy + row] = f32_to_bf16_bits_rn(o);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ac]);
+            if (++ac == 2) { ac = 0; acph ^= 1u; }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                     :: "r"(tmem_base), "r"(C::kTmemCols) : "memory");
+    }
+}
+
+static int gemm_sms() {
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = sms > 0 ? sms : 1;
+    }
+    return cache[dev];
+}
+
+template <int BN>
+static int launch_gemm(GemmParams &p, const uint8_t *layout, int64_t in_f, const uint16_t *x, int64_t ldx,
+                       cudaStream_t st) {
+    using C = GemmCfg<BN>;
+    const cuuint64_t wdims[3] = {(cuuint64_t)(kChunkBytes / 4), (cuuint64_t)p.nch, (cuuint64_t)p.rows};
+    const cuuint64_t wstr[2] = {(cuuint64_t)kChunkBytes, (cuuint64_t)resident_row_bytes(in_f)};
+    const cuuint32_t wbox[3] = {(cuuint32_t)(kChunkBytes / 4), 1u, (cuuint32_t)kGemmBM};
+    if (!encode_tiled(&p.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, layout, wdims, wstr, wbox))
+        return set_error(BF16X_ERR_CUDA, "bf16x_gemm: weight tensor map");
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t xdims[2] = {(cuuint64_t)in_f, (cuuint64_t)p.M};
+    const cuuint64_t xstr[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t xbox[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)BN};
+    const cuuint32_t estr[2] = {1, 1};
+    if (fn(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), xdims, xstr, xbox, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return set_error(BF16X_ERR_CUDA, "bf16x_gemm: activation tensor map");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool attr_set[64] = {false};
+    if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: device index");
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: smem attribute: %s", cudaGetErrorString(e));
+        attr_set[dev] = true;
+    }
+    const int grid = std::min(p.tiles_total, gemm_sms());
+    gemm_kernel<BN><<<grid, kGemmThreads, C::kSmem, st>>>(p);
+    return check_launch("bf16x_gemm");
+}
+
+}  // namespace bf16x
+
+using namespace bf16x;
+
+extern "C" int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                          int64_t rows, int64_t in_f, const uint16_t *x, int64_t M, int64_t ldx,
+                          const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream) {
+    if (rows < 0 || in_f <= 0 || M < 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemm: bad shape");
+    if (in_f > 65536) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: in_f > 65536");
+    if (y_dtype != BF16X_DTYPE_BF16 && y_dtype != BF16X_DTYPE_F32)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemm: bad y_dtype");
+    if (rows == 0 || M == 0) return BF16X_OK;
+    if (!layout || !ptile_off || !precs || !x || !y) return set_error(BF16X_ERR_INVALID, "bf16x_gemm: null pointer");
+    if (ldx < in_f || (ldx % 8) != 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemm: ldx must be >= in_f and a multiple of 8");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(layout) | reinterpret_cast<uintptr_t>(precs)) & 15u)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemm: x, layout and records must be 16-byte aligned");
+    if (ldy < rows) return set_error(BF16X_ERR_INVALID, "bf16x_gemm: ldy < rows");
+    GemmParams p;
+    p.ptile_off = ptile_off;
+    p.precs = precs;
+    p.rows = rows;
+    p.M = M;
+    p.nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
+    p.n_tiles16 = (int)((rows + kTileRows - 1) / kTileRows);
+    p.bias = bias;
+    p.y = y;
+    p.y_f32 = y_dtype == BF16X_DTYPE_F32;
+    p.ldy = ldy;
+    const int64_t tiles_m = (rows + kGemmBM - 1) / kGemmBM;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int sms = gemm_sms();
+    // token tile: 256 when that still fills the GPU, else smaller
+    int bn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    if (bn == 256 && tiles_m * ((M + 255) / 256) < sms) bn = 128;
+    p.tiles_n = (int)((M + bn - 1) / bn);
+    const int64_t total = tiles_m * p.tiles_n;
+    if (total > 0x7fffffffLL) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: too many tiles");
+    p.tiles_total = (int)total;
+    if (bn == 64) return launch_gemm<64>(p, layout, in_f, x, ldx, st);
+    if (bn == 128) return launch_gemm<128>(p, layout, in_f, x, ldx, st);
+    return launch_gemm<256>(p, layout, in_f, x, ldx, st);
+}

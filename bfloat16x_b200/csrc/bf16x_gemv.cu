@@ -103,10 +103,6 @@ __device__ __forceinline__ void mma_bf16_16816(float &c0, float &c1, float &c2, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // Decode step J of one group: k-slots (2t, 2t+1 | 2t+8, 2t+9) of mma step J
 // carry the group's columns 4J..4J+3, i.e. pairs 2J (a0/a1) and 2J+1 (a2/a3)
 // of rows g (a0/a2) and g+8 (a1/a3).  The lane stores them as one 16-byte

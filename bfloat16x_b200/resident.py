@@ -203,16 +203,37 @@ class ResidentWeight:
                  self._stream())
         return out
 
+    def gemm(self, x: torch.Tensor, bias: torch.Tensor | None = None,
+             out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y[m, n] = sum_k W[n, k] x[m, k] (+ bias) on the tensor cores, any number of rows m."""
+        _lib.require_cuda(x, "x")
+        x2 = x.reshape(-1, self.in_f).to(torch.bfloat16)
+        M = x2.shape[0]
+        if not (x2.is_contiguous() and x2.data_ptr() % 16 == 0 and self.in_f % 8 == 0):
+            ld = (self.in_f + 7) // 8 * 8
+            xp = torch.zeros((M, ld), dtype=torch.bfloat16, device=self.device)
+            xp[:, : self.in_f] = x2
+            x2 = xp
+        if out is None:
+            out = torch.empty((M, self.rows), dtype=out_dtype, device=self.device)
+        ydt = {torch.bfloat16: BF16X_DTYPE_BF16, torch.float32: BF16X_DTYPE_F32}[out.dtype]
+        b = None if bias is None else bias.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        with torch.cuda.device(self.device):
+            call("bf16x_gemm", ptr(self.layout), ptr(self.ptile_off), ptr(self.precs), self.rows, self.in_f,
+                 ptr(x2), M, x2.stride(0), ptr(b), ptr(out), ydt, out.stride(0), self._stream())
+        return out
+
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None,
                out_dtype: torch.dtype | None = None) -> torch.Tensor:
-        """x[..., in_f] -> [..., rows] with the fused kernels."""
+        """x[..., in_f] -> [..., rows]: the GEMV kernel for up to 8 rows of
+        activations, the tensor-core GEMM above that."""
         od = out_dtype or (x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.bfloat16)
         x2 = x.reshape(-1, self.in_f)
         M = x2.shape[0]
-        y = torch.empty((M, self.rows), dtype=od, device=self.device)
-        for m0 in range(0, M, GEMV_MAX_BATCH):
-            m1 = min(M, m0 + GEMV_MAX_BATCH)
-            self.gemv(x2[m0:m1], bias, out=y[m0:m1])
+        if M <= GEMV_MAX_BATCH:
+            y = self.gemv(x2, bias, out_dtype=od)
+        else:
+            y = self.gemm(x2, bias, out_dtype=od)
         return y.reshape(*x.shape[:-1], self.rows)
 
 

@@ -143,6 +143,20 @@ int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *
                const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
                int32_t *tile_counters, void *scratch, int64_t scratch_bytes, void *stream);
 
+/* ---- fused decode + GEMM (tcgen05, prefill) ----------------------------- */
+/* Replaces bf16x_fused_gemm / _bf16x_gemm_fused_kernel
+ * (bf16x_gemm_fused.py:31-114): y[m][n] = sum_k x[m][k] * W[n][k] (+ bias[n])
+ * for m < M tokens, W decoded tile by tile into shared memory (exact: the
+ * patches are applied, unlike the reference's saturated decode) and
+ * multiplied on the tensor cores (tcgen05.mma, fp32 accumulation in tensor
+ * memory).  x: bf16 [M][ldx], ldx >= in_f and a multiple of 8, 16-byte
+ * aligned; columns past in_f are never read.  bias: bf16 [rows] or NULL.
+ * y: [M][ldy] of y_dtype. */
+int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+               int64_t rows, int64_t in_f,
+               const uint16_t *x, int64_t M, int64_t ldx,
+               const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

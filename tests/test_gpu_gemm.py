@@ -1,0 +1,70 @@
+"""GPU parity of the tcgen05 decode+GEMM: identity probes (bit-exact: each
+output equals one decoded weight), then random activations against the CPU
+oracle within the 1e-3 relative-L2 gate, ragged shapes included."""
+import numpy as np
+import pytest
+import torch
+
+from bfloat16x_b200 import _lib
+from bfloat16x_b200.resident import ResidentWeight
+from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
+from oracle import oracle
+from tests.gpu_util import bits_of, oracle_dict, rel_l2
+
+pytestmark = pytest.mark.gpu
+GATE = 1e-3
+
+
+@pytest.mark.parametrize("shape,M", [((128, 256), 64), ((256, 512), 256), ((300, 1536), 130), ((200, 320), 300)])
+def test_gemm_identity_probe(shape, M):
+    # x = one-hot rows: y[m, n] = W[n, m] exactly (fp32 of the bf16 weight)
+    rows, in_f = shape
+    w = synthetic_weight(rows, in_f, seed=3)
+    wb = bits_of(w)
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    M = min(M, in_f)
+    x = torch.zeros(M, in_f, dtype=torch.bfloat16)
+    x[torch.arange(M), torch.arange(M)] = 1.0
+    y = rw.gemm(x.cuda(), out_dtype=torch.float32).cpu().numpy()
+    expect = oracle.bf16_bits_to_f32(wb)[:, :M].T
+    assert np.array_equal(y.view(np.uint32), np.ascontiguousarray(expect).view(np.uint32))
+    _lib.check_device_status()
+
+
+@pytest.mark.parametrize("shape", [(128, 256), (1000, 1536), (333, 4099), (4096, 4096), (200, 14336)])
+@pytest.mark.parametrize("M", [9, 64, 200, 512])
+def test_gemm_vs_oracle(shape, M):
+    w = synthetic_weight(*shape, seed=5)
+    wb = bits_of(w)
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    x = synthetic_activation(M, shape[1], seed=M)
+    ref = oracle.matmul_bf16w(x.float().numpy(), wb)
+    y32 = rw.gemm(x.cuda(), out_dtype=torch.float32).cpu().numpy()
+    assert rel_l2(y32, ref) < GATE
+    y16 = rw.gemm(x.cuda(), out_dtype=torch.bfloat16).float().cpu().numpy()
+    ref16 = torch.from_numpy(ref).to(torch.bfloat16).float().numpy()
+    assert rel_l2(y16, ref16) < GATE
+
+
+def test_gemm_bias_and_dispatch():
+    w = synthetic_weight(640, 2048, seed=9)
+    wb = bits_of(w)
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    bias = torch.randn(640).to(torch.bfloat16)
+    for M in (3, 8, 9, 300):
+        x = synthetic_activation(M, 2048, seed=M)
+        ref = oracle.matmul_bf16w(x.float().numpy(), wb, bias.float().numpy())
+        y = rw.linear(x.cuda(), bias=bias.cuda(), out_dtype=torch.float32).cpu().numpy()
+        assert rel_l2(y, ref) < GATE, M
+    _lib.check_device_status()
+
+
+def test_gemm_large_m_deterministic():
+    w = synthetic_weight(4096, 4096, seed=1, device="cuda")
+    rw = ResidentWeight.from_packed(oracle_dict(bits_of(w)), device="cuda")
+    x = synthetic_activation(2048, 4096, seed=2, device="cuda")
+    a = rw.gemm(x, out_dtype=torch.float32)
+    b = rw.gemm(x, out_dtype=torch.float32)
+    assert torch.equal(a, b)
+    ref = x.float() @ w.float().T
+    assert float((a - ref).norm() / ref.norm()) < GATE
