@@ -53,6 +53,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--mode", choices=["gemv", "gemm"], default="gemv",
+                    help="gemv: decode+GEMV sweep (the headline); gemm: decode+GEMM prefill TFLOPS")
+    ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens M for --mode gemm")
     return ap.parse_args()
 
 
@@ -434,10 +437,122 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_gemm(args):
+    """Prefill: one step = the fused decode+GEMM over the four weight shapes at
+    M tokens; value = TFLOPS (2*M*out*in per launch)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    from bfloat16x_b200 import _lib
+    from bfloat16x_b200.opqk_linear import bf16x_quantize
+    from bfloat16x_b200.resident import ResidentWeight
+    from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
+
+    M = args.tokens
+    shapes = shapes_of(args)
+    layers = []
+    for si, (out_f, in_f) in enumerate(shapes):
+        rows = out_f if args.scaling == "weak" else out_f // world + (out_f % world if rank == world - 1 else 0)
+        w = synthetic_weight(rows, in_f, seed=1000 * si + rank, device=dev)
+        rw = ResidentWeight.from_packed(bf16x_quantize(w, device=dev), device=dev)
+        x = synthetic_activation(M, in_f, seed=si + 1, device=dev)
+        y = torch.empty((M, rows), dtype=torch.bfloat16, device=dev)
+        layers.append(dict(rw=rw, x=x, y=y, w=None if args.no_cublas else w, rows=rows, in_f=in_f))
+        del w
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def step():
+        for L in layers:
+            L["rw"].gemm(L["x"], out=L["y"])
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    clock = ClockSampler(local)
+    clock.start()
+    per_layer = [0.0] * len(layers)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in layers]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    a.record()
+    for _ in range(args.steps):
+        for i, L in enumerate(layers):
+            ev[i][0].record()
+            L["rw"].gemm(L["x"], out=L["y"])
+            ev[i][1].record()
+    b.record()
+    barrier()
+    clocks = clock.stop()
+    el = a.elapsed_time(b)
+    for i in range(len(layers)):
+        per_layer[i] = ev[i][0].elapsed_time(ev[i][1])   # last step's launch
+    if world > 1:
+        t = torch.tensor([el], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    flops = sum(2.0 * M * L["rows"] * L["in_f"] for L in layers) * args.steps * world
+    value = flops / (el / 1e3) / 1e12
+    _lib.check_device_status(local)
+    dom = max(range(len(layers)), key=lambda i: per_layer[i])
+    Ld = layers[dom]
+    ach = 2.0 * M * Ld["rows"] * Ld["in_f"] / (per_layer[dom] / 1e3) / 1e12
+    peak_tf, peak_kind = 1688.4, "measured"
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak_tf = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        peak_tf, peak_kind = 1590.0, "fallback"
+    cublas = None
+    if not args.no_cublas:
+        import torch.nn.functional as F
+        for L in layers:
+            F.linear(L["x"], L["w"])
+        barrier()
+        a.record()
+        for _ in range(args.steps):
+            for L in layers:
+                F.linear(L["x"], L["w"])
+        b.record()
+        barrier()
+        c_ms = a.elapsed_time(b) / args.steps
+        cublas = {"ms_per_step": round(c_ms, 4), "TFLOPS": round(flops / args.steps / world / (c_ms / 1e3) / 1e12, 1),
+                  "note": "torch F.linear (cuBLAS) on the uncompressed bf16 weights"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(el / args.steps, 4), "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "configs[2] fused decode+GEMM prefill: " + ", ".join(f"{o}x{i}" for o, i in shapes)
+                                   + f" at M={M} tokens", "tokens": M, "l2": "inputs larger than L2"},
+            "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per_layer[i], 4) for i, L in enumerate(layers)},
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": round(ach / peak_tf, 4), "peak_source": peak_kind,
+                         "kernel": f"gemm_kernel {Ld['rows']}x{Ld['in_f']} M={M}", "traffic": None},
+            "gpu_launches": args.steps * len(layers), "clocks": clocks, "cublas_bf16": cublas,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "gemm":
+        run_gemm(args)
     else:
         run_ours(args)
 

@@ -12,16 +12,18 @@
 // 64 columns: A = the decoded weights, B = the activations, both K-major
 // 128-byte-swizzled in shared memory, D in tensor memory.
 //
-// Warp roles (15 warps):
-//   0      W producer: one TMA per 256-column chunk (128 rows x 368 bytes of
-//          the resident layout) + the eight 16-row patch records of the chunk
+// Warp roles (23 warps):
+//   0      W producer: per 256-column chunk two TMAs of 64 rows x 368 bytes
+//          of the resident layout (a ring of half-tile stages) + the four
+//          16-row patch records of each half
 //   1      B producer: one swizzled TMA per k-block (BN rows x 64 columns)
 //   2      MMA issuer: TMEM allocation, 4 x tcgen05.mma (K=16) per k-block,
 //          tcgen05.commit to release the A and B slots and to publish a tile
-//   3..10  decoders: each k-block (128 x 64 weights) is decoded from the
-//          compressed chunk into the swizzled A slot (five integer ops per
-//          pair), patched with the exact values, fenced for the async proxy
-//   11..14 epilogue: tcgen05.ld of the fp32 accumulator (each warp its TMEM
+//   3..18  decoders, two groups of 8 alternating k-blocks: each k-block
+//          (128 x 64 weights) is decoded from the compressed chunk into the
+//          swizzled A slot (five integer ops per pair), patched with the
+//          exact values, fenced for the async proxy
+//   19..22 epilogue: tcgen05.ld of the fp32 accumulator (each warp its TMEM
 //          lane quarter = 32 weight rows), bias, coalesced transposed stores
 // The accumulator is double-buffered in TMEM (2 x BN columns), so the
 // epilogue of one tile overlaps the MMAs of the next.  Every wait is bounded;
@@ -41,33 +43,40 @@ namespace bf16x {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-constexpr int kGemmThreads = 15 * 32;
+constexpr int kGemmDecWarps = 16;                  // two groups of 8, alternating k-blocks
+constexpr int kGemmThreads = (3 + kGemmDecWarps + 4) * 32;
 constexpr int kGemmRecCap = 192;                     // record words staged per 16-row sub-tile
-constexpr int kGemmWStage = kGemmBM * kChunkBytes;   // 47104
+#ifndef BF16X_GEMM_WROWS
+#define BF16X_GEMM_WROWS 128
+#endif
+constexpr int kGemmWRows = BF16X_GEMM_WROWS;          // weight rows per compressed stage
+constexpr int kWHalves = kGemmBM / kGemmWRows;        // compressed stages per chunk
+constexpr int kSubsPerStage = kGemmWRows / 16;        // 16-row patch records per stage
+constexpr int kGemmWStage = kGemmWRows * kChunkBytes;
 
 template <int BN>
 struct GemmCfg {
-    static constexpr int kWStages = 2;
+    static constexpr int kWStages = kWHalves == 2 ? 3 : 2;   // ring of compressed stages
     static constexpr int kAStages = 3;
-    static constexpr int kBStages = BN >= 256 ? 2 : 3;
+    static constexpr int kBStages = BN >= 256 ? (kWHalves == 2 ? 3 : 2) : 4;
     static constexpr int kAStage = kGemmBM * 128;     // 16 KB
     static constexpr int kBStage = BN * 128;
-    static constexpr int kRecStage = 8 * kGemmRecCap * 4;
+    static constexpr int kRecStage = kSubsPerStage * kGemmRecCap * 4;   // the 16-row records of a stage
     static constexpr int kAOff = 0;                                       // 1024-aligned slots first
     static constexpr int kBOff = kAOff + kAStages * kAStage;
     static constexpr int kWOff = kBOff + kBStages * kBStage;
     static constexpr int kROff = kWOff + kWStages * kGemmWStage;
     static constexpr int kBarOff = kROff + kWStages * kRecStage;
-    // barriers: w_full, w_empty (2 each), a_full, a_empty (3), b_full, b_empty, acc_full, acc_empty (2)
+    // barriers: w_full, w_empty, a_full, a_empty, b_full, b_empty, acc_full, acc_empty (2)
     static constexpr int kNumBars = 2 * kWStages + 2 * kAStages + 2 * kBStages + 4;
-    static constexpr int kMiscOff = kBarOff + kNumBars * 8;               // tmem base, abort flag, decoder flag
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;               // tmem base, abort flag
     static constexpr int kSmem = kMiscOff + 16 + 1024;                    // + alignment slack
     static constexpr int kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
     static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct GemmParams {
-    CUtensorMap wmap;    // resident layout [rows][chunks][92 words], box 128 rows x 1 chunk
+    CUtensorMap wmap;    // resident layout [rows][chunks][92 words], box 64 rows x 1 chunk
     CUtensorMap xmap;    // activations [M][in_f] bf16, box BN rows x 64 columns, 128B swizzle
     const int32_t *ptile_off;
     const uint32_t *precs;
@@ -161,8 +170,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::kWStages; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], 1); }
-        for (int s = 0; s < C::kAStages; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
+        for (int s = 0; s < C::kWStages; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], kGemmDecWarps / kWHalves); }
+        for (int s = 0; s < C::kAStages; ++s) { mbar_init(&a_full[s], 8); mbar_init(&a_empty[s], 1); }
         for (int s = 0; s < C::kBStages; ++s) { mbar_init(&b_full[s], 1); mbar_init(&b_empty[s], 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
         abort_flag[0] = 0;
@@ -182,39 +191,56 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
     if (warp == 0) {
         // ------------------------------------------------------- W producer
+        // Stages are (tile, chunk, half) in order; the record offsets of the
+        // next stage are loaded while the current one is issued, so their
+        // global-memory latency stays off the critical path.
         if (lane == 0) {
             prefetch_tensormap(&p.wmap);
             int ws = 0;
             uint32_t wph = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
-                const int rt = t / p.tiles_n;
-                for (int c = 0; c < p.nch && ok; ++c) {
-                    int32_t off[8], len[8];
-                    int total = 0;
+            const int per_tile = p.nch * kWHalves;
+            int t = blockIdx.x, c = 0, hf = 0;
+            int32_t off[kSubsPerStage], len[kSubsPerStage];
+            auto load_offsets = [&](int tt, int cc, int hh) {
+                const int rt = tt / p.tiles_n;
 #pragma unroll
-                    for (int sub = 0; sub < 8; ++sub) {
-                        const int64_t t16 = (int64_t)rt * 8 + sub;
-                        if (t16 < p.n_tiles16) {
-                            const int64_t i = t16 * p.nch + c;
-                            off[sub] = __ldg(p.ptile_off + i);
-                            len[sub] = min(__ldg(p.ptile_off + i + 1) - off[sub], kGemmRecCap);
-                        } else {
-                            off[sub] = 0;
-                            len[sub] = 0;
-                        }
-                        total += len[sub];
+                for (int sub = 0; sub < kSubsPerStage; ++sub) {
+                    const int64_t t16 = (int64_t)rt * 8 + kSubsPerStage * hh + sub;
+                    if (tt < p.tiles_total && t16 < p.n_tiles16) {
+                        const int64_t i = t16 * p.nch + cc;
+                        off[sub] = __ldg(p.ptile_off + i);
+                        len[sub] = __ldg(p.ptile_off + i + 1);
+                    } else {
+                        off[sub] = 0;
+                        len[sub] = 0;
                     }
-                    if (!role_wait(&w_empty[ws], wph ^ 1u, abort_flag)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(kGemmWStage + total * 4));
-                    tma_load_3d(smem + C::kWOff + ws * kGemmWStage, &p.wmap, 0, c, rt * kGemmBM, &w_full[ws]);
-                    uint8_t *rec = smem + C::kROff + ws * C::kRecStage;
-#pragma unroll
-                    for (int sub = 0; sub < 8; ++sub)
-                        if (len[sub] > 0)
-                            bulk_g2s(rec + sub * kGemmRecCap * 4, p.precs + off[sub], (uint32_t)len[sub] * 4, &w_full[ws]);
-                    if (++ws == C::kWStages) { ws = 0; wph ^= 1u; }
                 }
+            };
+            load_offsets(t, c, hf);
+            (void)per_tile;
+            while (t < p.tiles_total) {
+                int32_t o[kSubsPerStage], l[kSubsPerStage];
+                int total = 0;
+#pragma unroll
+                for (int sub = 0; sub < kSubsPerStage; ++sub) {
+                    o[sub] = off[sub];
+                    l[sub] = min(len[sub] - off[sub], kGemmRecCap);
+                    total += l[sub];
+                }
+                const int rt = t / p.tiles_n, cc = c, hh = hf;
+                // advance to the next stage and prefetch its offsets
+                if (++hf == kWHalves) { hf = 0; if (++c == p.nch) { c = 0; t += gridDim.x; } }
+                load_offsets(t, c, hf);
+                if (!role_wait(&w_empty[ws], wph ^ 1u, abort_flag)) break;
+                mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(kGemmWStage + total * 4));
+                tma_load_3d(smem + C::kWOff + ws * kGemmWStage, &p.wmap, 0, cc, rt * kGemmBM + kGemmWRows * hh,
+                            &w_full[ws]);
+                uint8_t *rec = smem + C::kROff + ws * C::kRecStage;
+#pragma unroll
+                for (int sub = 0; sub < kSubsPerStage; ++sub)
+                    if (l[sub] > 0)
+                        bulk_g2s(rec + sub * kGemmRecCap * 4, p.precs + o[sub], (uint32_t)l[sub] * 4, &w_full[ws]);
+                if (++ws == C::kWStages) { ws = 0; wph ^= 1u; }
             }
         }
     } else if (warp == 1) {
@@ -266,78 +292,83 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 if (++ac == 2) { ac = 0; acph ^= 1u; }
             }
         }
-    } else if (warp <= 10) {
+    } else if (warp < 3 + kGemmDecWarps) {
         // ------------------------------------------------------- decoders
-        // One thread waits on the pipeline barriers and publishes the
-        // outcome through the named barrier, so the 256 decoder threads
-        // always agree on whether to continue (no thread is left alone at a
-        // bar.sync after a timeout).
-        volatile int *dec_ok = abort_flag + 1;
-        const int dt = (warp - 3) * 32 + lane;        // 0..255
-        const int row = dt >> 1, hh = dt & 1;         // weight row, 32-column half of the k-block
-        int ws = 0, as = 0;
-        uint32_t wph = 0, aph = 0;
+        // Two groups of 8 warps take alternate k-blocks, so two k-blocks are
+        // decoded at once.  Warp d of a group owns weight rows 16d..16d+15:
+        // two lanes per row (32 columns each of the 64-column k-block), and
+        // the patch record of that 16-row sub-tile, whose entries for the
+        // k-block are one contiguous range (records are sorted by 64-column
+        // quarter).  Everything a warp writes it also patches, so warps
+        // never wait for each other; each arrives on the MMA barrier on its
+        // own (count 8 per k-block, 16 per chunk for the W slot).
+        const int dg = (warp - 3) >> 3, d = (warp - 3) & 7;
+        const int hf = d / kSubsPerStage;              // which stage of the chunk holds my rows
+        const int lrow = 16 * (d % kSubsPerStage) + (lane >> 1);   // row inside that stage
+        const int row = 16 * d + (lane >> 1), hh = lane & 1;
+        int as = 0, wseq = 0;
+        uint32_t aph = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
             const int rt = t / p.tiles_n;
-            const int nsub = (int)(p.n_tiles16 - (int64_t)rt * 8 < 8 ? p.n_tiles16 - (int64_t)rt * 8 : 8);
-            for (int c = 0; c < p.nch && ok; ++c) {
-                const uint8_t *wst = smem + C::kWOff + ws * kGemmWStage;
-                const uint32_t *rec = reinterpret_cast<const uint32_t *>(smem + C::kROff + ws * C::kRecStage);
+            const bool has_rec = (int64_t)rt * 8 + d < p.n_tiles16;
+            for (int c = 0; c < p.nch && ok; ++c, wseq += kWHalves) {
+                const int wslot = (wseq + hf) % C::kWStages;
+                const uint32_t wpar = (uint32_t)(((wseq + hf) / C::kWStages) & 1);
+                const uint8_t *wst = smem + C::kWOff + wslot * kGemmWStage;
+                const uint32_t *rec = reinterpret_cast<const uint32_t *>(smem + C::kROff + wslot * C::kRecStage) +
+                                      (d % kSubsPerStage) * kGemmRecCap;
                 for (int kq = 0; kq < 4; ++kq) {
-                    if (dt == 0) {
-                        bool w = true;
-                        if (kq == 0) w = role_wait(&w_full[ws], wph, abort_flag);
-                        w = w && role_wait(&a_empty[as], aph ^ 1u, abort_flag);
-                        *dec_ok = w ? 1 : 0;
-                    }
-                    named_bar_sync(1, 256);
-                    if (!*dec_ok) { ok = false; break; }
-                    uint8_t *ast = smem + C::kAOff + as * C::kAStage;
-                    {
-                        // row `row`, columns 64*kq + 32*hh .. +31 of the chunk
-                        uint32_t sm[8], dw[3], e2lo, e2hi;
-                        load_group(wst + row * kChunkBytes, 2 * kq + hh, sm, dw, e2lo, e2hi);
-                        GroupPairs gp;
-                        decode_pairs_from<0>(gp, sm, dw, e2lo, e2hi);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const uint32_t col = 32u * hh + 8u * i;
-                            *reinterpret_cast<uint4 *>(ast + sw128_offset((uint32_t)row, col)) =
-                                make_uint4(gp.w[4 * i], gp.w[4 * i + 1], gp.w[4 * i + 2], gp.w[4 * i + 3]);
+                    const bool mine = (kq & 1) == dg;
+                    if (mine) {
+                        int w = 1;
+                        if (lane == 0) {
+                            if (kq == dg) w = role_wait(&w_full[wslot], wpar, abort_flag);
+                            w = w && role_wait(&a_empty[as], aph ^ 1u, abort_flag);
                         }
-                    }
-                    named_bar_sync(1, 256);
-                    // exact values of the patched weights of this k-block
-                    const int half = kq >> 1;
-                    int base = 0;
-                    for (int sub = 0; sub < nsub; ++sub) {
-                        const uint32_t *r = rec + sub * kGemmRecCap;
-                        const uint32_t hdr = r[0];
-                        const int lo = half ? (int)(hdr & 0xFFFFu) : 0;
-                        const int hi = half ? (int)(hdr >> 16) : (int)(hdr & 0xFFFFu);
-                        for (int j = lo + ((dt - base) & 255); j < hi; j += 256) {
-                            const uint32_t ent = (kRecHdrWords + j < kGemmRecCap)
-                                                     ? r[kRecHdrWords + j]
-                                                     : __ldg(p.precs + __ldg(p.ptile_off + ((int64_t)rt * 8 + sub) * p.nch + c) +
-                                                             kRecHdrWords + j);
-                            uint32_t rr, cc;
-                            frag_position(ent, rr, cc);
-                            if ((cc >> 6) == (uint32_t)kq) {
-                                *reinterpret_cast<uint16_t *>(ast + sw128_offset(16u * sub + rr, cc & 63u)) =
+                        w = __shfl_sync(0xffffffffu, w, 0);
+                        if (!w) { ok = false; break; }
+                        uint8_t *ast = smem + C::kAOff + as * C::kAStage;
+                        {
+                            // row `row`, columns 64*kq + 32*hh .. +31 of the chunk
+                            uint32_t sm[8], dw[3], e2lo, e2hi;
+                            load_group(wst + lrow * kChunkBytes, 2 * kq + hh, sm, dw, e2lo, e2hi);
+                            GroupPairs gp;
+                            decode_pairs_from<0>(gp, sm, dw, e2lo, e2hi);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t col = 32u * hh + 8u * i;
+                                *reinterpret_cast<uint4 *>(ast + sw128_offset((uint32_t)row, col)) =
+                                    make_uint4(gp.w[4 * i], gp.w[4 * i + 1], gp.w[4 * i + 2], gp.w[4 * i + 3]);
+                            }
+                        }
+                        __syncwarp();
+                        if (has_rec) {
+                            // exact values of this sub-tile's patched weights in the k-block:
+                            // quarter boundaries 0 | n_q0 | n_low | n_q012 | n_all
+                            const uint32_t h0 = rec[0], h1 = rec[1];
+                            const int b1 = (int)(h1 & 0xFFFFu), b2 = (int)(h0 & 0xFFFFu), b3 = (int)(h1 >> 16);
+                            const int lo = kq == 0 ? 0 : kq == 1 ? b1 : kq == 2 ? b2 : b3;
+                            const int hi = kq == 0 ? b1 : kq == 1 ? b2 : kq == 2 ? b3 : (int)(h0 >> 16);
+                            for (int j = lo + lane; j < hi; j += 32) {
+                                const uint32_t ent = (kRecHdrWords + j < kGemmRecCap)
+                                                         ? rec[kRecHdrWords + j]
+                                                         : __ldg(p.precs + __ldg(p.ptile_off + ((int64_t)rt * 8 + d) * p.nch + c) +
+                                                                 kRecHdrWords + j);
+                                uint32_t rr, cc;
+                                frag_position(ent, rr, cc);
+                                *reinterpret_cast<uint16_t *>(ast + sw128_offset(16u * d + rr, cc & 63u)) =
                                     (uint16_t)(ent >> 16);
                             }
                         }
-                        base += hi - lo;
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&a_full[as]);
                     }
-                    fence_proxy_async_smem();
-                    named_bar_sync(1, 256);
-                    if (dt == 0) mbar_arrive(&a_full[as]);
                     if (++as == C::kAStages) { as = 0; aph ^= 1u; }
                 }
                 if (!ok) break;
-                if (dt == 0) mbar_arrive(&w_empty[ws]);
-                if (++ws == C::kWStages) { ws = 0; wph ^= 1u; }
+                if (lane == 0) mbar_arrive(&w_empty[wslot]);
             }
         }
     } else {
@@ -402,7 +433,7 @@ static int launch_gemm(GemmParams &p, const uint8_t *layout, int64_t in_f, const
     using C = GemmCfg<BN>;
     const cuuint64_t wdims[3] = {(cuuint64_t)(kChunkBytes / 4), (cuuint64_t)p.nch, (cuuint64_t)p.rows};
     const cuuint64_t wstr[2] = {(cuuint64_t)kChunkBytes, (cuuint64_t)resident_row_bytes(in_f)};
-    const cuuint32_t wbox[3] = {(cuuint32_t)(kChunkBytes / 4), 1u, (cuuint32_t)kGemmBM};
+    const cuuint32_t wbox[3] = {(cuuint32_t)(kChunkBytes / 4), 1u, (cuuint32_t)kGemmWRows};
     if (!encode_tiled(&p.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, layout, wdims, wstr, wbox))
         return set_error(BF16X_ERR_CUDA, "bf16x_gemm: weight tensor map");
     EncodeTiledFn fn = encode_tiled_fn();

@@ -140,43 +140,49 @@ repack_count_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int
 }
 
 // One CTA per 16-row tile: pass A counts each row's patches per chunk and
-// half (columns < 128 / >= 128), pass B writes the resident chunks, the
-// record headers and the entries sorted by (half, row, column).
+// quarter (64-column block), pass B writes the resident chunks, the record
+// headers and the entries sorted by (quarter, row, column).
 __global__ void __launch_bounds__(kTileRows * 32)
 repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int nch,
                     const int32_t *__restrict__ ptile_off, uint8_t *__restrict__ layout,
                     uint32_t *__restrict__ precs) {
-    extern __shared__ uint16_t rc[];   // [16][nch][2]
+    extern __shared__ uint16_t rc[];   // [16][nch][4]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t tile = blockIdx.x;
     const int64_t r = row0 + tile * kTileRows + warp;
     const bool valid = r < row1;
     const int64_t pos0 = r * in_f;
     const RowSlice s = valid ? row_ovf_slice(f, pos0, in_f) : RowSlice{0, 0};
-    const int half = lane >> 4;        // lanes 0..15: columns 0..127, 16..31: 128..255
+    const int quarter = lane >> 3;     // lanes 8q..8q+7: columns 64q..64q+63
     for (int c = 0; c < nch; ++c) {
         int n = 0;
         if (valid) {
             const Enc8 e = encode8(f, pos0, in_f, c, s);
             n = __popc(e.pmask);
 #pragma unroll
-            for (int o = 8; o; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);   // sum within the half
+            for (int o = 4; o; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);   // sum within the quarter
         }
-        if ((lane & 15) == 0) rc[(warp * nch + c) * 2 + half] = (uint16_t)n;
+        if ((lane & 7) == 0) rc[(warp * nch + c) * 4 + quarter] = (uint16_t)n;
     }
     __syncthreads();
     const int64_t row_bytes = resident_row_bytes(in_f);
     uint8_t *row = layout + (r - row0) * row_bytes;
     for (int c = 0; c < nch; ++c) {
-        int n_low = 0, start_low = 0, start_high = 0, n_all = 0;
+        int qtot[4] = {0, 0, 0, 0}, qstart[4] = {0, 0, 0, 0};
         for (int q = 0; q < kTileRows; ++q) {
-            const int v0 = rc[(q * nch + c) * 2], v1 = rc[(q * nch + c) * 2 + 1];
-            if (q < warp) { start_low += v0; start_high += v1; }
-            n_low += v0;
-            n_all += v0 + v1;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int v = rc[(q * nch + c) * 4 + k];
+                if (q < warp) qstart[k] += v;
+                qtot[k] += v;
+            }
         }
+        const int n_q0 = qtot[0], n_low = qtot[0] + qtot[1], n_q012 = n_low + qtot[2], n_all = n_q012 + qtot[3];
         uint32_t *rec = precs + ptile_off[tile * nch + c];
-        if (warp == 0 && lane == 0) rec[0] = (uint32_t)n_low | ((uint32_t)n_all << 16);
+        if (warp == 0 && lane == 0) {
+            rec[0] = (uint32_t)n_low | ((uint32_t)n_all << 16);
+            rec[1] = (uint32_t)n_q0 | ((uint32_t)n_q012 << 16);
+        }
         if (warp == kTileRows - 1) {
             const int64_t used = kRecHdrWords + n_all, words = rec_words(n_all);
             for (int64_t w = used + lane; w < words; w += 32) rec[w] = 0u;
@@ -214,16 +220,16 @@ repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int
             dp[0] = w0; dp[1] = w1; dp[2] = w2;
         }
         if ((lane & 1) == 0) chunk[kEOff + (lane >> 1)] = (uint8_t)e.emax;
-        // ordered entries: exclusive prefix of the per-lane counts within the half
+        // ordered entries: exclusive prefix of the per-lane counts within the quarter
         const int n = __popc(e.pmask);
         int x = n;
 #pragma unroll
-        for (int o = 1; o < 16; o <<= 1) {
+        for (int o = 1; o < 8; o <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, x, o);
-            if ((lane & 15) >= o) x += y;
+            if ((lane & 7) >= o) x += y;
         }
-        const int base = half ? n_low + start_high : start_low;
-        uint32_t *dst = rec + kRecHdrWords + base + (x - n);
+        const int qbase = quarter == 0 ? 0 : quarter == 1 ? n_q0 : quarter == 2 ? n_low : n_q012;
+        uint32_t *dst = rec + kRecHdrWords + qbase + qstart[quarter] + (x - n);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if (e.pmask & (1u << i)) {
@@ -363,7 +369,7 @@ extern "C" int bf16x_repack(const uint32_t *sign, int64_t n_sign_words,
                   emax, n_emax, ovf_idx, ovf_val, n_ovf, out_f * in_f};
     const int nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
     const int64_t n_tiles = (rows + kTileRows - 1) / kTileRows;
-    repack_write_kernel<<<(unsigned)n_tiles, kTileRows * 32, 2 * kTileRows * nch * sizeof(uint16_t),
+    repack_write_kernel<<<(unsigned)n_tiles, kTileRows * 32, 4 * kTileRows * nch * sizeof(uint16_t),
                           (cudaStream_t)stream>>>(f, in_f, row0, row1, nch, ptile_off, layout, precs);
     return check_launch("repack_write_kernel");
 }

@@ -30,7 +30,9 @@
 // nchunks + chunk]:
 //   word 0       n_low (bits 0..15): entries in columns 0..127 of the chunk,
 //                n_all (bits 16..31): all entries
-//   words 1..    entries sorted by (column >= 128, row, column), u32 each:
+//   word 1       n_q0 (bits 0..15): entries in columns 0..63,
+//                n_q012 (bits 16..31): entries in columns 0..191
+//   words 2..    entries sorted by (column / 64, row, column), u32 each:
 //                frag (bits 0..10) | half (bit 11) | exact bf16 bits << 16
 //                where half = column >= 128 and frag is the element's 16-bit
 //                slot in the mma fragment order of its half chunk (see
@@ -49,7 +51,7 @@ constexpr int kSmOff = 0;
 constexpr int kDOff = 256;
 constexpr int kEOff = 352;
 constexpr int kTileRows = 16;
-constexpr int kRecHdrWords = 1;
+constexpr int kRecHdrWords = 2;
 
 __host__ __device__ inline int64_t rec_words(int64_t n_entries) {
     return (kRecHdrWords + n_entries + 3) / 4 * 4;
