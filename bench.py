@@ -108,8 +108,7 @@ def cpu_sample(batch: int, seconds: float):
     bits = w.view(torch.int16).numpy().view(np.uint16)
     p = oracle.quantize(bits, out_f, in_f)
     x = synthetic_activation(batch, in_f, seed=1).float().numpy()
-    n_patch = int((p["delta_ovf_val"] > 7).sum())
-    nbytes = workload_bytes(out_f, in_f, n_patch, batch)
+    nbytes = workload_bytes(stored_weight_bytes(p, out_f, in_f), out_f, in_f, batch)
     oracle.linear(p, x)   # warm
     t0 = time.perf_counter()
     passes = 0
@@ -122,11 +121,28 @@ def cpu_sample(batch: int, seconds: float):
     return nbytes, el / passes, oracle.num_threads(), passes
 
 
-def workload_bytes(rows, in_f, n_patch, batch, y_bytes=2):
-    """Bytes one fused decode+GEMV launch must move: resident layout + patch
-    table + patch offsets + activations + outputs."""
-    row_bytes = (in_f + 255) // 256 * 368
-    return rows * row_bytes + 4 * n_patch + 4 * (rows + 1) + 2 * batch * in_f + y_bytes * batch * rows
+def workload_bytes(weight_bytes, rows, in_f, batch, y_bytes=2):
+    """Bytes one fused decode+GEMV launch must move: the stored weight
+    (resident layout + patch records + record offsets, ResidentWeight.nbytes)
+    + activations + outputs."""
+    return weight_bytes + 2 * batch * in_f + y_bytes * batch * rows
+
+
+def stored_weight_bytes(p, rows, in_f):
+    """ResidentWeight.nbytes of a flat dict, computed on the host: 368 B per
+    256-column chunk of each row, one patch record per (16-row tile, chunk) of
+    2 header words + one word per delta > 7 entry padded to 4 words, and
+    tiles x chunks + 1 record offsets.  Exact when in_f % 16 == 0 (the row-local
+    sub-blocks are then the flat ones)."""
+    import numpy as np
+    nch = (in_f + 255) // 256
+    n_tiles = (rows + 15) // 16
+    idx = np.asarray(p["delta_ovf_idx"]).astype(np.int64)
+    big = idx[np.asarray(p["delta_ovf_val"]) > 7]
+    rec = (big // in_f) // 16 * nch + (big % in_f) // 256
+    counts = np.bincount(rec, minlength=n_tiles * nch)
+    rec_words = int(((2 + counts + 3) // 4 * 4).sum())
+    return rows * nch * 368 + 4 * rec_words + 4 * (n_tiles * nch + 1)
 
 
 def run_reference(args):
@@ -145,7 +161,7 @@ def run_reference(args):
     bits = w.view(torch.int16).numpy().view(np.uint16)
     p = oracle.quantize(bits, 4096, 4096)
     x = synthetic_activation(args.batch, 4096, seed=1).float().numpy()
-    nbytes = workload_bytes(4096, 4096, int((p["delta_ovf_val"] > 7).sum()), args.batch)
+    nbytes = workload_bytes(stored_weight_bytes(p, 4096, 4096), 4096, 4096, args.batch)
     for _ in range(warmup):
         oracle.linear(p, x)
     t0 = time.perf_counter()
@@ -257,7 +273,7 @@ def run_ours(args):
         x = synthetic_activation(B, in_f, seed=si + 1, device=dev)
         y = torch.empty((B, rows), dtype=torch.bfloat16, device=dev)
         layers.append(dict(rw=rw, x=x, y=y, w=wb, rows=rows, in_f=in_f,
-                           nbytes=workload_bytes(rows, in_f, rw.n_patches, B)))
+                           nbytes=workload_bytes(rw.nbytes(), rows, in_f, B)))
     torch.cuda.synchronize()
 
     def step():

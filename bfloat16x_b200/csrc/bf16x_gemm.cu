@@ -13,9 +13,9 @@
 // 128-byte-swizzled in shared memory, D in tensor memory.
 //
 // Warp roles (23 warps):
-//   0      W producer: per 256-column chunk two TMAs of 64 rows x 368 bytes
-//          of the resident layout (a ring of half-tile stages) + the four
-//          16-row patch records of each half
+//   0      W producer: per 256-column chunk, TMAs of kGemmWRows rows x 368
+//          bytes of the resident layout (128 rows by default: one stage per
+//          chunk, in a ring of stages) + the 16-row patch records of the stage
 //   1      B producer: one swizzled TMA per k-block (BN rows x 64 columns)
 //   2      MMA issuer: TMEM allocation, 4 x tcgen05.mma (K=16) per k-block,
 //          tcgen05.commit to release the A and B slots and to publish a tile

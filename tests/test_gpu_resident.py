@@ -121,3 +121,14 @@ def test_gemv_config_shapes(shape):
     for b in (1, 8):
         _gemv_check(wb, synthetic_activation(b, shape[1], seed=b), rw)
     _lib.check_device_status()
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096), (1000, 1536), (40, 14336)])
+def test_bench_byte_count_matches_stored_weight(shape):
+    """bench.py's host-side count of the stored weight bytes (used for the CPU
+    arms' GB/s) equals what the repack actually stores."""
+    import bench
+    w = bits_of(synthetic_weight(*shape, seed=19))
+    p = oracle_dict(w)
+    rw = ResidentWeight.from_packed(p, device="cuda")
+    assert bench.stored_weight_bytes(p, *shape) == rw.nbytes()
