@@ -45,6 +45,8 @@ _SIGS = {
     "bf16x_resident_decode": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _p]),
     "bf16x_gemv_scratch_bytes": (_i64, [_i64, _i64]),
     "bf16x_gemv": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p, _p, _i64, _p]),
+    "bf16x_gemv_noalloc_max_rows": (_i64, []),
+    "bf16x_gemv_noalloc": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p]),
     "bf16x_gemm": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p]),
 }
 

@@ -504,3 +504,71 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
     if (batch <= 4) return launch_gemv<4, 8>(p, L, st);
     return launch_gemv<8, 8>(p, L, st);
 }
+
+// ------------------------------------------------ no-allocation GEMV entry
+// bf16x_gemv_noalloc serves callers that cannot hand this library device
+// memory: a plain C host or FFI binding with no device allocator of its own,
+// or a serving loop that must not call cudaMalloc/cudaFree (they synchronise
+// the device) once it is running.  Its tile counters and partial sums live in
+// one fixed, file-scope device array instead of caller-owned buffers.
+namespace bf16x {
+
+constexpr int64_t kNoAllocMaxTiles = 32768;                   // rows <= 524288
+constexpr int64_t kNoAllocCounterBytes = kNoAllocMaxTiles * 4;  // 128 KiB
+constexpr int64_t kNoAllocPartialBytes = 2ll << 20;           // 2 MiB: 2048 warps x 1 KiB
+constexpr int64_t kNoAllocBytes = kNoAllocCounterBytes + kNoAllocPartialBytes;
+
+static __device__ __align__(256) unsigned char g_gemv_noalloc_scratch[kNoAllocBytes];
+
+// Device address of g_gemv_noalloc_scratch on the current device, looked up
+// once per device (with that device current) and cached.
+static int noalloc_scratch(void **out) {
+    static void *addr[64] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv_noalloc: device index %d", dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(BF16X_ERR_CUDA, "bf16x_gemv_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return BF16X_OK;
+}
+
+}  // namespace bf16x
+
+extern "C" int64_t bf16x_gemv_noalloc_max_rows(void) { return kNoAllocMaxTiles * kTileRows; }
+
+extern "C" int bf16x_gemv_noalloc(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                                  int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
+                                  const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream) {
+    if (rows < 0 || in_f <= 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_noalloc: bad shape");
+    if (in_f > 65536) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv_noalloc: in_f > 65536");
+    if (batch < 1 || batch > 8)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv_noalloc: batch must be 1..8 (got %lld)", (long long)batch);
+    if (rows == 0) return BF16X_OK;
+    const int64_t n_tiles = (rows + kTileRows - 1) / kTileRows;
+    if (n_tiles > kNoAllocMaxTiles)
+        return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv_noalloc: rows %lld exceed the fixed scratch limit of %lld",
+                         (long long)rows, (long long)(kNoAllocMaxTiles * kTileRows));
+    const int64_t need = scratch_need(plan_gemv(rows, in_f, warps_for(batch, rows, in_f)));
+    if (need > kNoAllocPartialBytes)
+        return set_error(BF16X_ERR_UNSUPPORTED,
+                         "bf16x_gemv_noalloc: %lld bytes of partial sums needed, fixed scratch holds %lld",
+                         (long long)need, (long long)kNoAllocPartialBytes);
+    void *base = nullptr;
+    if (int rc = noalloc_scratch(&base)) return rc;
+    // The counters must be zero at launch; a call that failed part-way could
+    // have left some set, so clear this call's range every time.
+    int32_t *counters = static_cast<int32_t *>(base);
+    cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)n_tiles * 4, (cudaStream_t)stream);
+    if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv_noalloc: clearing counters: %s", cudaGetErrorString(e));
+    return bf16x_gemv(layout, ptile_off, precs, rows, in_f, x, batch, ldx, bias, y, y_dtype, ldy, counters,
+                      static_cast<unsigned char *>(base) + kNoAllocCounterBytes, kNoAllocPartialBytes, stream);
+}

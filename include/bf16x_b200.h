@@ -143,6 +143,26 @@ int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *
                const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
                int32_t *tile_counters, void *scratch, int64_t scratch_bytes, void *stream);
 
+/* No counterpart in the reference.  bf16x_gemv without caller-supplied
+ * device memory, for callers that cannot allocate: a plain C host or FFI
+ * binding with no device allocator of its own, or a serving loop that must
+ * not call cudaMalloc/cudaFree (which synchronise the device) once running.
+ * Same arguments, results and limits as bf16x_gemv otherwise; nothing is
+ * allocated.  The tile counters and partial sums live in one fixed device
+ * array of this library (2 MiB of partial sums + 128 KiB of counters per
+ * device), so rows <= bf16x_gemv_noalloc_max_rows() (524288); larger requests
+ * fail with BF16X_ERR_UNSUPPORTED.  Each call clears its counters on
+ * `stream` before the launch.  The first call on a device looks up that
+ * array's address (cudaGetSymbolAddress), so make it before any stream
+ * capture.  All calls on a device share the one array: calls that can
+ * overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller. */
+int64_t bf16x_gemv_noalloc_max_rows(void);
+int bf16x_gemv_noalloc(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                       int64_t rows, int64_t in_f,
+                       const uint16_t *x, int64_t batch, int64_t ldx,
+                       const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream);
+
 /* ---- fused decode + GEMM (tcgen05, prefill) ----------------------------- */
 /* Replaces bf16x_fused_gemm / _bf16x_gemm_fused_kernel
  * (bf16x_gemm_fused.py:31-114): y[m][n] = sum_k x[m][k] * W[n][k] (+ bias[n])
