@@ -56,7 +56,20 @@ def parse_args():
     ap.add_argument("--mode", choices=["gemv", "gemm"], default="gemv",
                     help="gemv: decode+GEMV sweep (the headline); gemm: decode+GEMM prefill TFLOPS")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens M for --mode gemm")
+    ap.add_argument("--format", choices=["flat", "gguf", "gguf-lossless"], default="flat",
+                    help="weight source: the bf16x_quantize dict (flat), the 11.5-bpw GGUF blocks "
+                         "(zero marker, lossy) or GGUF blocks + side table (exact)")
     return ap.parse_args()
+
+
+def make_resident(w, fmt, dev):
+    """The fused kernels' resident weight built from `w` through the chosen format."""
+    from bfloat16x_b200.opqk_linear import bf16x_quantize
+    from bfloat16x_b200.resident import ResidentWeight
+    if fmt == "flat":
+        return ResidentWeight.from_packed(bf16x_quantize(w, device=dev), device=dev)
+    from bfloat16x_b200.bf16x_gguf_block import GgufWeight
+    return GgufWeight.from_float(w, lossless=(fmt == "gguf-lossless")).resident()
 
 
 def shapes_of(args):
@@ -265,9 +278,7 @@ def run_ours(args):
             base = out_f // world
             rows = base + (out_f % world if rank == world - 1 else 0)
         w = synthetic_weight(rows, in_f, seed=1000 * si + rank, device=dev)
-        p = bf16x_quantize(w, device=dev)
-        rw = ResidentWeight.from_packed(p, device=dev)
-        del p
+        rw = make_resident(w, args.format, dev)
         wb = None if args.no_cublas else w
         del w
         x = synthetic_activation(B, in_f, seed=si + 1, device=dev)
@@ -428,7 +439,7 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights with 0.5% x 2^U{4..8} outliers, bf16 N(0,1) activations)",
-            "config": {"workload": workload_name(args, shapes), "batch": B,
+            "config": {"workload": workload_name(args, shapes), "batch": B, "format": args.format,
                        "parallelism": f"row-shard x{world} ({args.scaling})",
                        "l2": "inputs larger than L2 (%.0f MB of weights per step per GPU)" % (step_bytes / 1e6),
                        "resident_bpw": round(8 * sum(L['rw'].nbytes() for L in layers) /
@@ -477,7 +488,7 @@ def run_gemm(args):
     for si, (out_f, in_f) in enumerate(shapes):
         rows = out_f if args.scaling == "weak" else out_f // world + (out_f % world if rank == world - 1 else 0)
         w = synthetic_weight(rows, in_f, seed=1000 * si + rank, device=dev)
-        rw = ResidentWeight.from_packed(bf16x_quantize(w, device=dev), device=dev)
+        rw = make_resident(w, args.format, dev)
         x = synthetic_activation(M, in_f, seed=si + 1, device=dev)
         y = torch.empty((M, rows), dtype=torch.bfloat16, device=dev)
         layers.append(dict(rw=rw, x=x, y=y, w=None if args.no_cublas else w, rows=rows, in_f=in_f))
@@ -550,7 +561,8 @@ def run_gemm(args):
             "warmup": args.warmup, "ms_per_step": round(el / args.steps, 4), "higher_is_better": True,
             "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "configs[2] fused decode+GEMM prefill: " + ", ".join(f"{o}x{i}" for o, i in shapes)
-                                   + f" at M={M} tokens", "tokens": M, "l2": "inputs larger than L2"},
+                                   + f" at M={M} tokens", "tokens": M, "format": args.format,
+                       "l2": "inputs larger than L2"},
             "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per_layer[i], 4) for i, L in enumerate(layers)},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(ach / peak_tf, 4), "peak_source": peak_kind,

@@ -16,6 +16,7 @@ LIB_PATH = os.environ.get("BF16X_LIB") or os.path.join(_HERE, "libbf16x_b200.so"
 
 BF16X_DTYPE_BF16 = 0
 BF16X_DTYPE_F32 = 1
+BF16X_DTYPE_F32_TRUNC = 2
 CHUNK_ELEMS = 256
 CHUNK_BYTES = 368
 TILE_ROWS = 16
@@ -47,6 +48,11 @@ _SIGS = {
     "bf16x_gemv": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p, _p, _i64, _p]),
     "bf16x_gemv_noalloc_max_rows": (_i64, []),
     "bf16x_gemv_noalloc": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p]),
+    "bf16x_gguf_quantize": (_i32, [_p, _i32, _i64, _p, _p]),
+    "bf16x_gguf_dequantize": (_i32, [_p, _i64, _p, _i32, _p]),
+    "bf16x_gguf_ovf_count": (_i32, [_p, _i32, _i64, _i64, _p, _p]),
+    "bf16x_gguf_ovf_pack": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _p]),
+    "bf16x_gguf_apply_ovf": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _p]),
     "bf16x_gemm": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p]),
 }
 

@@ -65,20 +65,22 @@ __device__ __forceinline__ int64_t warp_lower_bound(const int32_t *idx, int64_t 
     return lo + __popc(m);
 }
 
-// Exact bf16 bits of flat element pos, with the reference's decode semantics
-// (opqk_linear.py:364-376): a saturated stream delta (7) takes the table value
-// at lower_bound(idx, pos) (clamped to the last entry); the row's slice
-// [lo, hi) of the table is searched, which equals the global search for a
-// position inside that row.  exponent = (emax - d) & 0xFF.
+// Exact bf16 bits of flat element pos: a saturated stream delta (7) takes the
+// true delta of the table entry AT pos, and stays 7 when the table has none.
+// For the complete tables bf16x_quantize writes (every stream 7 listed) this
+// is the reference decode (opqk_linear.py:364-376, whose searchsorted always
+// lands on pos); for the filtered tables of the reference's GPU paths (only
+// delta > 7 kept, bf16x_triton_test.py:96, bf16x_fused.py:168-170) it is their
+// exact-position fix.  The row's slice [lo, hi) of the table is searched.
+// exponent = (emax - d) & 0xFF.
 __device__ __forceinline__ uint32_t flat_exact_bits(const FlatStreams &f, int64_t pos,
                                                     int64_t lo, int64_t hi, int sub) {
     const uint32_t m = flat_field(f.mant, f.n_mant, pos, 7);
     uint32_t d = flat_field(f.delta, f.n_delta, pos, 3);
     const uint32_t s = flat_field(f.sign, f.n_sign, pos, 1);
-    if (d == 7u && f.n_ovf > 0) {
-        int64_t loc = lower_bound_dev(f.ovf_idx, lo, hi, pos);
-        if (loc > f.n_ovf - 1) loc = f.n_ovf - 1;
-        d = __ldg(f.ovf_val + loc);
+    if (d == 7u && hi > lo) {
+        const int64_t loc = lower_bound_dev(f.ovf_idx, lo, hi, pos);
+        if (loc < hi && (int64_t)__ldg(f.ovf_idx + loc) == pos) d = __ldg(f.ovf_val + loc);
     }
     const int64_t ei = pos / sub;
     const uint32_t e = ei < f.n_emax ? __ldg(f.emax + ei) : 0u;

@@ -23,8 +23,10 @@
  *                    ([256 B sign|mant bytes][96 B pair-aligned deltas][16 B emax]),
  *                    i.e. the same 11.5 bits per weight, plus one patch record
  *                    per (16-row tile, 256-column chunk) for the weights whose
- *                    exact exponent delta exceeds 7 (u32 entries:
- *                    col_in_chunk | row_in_tile << 8 | delta << 16 | sign_mant << 24).
+ *                    exact exponent delta exceeds 7: two header words of
+ *                    per-quarter entry counts, then u32 entries
+ *                    mma-fragment slot (11 b) | column half << 11 | exact bf16 << 16,
+ *                    sorted by (64-column quarter, row, column).
  *   GGUF blocks    : 46-byte blocks of 32 weights (bf16x_gguf_block.py:6-17).
  */
 #ifndef BF16X_B200_H
@@ -44,6 +46,9 @@ extern "C" {
 
 #define BF16X_DTYPE_BF16 0
 #define BF16X_DTYPE_F32  1
+/* float32 input whose values are bf16-exact: the high half is taken as is
+ * (the reference's bf16_exact=True, bf16x_gguf_block.py:115-120) */
+#define BF16X_DTYPE_F32_TRUNC 2
 
 #define BF16X_CHUNK_ELEMS 256
 #define BF16X_CHUNK_BYTES 368
@@ -176,6 +181,31 @@ int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *
                int64_t rows, int64_t in_f,
                const uint16_t *x, int64_t M, int64_t ldx,
                const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream);
+
+/* ---- GGUF BF16X block format (llama.cpp GGML_TYPE_BF16X) --------------- */
+/* 32 weights per 46-byte block: emax[2] (per 16-weight half, floored at 7),
+ * sign[4], mant[28], delta[12]; delta 7 is the zero marker.  x_dtype:
+ * BF16X_DTYPE_BF16 (bf16 bits), BF16X_DTYPE_F32 (rounded to nearest even,
+ * NaNs quieted, as bf16x_gguf_block.py:45-50) or BF16X_DTYPE_F32_TRUNC.
+ * Replaces quantize_blocks (bf16x_gguf_block.py:64-81): n % 32 == 0,
+ * blocks: n/32 x 46 bytes, 4-byte aligned. */
+int bf16x_gguf_quantize(const void *x, int x_dtype, int64_t n, uint8_t *blocks, void *stream);
+/* Replaces dequantize_blocks (bf16x_gguf_block.py:84-95): y gets
+ * nblocks*32 values, bf16 bits or float32 (y_dtype). */
+int bf16x_gguf_dequantize(const uint8_t *blocks, int64_t nblocks, void *y, int y_dtype, void *stream);
+/* Lossless side table, replaces pack_ovf (bf16x_gguf_block.py:143-161) in two
+ * steps.  bf16x_gguf_ovf_count writes row_off[0..rows] (rows+1 uint32): entry
+ * offsets per row, row_off[rows] = number of entries (cols % 32 == 0, cols <=
+ * 65536).  bf16x_gguf_ovf_pack then writes the entries: column (u16) and
+ * exact bf16 bits (u16), sorted by row then column. */
+int bf16x_gguf_ovf_count(const void *x, int x_dtype, int64_t rows, int64_t cols, uint32_t *row_off,
+                         void *stream);
+int bf16x_gguf_ovf_pack(const void *x, int x_dtype, int64_t rows, int64_t cols, const uint32_t *row_off,
+                        uint16_t *ecols, uint16_t *ebits, void *stream);
+/* Replaces apply_ovf (bf16x_gguf_block.py:174-181): writes each entry's
+ * exact value into y [rows][cols] (bf16 bits or float32). */
+int bf16x_gguf_apply_ovf(void *y, int y_dtype, int64_t rows, int64_t cols, const uint32_t *row_off,
+                         const uint16_t *ecols, const uint16_t *ebits, int64_t n_entries, void *stream);
 
 #ifdef __cplusplus
 }

@@ -132,3 +132,15 @@ def test_bench_byte_count_matches_stored_weight(shape):
     p = oracle_dict(w)
     rw = ResidentWeight.from_packed(p, device="cuda")
     assert bench.stored_weight_bytes(p, *shape) == rw.nbytes()
+
+
+def test_repack_filtered_table():
+    # tables holding only the delta > 7 entries (the reference's GPU paths
+    # filter them so) repack to the same exact weights
+    w = bits_of(synthetic_weight(257, 320, seed=3))
+    p = oracle_dict(w)
+    keep = p["delta_ovf_val"] > 7
+    p["delta_ovf_idx"], p["delta_ovf_val"] = p["delta_ovf_idx"][keep], p["delta_ovf_val"][keep]
+    rw = ResidentWeight.from_packed(p, device="cuda")
+    assert np.array_equal(bits_of(rw.decode()), w)
+    _lib.check_device_status()

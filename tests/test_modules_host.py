@@ -1,0 +1,57 @@
+"""Host-side logic of the drop-in modules (no GPU): the per-row overflow CSR
+that the reference's Bf16xFused builds (bf16x_fused.py:165-179) converts back
+to the flat overflow table the kernels read."""
+import numpy as np
+import torch
+
+from bfloat16x_b200.bf16x_fused import csr_to_table
+from tests.gpu_util import load_flat, oracle_dict
+from bfloat16x_b200.synthetic import synthetic_weight
+from tests.gpu_util import bits_of
+
+
+def reference_csr(ovf_idx, ovf_val, out_f, in_f):
+    """The reference's CSR build, restated: keep true delta > 7, sort by row
+    (stable), column and delta per entry, row offsets."""
+    idx = torch.as_tensor(np.asarray(ovf_idx)).to(torch.int64)
+    val = torch.as_tensor(np.asarray(ovf_val)).to(torch.int64)
+    keep = val > 7
+    idx, val = idx[keep], val[keep]
+    rows = idx // in_f
+    k = idx % in_f
+    order = torch.argsort(rows, stable=True)
+    rows, k, val = rows[order], k[order], val[order]
+    counts = torch.bincount(rows, minlength=out_f)
+    offs = torch.zeros(out_f + 1, dtype=torch.int32)
+    offs[1:] = counts.cumsum(0).to(torch.int32)
+    return k.to(torch.int32), val.to(torch.int32), offs
+
+
+def test_csr_to_table_roundtrip_golden():
+    flat = load_flat()
+    for case in flat["cases"]:
+        w = flat[f"{case}/w"]
+        out_f, in_f = w.shape
+        oi, ov = flat[f"{case}/delta_ovf_idx"], flat[f"{case}/delta_ovf_val"]
+        olk, old, oloff = reference_csr(oi, ov, out_f, in_f)
+        ti, tv = csr_to_table(olk, old, oloff, in_f)
+        keep = ov > 7
+        assert np.array_equal(ti.numpy(), oi[keep].astype(np.int32))
+        assert np.array_equal(tv.numpy(), ov[keep].astype(np.uint8))
+
+
+def test_csr_to_table_synthetic():
+    wb = bits_of(synthetic_weight(300, 1000, seed=5))
+    p = oracle_dict(wb)
+    olk, old, oloff = reference_csr(p["delta_ovf_idx"], p["delta_ovf_val"], 300, 1000)
+    ti, tv = csr_to_table(olk, old, oloff, 1000)
+    keep = p["delta_ovf_val"].numpy() > 7
+    assert np.array_equal(ti.numpy(), p["delta_ovf_idx"].numpy()[keep])
+    assert np.array_equal(tv.numpy(), p["delta_ovf_val"].numpy()[keep])
+    assert ti.numel() > 0
+
+
+def test_empty_csr():
+    ti, tv = csr_to_table(torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
+                          torch.zeros(5, dtype=torch.int32), 64)
+    assert ti.numel() == 0 and tv.numel() == 0
