@@ -119,7 +119,7 @@ __device__ __forceinline__ uint32_t shl_signed(uint32_t v) {
 // ------------------------------------------------------- tensor-map copies
 namespace bf16x {
 
-// Tiled TMA loads (no multicast) into shared memory, completion counted on an
+// Tiled TMA loads into this CTA's shared memory, completion counted on an
 // mbarrier.  `map` is the address of a __grid_constant__ kernel parameter.
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int c0, int c1, uint64_t *bar) {
     asm volatile(
