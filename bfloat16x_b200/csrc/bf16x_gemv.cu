@@ -191,12 +191,17 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         ++i_it;
         if (++i_c == p.nch) { i_c = 0; ++i_tile; }
     };
-    for (int s = 0; s < S && i_it < hi; ++s) {
-        load_rec();
-        issue(i_tile, i_c, s, nxt_off, nxt_end);
-        advance_issue();
+    {
+        // record offsets of the first S items and of the one after: one load
+        // per lane, so their latencies overlap
+        const int32_t v = (lane <= S + 1 && lo + lane <= p.T) ? __ldg(p.ptile_off + lo + lane) : 0;
+        for (int s = 0; s < S && i_it < hi; ++s) {
+            issue(i_tile, i_c, s, __shfl_sync(0xffffffffu, v, s), __shfl_sync(0xffffffffu, v, s + 1));
+            advance_issue();
+        }
+        nxt_off = __shfl_sync(0xffffffffu, v, S);
+        nxt_end = __shfl_sync(0xffffffffu, v, S + 1);
     }
-    load_rec();
 
     const int g = lane >> 2, t = lane & 3;
     float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
@@ -215,6 +220,16 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         {
             const uint32_t *rec = reinterpret_cast<const uint32_t *>(slot + C::kPOff);
             const uint32_t hdr = rec[0];
+            // lane j holds record entries j, 32+j, 64+j, 96+j (zero past the end)
+            uint32_t pe[4];
+            {
+                const int n_all = (int)(hdr >> 16);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int j = 32 * k + lane;
+                    pe[k] = j < n_all ? rec[kRecHdrWords + j] : 0u;   // j < 128 <= staged capacity
+                }
+            }
             const uint8_t *rowA = slot + g * kChunkBytes;
             const uint8_t *rowB = rowA + 8 * kChunkBytes;
             const uint16_t *xg = g < BMAX ? xs + g * kChunkElems : zero_x;
@@ -237,7 +252,12 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                     const int jlo = h ? (int)(hdr & 0xFFFFu) : 0;
                     const int jhi = h ? (int)(hdr >> 16) : (int)(hdr & 0xFFFFu);
                     uint16_t *frag16 = reinterpret_cast<uint16_t *>(frag);
-                    for (int j = jlo + lane; j < jhi; j += 32) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int j = 32 * k + lane;
+                        if (j >= jlo && j < jhi) frag16[pe[k] & 0x7FFu] = (uint16_t)(pe[k] >> 16);
+                    }
+                    for (int j = (jlo > 128 ? jlo : 128) + lane; j < jhi; j += 32) {   // records past 128 entries
                         const uint32_t ent = (kRecHdrWords + j < kPcapWords)
                                                  ? rec[kRecHdrWords + j]
                                                  : __ldg(p.precs + rec_of[s] + kRecHdrWords + j);
@@ -272,8 +292,9 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
 
         // ---- refill this slot S items ahead
         __syncwarp();
+        // the slot was only read with ordinary loads, which have completed
+        // (their values are consumed), so the bulk copies may overwrite it
         if (i_it < hi) {
-            fence_proxy_async_smem();
             issue(i_tile, i_c, s, nxt_off, nxt_end);
             advance_issue();
             load_rec();
@@ -314,15 +335,36 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     __threadfence();
+                    // pieces in warp order: w_first's is in its slot 1 when its
+                    // range began in an earlier tile; every later warp's range
+                    // begins in this tile, so theirs are in slot 0
+                    const int sl_first = item_lo(w_first, p.T, p.W) < tile * p.nch ? 1 : 0;
+                    float o4[4];
+                    {
+                        const float *src = p.partials + (w_first * 2 + sl_first) * 128 + lane;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) o4[k] = __ldcg(src + 32 * k);
+                    }
+                    int64_t w2 = w_first + 1;
+                    for (; w2 + 1 <= w_last; w2 += 2) {
+                        const float *a = p.partials + (w2 * 2) * 128 + lane;
+                        const float *b2 = a + 2 * 128;
+                        float va[4], vb[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) { va[k] = __ldcg(a + 32 * k); vb[k] = __ldcg(b2 + 32 * k); }
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) { o4[k] += va[k]; o4[k] += vb[k]; }
+                    }
+                    if (w2 <= w_last) {
+                        const float *a = p.partials + (w2 * 2) * 128 + lane;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) o4[k] += __ldcg(a + 32 * k);
+                    }
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const int idx = lane + 32 * k;
                         const int rr = idx >> 3, b = idx & 7;
-                        float o = 0.f;
-                        for (int64_t w2 = w_first; w2 <= w_last; ++w2) {
-                            const int sl2 = (tile == item_lo(w2, p.T, p.W) / p.nch) ? 0 : 1;
-                            o += __ldcg(p.partials + (w2 * 2 + sl2) * 128 + idx);
-                        }
+                        float o = o4[k];
                         const int64_t row = row0 + rr;
                         if (b < p.batch && row < p.rows) {
                             if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
