@@ -55,6 +55,25 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// Raise the barrier's expected transaction bytes without arriving (the
+// arrival comes later, with the rest of the phase's copies).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;"
+                 :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// Programmatic dependent launch.  launch_dependents lets the next kernel of
+// the stream (launched with programmatic stream serialization) be scheduled
+// as this grid's CTAs retire; wait blocks until the previous kernel of the
+// stream has completed and its writes are visible.  Without a dependent
+// launch both are no-ops.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // try_wait with a suspend-time hint: a waiting warp sleeps (up to the hint)
 // instead of spinning, so it does not take issue slots from working warps.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {

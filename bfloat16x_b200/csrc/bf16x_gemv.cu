@@ -24,6 +24,9 @@
 //   * a tile split between warps is finished by whichever warp arrives last
 //     (an atomic counter per tile in the workspace), summing the pieces in a
 //     fixed order, so results are deterministic and no warp ever waits;
+//   * launched with programmatic stream serialization: the next GEMV of a
+//     stream (the next layer) starts on the SMs this one frees and requests
+//     its weights before it waits for this kernel to complete;
 //   * every mbarrier wait is bounded (bf16x_common.cuh) and reports a timeout
 //     through the device status word instead of hanging.
 #include <algorithm>
@@ -149,6 +152,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
     __syncthreads();
+    griddep_launch_dependents();
 
     const int64_t gw = (int64_t)blockIdx.x * C::kWarps + warp;
     if (gw >= p.W) return;
@@ -192,11 +196,33 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         if (++i_c == p.nch) { i_c = 0; ++i_tile; }
     };
     {
-        // record offsets of the first S items and of the one after: one load
-        // per lane, so their latencies overlap
+        // First S items.  Everything read from the weight (rows, records,
+        // record offsets) is requested before griddep_wait, so it overlaps
+        // the end of the previous kernel of the stream; the activations, the
+        // outputs and the scratch are touched only after it.  Each slot's
+        // expected bytes are raised without arriving; the activation copy's
+        // arrival completes the phase.
         const int32_t v = (lane <= S + 1 && lo + lane <= p.T) ? __ldg(p.ptile_off + lo + lane) : 0;
+        int64_t tl = i_tile;
+        int cc = i_c;
+        for (int s = 0; s < S && lo + s < hi; ++s) {
+            const int32_t r_off = __shfl_sync(0xffffffffu, v, s), r_end = __shfl_sync(0xffffffffu, v, s + 1);
+            if (lane == 0) {
+                uint8_t *slot = wsm + s * C::kSlot;
+                const int staged = min(r_end - r_off, kPcapWords);
+                rec_of[s] = r_off;
+                mbar_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
+                tma_load_3d(slot, &p.wmap, 0, cc, (int)(tl * kTileRows), &bars[s]);
+                bulk_g2s(slot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
+            }
+            if (++cc == p.nch) { cc = 0; ++tl; }
+        }
+        griddep_wait();
         for (int s = 0; s < S && i_it < hi; ++s) {
-            issue(i_tile, i_c, s, __shfl_sync(0xffffffffu, v, s), __shfl_sync(0xffffffffu, v, s + 1));
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&bars[s], (uint32_t)(BMAX * kXRowBytes));
+                tma_load_2d(wsm + s * C::kSlot + C::kXOff, &p.xmap, i_c * kChunkElems, 0, &bars[s]);
+            }
             advance_issue();
         }
         nxt_off = __shfl_sync(0xffffffffu, v, S);
@@ -210,6 +236,56 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
     int tile_c0 = c;                                // first chunk of the current tile in this range
     int s = 0;
     uint32_t parity = 0;
+
+    // Split tiles: every piece's warp publishes its partial sums and counts
+    // itself on the tile's counter; the warp that brings the count to the
+    // number of pieces sums them in warp order (deterministic) and writes y.
+    auto pieces_before = [&](int64_t tl) -> int {
+        return (int)(item_owner(tl * p.nch + p.nch - 1, p.T, p.W) - item_owner(tl * p.nch, p.T, p.W));
+    };
+    auto reduce_split = [&](int64_t tl) {
+        __threadfence();
+        const int64_t w_first = item_owner(tl * p.nch, p.T, p.W);
+        const int64_t w_last = item_owner(tl * p.nch + p.nch - 1, p.T, p.W);
+        // w_first's piece is in its slot 1 when its range began in an earlier
+        // tile; every later warp's range begins in this tile: slot 0
+        const int sl_first = item_lo(w_first, p.T, p.W) < tl * p.nch ? 1 : 0;
+        float o4[4];
+        {
+            const float *src = p.partials + (w_first * 2 + sl_first) * 128 + lane;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o4[k] = __ldcg(src + 32 * k);
+        }
+        int64_t w2 = w_first + 1;
+        for (; w2 + 1 <= w_last; w2 += 2) {
+            const float *a = p.partials + (w2 * 2) * 128 + lane;
+            const float *b2 = a + 2 * 128;
+            float va[4], vb[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) { va[k] = __ldcg(a + 32 * k); vb[k] = __ldcg(b2 + 32 * k); }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) { o4[k] += va[k]; o4[k] += vb[k]; }
+        }
+        if (w2 <= w_last) {
+            const float *a = p.partials + (w2 * 2) * 128 + lane;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o4[k] += __ldcg(a + 32 * k);
+        }
+        const int64_t row0 = tl * kTileRows;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int idx = lane + 32 * k;
+            const int rr = idx >> 3, b = idx & 7;
+            float o = o4[k];
+            const int64_t row = row0 + rr;
+            if (b < p.batch && row < p.rows) {
+                if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
+                if (p.y_f32) reinterpret_cast<float *>(p.y)[b * p.ldy + row] = o;
+                else reinterpret_cast<uint16_t *>(p.y)[b * p.ldy + row] = f32_to_bf16_bits_rn(o);
+            }
+        }
+        if (lane == 0) p.tile_cnt[tl] = 0;
+    };
 
     for (int64_t it = lo; it < hi; ++it) {
         if (!mbar_wait(&bars[s], parity, &g_status)) return;
@@ -328,52 +404,9 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                 mine[(g + 8) * 8 + 2 * t + 1] = c3;
                 __threadfence();
                 __syncwarp();
-                const int64_t w_first = item_owner(tile * p.nch, p.T, p.W);
-                const int64_t w_last = item_owner(tile * p.nch + p.nch - 1, p.T, p.W);
-                int last = 0;
-                if (lane == 0) last = atomicAdd(p.tile_cnt + tile, 1) == (int)(w_last - w_first);
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    __threadfence();
-                    // pieces in warp order: w_first's is in its slot 1 when its
-                    // range began in an earlier tile; every later warp's range
-                    // begins in this tile, so theirs are in slot 0
-                    const int sl_first = item_lo(w_first, p.T, p.W) < tile * p.nch ? 1 : 0;
-                    float o4[4];
-                    {
-                        const float *src = p.partials + (w_first * 2 + sl_first) * 128 + lane;
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) o4[k] = __ldcg(src + 32 * k);
-                    }
-                    int64_t w2 = w_first + 1;
-                    for (; w2 + 1 <= w_last; w2 += 2) {
-                        const float *a = p.partials + (w2 * 2) * 128 + lane;
-                        const float *b2 = a + 2 * 128;
-                        float va[4], vb[4];
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) { va[k] = __ldcg(a + 32 * k); vb[k] = __ldcg(b2 + 32 * k); }
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) { o4[k] += va[k]; o4[k] += vb[k]; }
-                    }
-                    if (w2 <= w_last) {
-                        const float *a = p.partials + (w2 * 2) * 128 + lane;
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) o4[k] += __ldcg(a + 32 * k);
-                    }
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int idx = lane + 32 * k;
-                        const int rr = idx >> 3, b = idx & 7;
-                        float o = o4[k];
-                        const int64_t row = row0 + rr;
-                        if (b < p.batch && row < p.rows) {
-                            if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
-                            if (p.y_f32) reinterpret_cast<float *>(p.y)[b * p.ldy + row] = o;
-                            else reinterpret_cast<uint16_t *>(p.y)[b * p.ldy + row] = f32_to_bf16_bits_rn(o);
-                        }
-                    }
-                    if (lane == 0) p.tile_cnt[tile] = 0;
-                }
+                int old = 0;
+                if (lane == 0) old = atomicAdd(p.tile_cnt + tile, 1);
+                if (__shfl_sync(0xffffffffu, old, 0) == pieces_before(tile)) reduce_split(tile);
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) ce[k] = co[k] = 0.f;
@@ -484,7 +517,20 @@ static int launch_gemv(const GemvParams &p, const GemvLaunch &L, cudaStream_t st
         if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: smem attribute: %s", cudaGetErrorString(e));
         attr_set[dev] = true;
     }
-    gemv_kernel<BMAX, NW><<<L.grid, C::kWarps * 32, C::kSmem, st>>>(p);
+    // programmatic stream serialization: this launch may begin while the
+    // previous kernel of the stream finishes (see griddep_wait in the kernel)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)L.grid);
+    cfg.blockDim = dim3((unsigned)(C::kWarps * 32));
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<BMAX, NW>, p);
+    if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: launch: %s", cudaGetErrorString(e));
     return check_launch("bf16x_gemv");
 }
 
