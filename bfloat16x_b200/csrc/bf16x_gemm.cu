@@ -145,13 +145,26 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
     return row * 128u + ((((col >> 3) ^ row) & 7u) << 4) + ((col & 7u) << 1);
 }
 
-// Bounded wait used by every role; on timeout (or if another role already
-// gave up) the abort flag is raised and false is returned.
+// Bounded wait used by every role; on timeout the abort flag is raised and
+// false is returned, and a role that finds the flag raised while waiting
+// gives up too.
+// The fast path (phase already complete) reads nothing else: the abort flag
+// is a shared-memory load, and on the MMA issuer's path one such load per
+// wait measurably slows the issue of the k-blocks.  It is checked while
+// waiting instead.
 __device__ __forceinline__ bool role_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    if (*abort_flag) return false;
-    if (mbar_wait(bar, parity, &g_status)) return true;
-    *abort_flag = 1;
-    return false;
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (*abort_flag) return false;
+        if (mbar_try_wait(a, parity)) return true;
+        if ((i & 7u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_status, kErrWaitTimeout);
+            *abort_flag = 1;
+            return false;
+        }
+    }
 }
 
 template <int BN>
@@ -318,6 +331,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 const uint8_t *wst = smem + C::kWOff + wslot * kGemmWStage;
                 const uint32_t *rec = reinterpret_cast<const uint32_t *>(smem + C::kROff + wslot * C::kRecStage) +
                                       (d % kSubsPerStage) * kGemmRecCap;
+                // this warp's patch entries for its two quarters of the chunk
+                // (k-blocks dg and dg+2): lane j holds entries j and 32+j of
+                // each, read from the staged record once the chunk has landed
+                int qlo[2] = {0, 0}, qn[2] = {0, 0};
+                uint32_t qe[2][2] = {{0u, 0u}, {0u, 0u}};
                 for (int kq = 0; kq < 4; ++kq) {
                     const bool mine = (kq & 1) == dg;
                     if (mine) {
@@ -328,6 +346,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                         }
                         w = __shfl_sync(0xffffffffu, w, 0);
                         if (!w) { ok = false; break; }
+                        if (kq == dg && has_rec) {
+                            // quarter boundaries 0 | n_q0 | n_low | n_q012 | n_all
+                            const uint32_t h0 = rec[0], h1 = rec[1];
+                            const int bq[5] = {0, (int)(h1 & 0xFFFFu), (int)(h0 & 0xFFFFu), (int)(h1 >> 16), (int)(h0 >> 16)};
+#pragma unroll
+                            for (int u = 0; u < 2; ++u) {
+                                const int q = dg + 2 * u;
+                                const int lo = q == 0 ? bq[0] : q == 1 ? bq[1] : q == 2 ? bq[2] : bq[3];
+                                const int hi = q == 0 ? bq[1] : q == 1 ? bq[2] : q == 2 ? bq[3] : bq[4];
+                                qlo[u] = lo;
+                                qn[u] = hi - lo;
+                                const int j0 = kRecHdrWords + lo + lane;
+                                qe[u][0] = (lane < qn[u] && j0 < kGemmRecCap) ? rec[j0] : 0u;
+                                qe[u][1] = (lane + 32 < qn[u] && j0 + 32 < kGemmRecCap) ? rec[j0 + 32] : 0u;
+                            }
+                        }
                         uint8_t *ast = smem + C::kAOff + as * C::kAStage;
                         {
                             // row `row`, columns 64*kq + 32*hh .. +31 of the chunk
@@ -344,21 +378,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                         }
                         __syncwarp();
                         if (has_rec) {
-                            // exact values of this sub-tile's patched weights in the k-block:
-                            // quarter boundaries 0 | n_q0 | n_low | n_q012 | n_all
-                            const uint32_t h0 = rec[0], h1 = rec[1];
-                            const int b1 = (int)(h1 & 0xFFFFu), b2 = (int)(h0 & 0xFFFFu), b3 = (int)(h1 >> 16);
-                            const int lo = kq == 0 ? 0 : kq == 1 ? b1 : kq == 2 ? b2 : b3;
-                            const int hi = kq == 0 ? b1 : kq == 1 ? b2 : kq == 2 ? b3 : (int)(h0 >> 16);
-                            for (int j = lo + lane; j < hi; j += 32) {
-                                const uint32_t ent = (kRecHdrWords + j < kGemmRecCap)
-                                                         ? rec[kRecHdrWords + j]
-                                                         : __ldg(p.precs + __ldg(p.ptile_off + ((int64_t)rt * 8 + d) * p.nch + c) +
-                                                                 kRecHdrWords + j);
+                            // exact values of this sub-tile's patched weights in the k-block
+                            const int u = kq == dg ? 0 : 1;
+                            const int n = u ? qn[1] : qn[0], lo = u ? qlo[1] : qlo[0];
+                            auto put = [&](uint32_t ent) {
                                 uint32_t rr, cc;
                                 frag_position(ent, rr, cc);
                                 *reinterpret_cast<uint16_t *>(ast + sw128_offset(16u * d + rr, cc & 63u)) =
                                     (uint16_t)(ent >> 16);
+                            };
+                            const int cap = kGemmRecCap - kRecHdrWords - lo;   // entries staged in shared memory
+                            if (lane < n && lane < cap) put(u ? qe[1][0] : qe[0][0]);
+                            if (lane + 32 < n && lane + 32 < cap) put(u ? qe[1][1] : qe[0][1]);
+                            if (n > 64 || cap < n) {
+                                // past the staged words or past 64 entries: from global memory
+                                const int32_t base = __ldg(p.ptile_off + ((int64_t)rt * 8 + d) * p.nch + c);
+                                for (int j = lane; j < n; j += 32)
+                                    if (j >= 64 || j >= cap) put(__ldg(p.precs + base + kRecHdrWords + lo + j));
                             }
                         }
                         fence_proxy_async_smem();
@@ -414,6 +450,423 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     }
 }
 
+
+// ------------------------------------------------ CTA-pair (cluster of 2) glue
+struct Gemm2Cfg {
+    static constexpr int kWStages = 2;
+    static constexpr int kAStages = 4;
+    static constexpr int kBStages = 3;
+    static constexpr int kAStage = kGemmBM * 128;     // 16 KB: 128 rows x 64 columns
+    static constexpr int kBStage = 128 * 128;         // 16 KB: this CTA's 128 tokens x 64 columns
+    static constexpr int kRecStage = kSubsPerStage * kGemmRecCap * 4;
+    static constexpr int kAOff = 0;
+    static constexpr int kBOff = kAOff + kAStages * kAStage;
+    static constexpr int kWOff = kBOff + kBStages * kBStage;
+    static constexpr int kROff = kWOff + kWStages * kGemmWStage;
+    static constexpr int kBarOff = kROff + kWStages * kRecStage;
+    static constexpr int kNumBars = 2 * kWStages + 3 * kAStages + 2 * kBStages + 4;
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+    static constexpr int kSmem = kMiscOff + 16 + 1024;
+    static constexpr int kTmemCols = 512;             // two 256-column accumulators
+    static_assert(kSmem <= 227 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+
+// Relaxed arrival on a barrier of another CTA of the cluster: the ordering
+// that matters is already established by the caller (see its use).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;"
+                 :: "r"(cluster_addr), "r"(bytes) : "memory");
+}
+
+// Tiled TMA load into this CTA's shared memory whose completion is counted
+// on a barrier of the leader CTA of the pair (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const void *map, int c0, int c1, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(bar_cluster) : "memory");
+}
+
+template <int M, int N>
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_m() {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// Arrive on the barrier at `bar_cluster` (this CTA's or the peer's) once the
+// pair's MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(bar_cluster) : "memory");
+}
+
+// All threads of both CTAs of the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The CTA pair version (cluster of 2, tcgen05 cta_group::2): a tile is 256
+// weight rows x 256 tokens; CTA r of the pair decodes rows 128r..128r+127
+// and stages tokens 128r..128r+127 of the activations, and the leader
+// (rank 0) issues M=256 x N=256 MMAs that read both CTAs' operands and write
+// each CTA's 128 accumulator rows into its own tensor memory.  Per SM the
+// activation traffic and its shared-memory ring are half those of the
+// single-CTA kernel, which leaves room for a deeper ring of decoded tiles.
+// All "full" barriers that the MMA waits on live in the leader; the MMA's
+// commits release the slots of both CTAs; the epilogues of both CTAs
+// release the leader's accumulator.
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_constant__ GemmParams p) {
+    using C = Gemm2Cfg;
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled operand slots
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
+    uint64_t *w_full = bars, *w_empty = w_full + C::kWStages;
+    uint64_t *a_full = w_empty + C::kWStages, *a_empty = a_full + C::kAStages;
+    uint64_t *b_full = a_empty + C::kAStages, *b_empty = b_full + C::kBStages;
+    uint64_t *acc_full = b_empty + C::kBStages, *acc_empty = acc_full + 2;
+    uint64_t *a_ready = acc_empty + 2;             // peer only: its decoders' local count per A slot
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kWStages; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], kGemmDecWarps / kWHalves); }
+        // a_full: the leader's 8 decoder warps + one forwarded arrival for the peer's 8
+        for (int s = 0; s < C::kAStages; ++s) { mbar_init(&a_full[s], 9); mbar_init(&a_empty[s], 1); mbar_init(&a_ready[s], 8); }
+        // b_full: the leader's arrival carries the bytes of both halves
+        for (int s = 0; s < C::kBStages; ++s) { mbar_init(&b_full[s], 1); mbar_init(&b_empty[s], 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 8); }
+        abort_flag[0] = 0;
+        abort_flag[1] = 0;
+        fence_mbar_init();
+    }
+    // barriers of both CTAs initialised before any crosses the pair
+    cluster_sync_all();
+    if (warp == 2) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(tmem_slot)), "r"(C::kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // the leader's barrier addresses, as seen from this CTA
+    auto leader = [&](uint64_t *bar) { return mapa_shared(smem_u32(bar), 0u); };
+    const uint32_t tmem_base = *tmem_slot;
+    const int nkb = p.nch * 4;                     // k-blocks per tile
+
+    if (warp == 0) {
+        // ------------------------------------------------------- W producer
+        // Stages are (tile, chunk, half) in order; the record offsets of the
+        // next stage are loaded while the current one is issued, so their
+        // global-memory latency stays off the critical path.
+        if (lane == 0) {
+            prefetch_tensormap(&p.wmap);
+            int ws = 0;
+            uint32_t wph = 0;
+            const int per_tile = p.nch * kWHalves;
+            int t = pair, c = 0, hf = 0;
+            int32_t off[kSubsPerStage], len[kSubsPerStage];
+            auto load_offsets = [&](int tt, int cc, int hh) {
+                const int rt = tt / p.tiles_n;
+#pragma unroll
+                for (int sub = 0; sub < kSubsPerStage; ++sub) {
+                    const int64_t t16 = (int64_t)rt * 16 + 8 * rank + kSubsPerStage * hh + sub;
+                    if (tt < p.tiles_total && t16 < p.n_tiles16) {
+                        const int64_t i = t16 * p.nch + cc;
+                        off[sub] = __ldg(p.ptile_off + i);
+                        len[sub] = __ldg(p.ptile_off + i + 1);
+                    } else {
+                        off[sub] = 0;
+                        len[sub] = 0;
+                    }
+                }
+            };
+            load_offsets(t, c, hf);
+            (void)per_tile;
+            while (t < p.tiles_total) {
+                int32_t o[kSubsPerStage], l[kSubsPerStage];
+                int total = 0;
+#pragma unroll
+                for (int sub = 0; sub < kSubsPerStage; ++sub) {
+                    o[sub] = off[sub];
+                    l[sub] = min(len[sub] - off[sub], kGemmRecCap);
+                    total += l[sub];
+                }
+                const int rt = t / p.tiles_n, cc = c, hh = hf;
+                // advance to the next stage and prefetch its offsets
+                if (++hf == kWHalves) { hf = 0; if (++c == p.nch) { c = 0; t += npairs; } }
+                load_offsets(t, c, hf);
+                if (!role_wait(&w_empty[ws], wph ^ 1u, abort_flag)) break;
+                mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(kGemmWStage + total * 4));
+                tma_load_3d(smem + C::kWOff + ws * kGemmWStage, &p.wmap, 0, cc,
+                            rt * 2 * kGemmBM + (int)rank * kGemmBM + kGemmWRows * hh, &w_full[ws]);
+                uint8_t *rec = smem + C::kROff + ws * C::kRecStage;
+#pragma unroll
+                for (int sub = 0; sub < kSubsPerStage; ++sub)
+                    if (l[sub] > 0)
+                        bulk_g2s(rec + sub * kGemmRecCap * 4, p.precs + o[sub], (uint32_t)l[sub] * 4, &w_full[ws]);
+                if (++ws == C::kWStages) { ws = 0; wph ^= 1u; }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- B producer
+        if (lane == 0) {
+            prefetch_tensormap(&p.xmap);
+            int bs = 0;
+            uint32_t bph = 0;
+            bool ok = true;
+            for (int t = pair; t < p.tiles_total && ok; t += npairs) {
+                const int nt = t % p.tiles_n;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!role_wait(&b_empty[bs], bph ^ 1u, abort_flag)) { ok = false; break; }
+                    // this CTA's half of the token tile, counted on the leader's barrier
+                    const uint32_t lb = leader(&b_full[bs]);
+                    if (rank == 0) mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(2 * C::kBStage));
+                    tma_load_2d_pair(smem + C::kBOff + bs * C::kBStage, &p.xmap, kb * kGemmBK,
+                                     nt * BN + (int)rank * (BN / 2), lb);
+                    if (++bs == C::kBStages) { bs = 0; bph ^= 1u; }
+                }
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16_m<2 * kGemmBM, BN>();
+            const uint32_t peer = 1u;
+            int as = 0, bs = 0, ac = 0;
+            uint32_t aph = 0, bph = 0, acph = 0;
+            bool ok = true;
+            for (int t = pair; t < p.tiles_total && ok; t += npairs) {
+                if (!role_wait(&acc_empty[ac], acph ^ 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(ac * BN);
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!role_wait(&a_full[as], aph, abort_flag) || !role_wait(&b_full[bs], bph, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = umma_desc_sw128(smem_u32(smem + C::kAOff + as * C::kAStage));
+                    const uint64_t bd = umma_desc_sw128(smem_u32(smem + C::kBOff + bs * C::kBStage));
+#pragma unroll
+                    for (int k16 = 0; k16 < kGemmBK / 16; ++k16)   // 32 bytes along K per step
+                        umma_bf16_pair(d_tmem, ad + 2u * k16, bd + 2u * k16, idesc, (kb | k16) != 0);
+                    umma_commit_pair(smem_u32(&a_empty[as]));
+                    umma_commit_pair(mapa_shared(smem_u32(&a_empty[as]), peer));
+                    umma_commit_pair(smem_u32(&b_empty[bs]));
+                    umma_commit_pair(mapa_shared(smem_u32(&b_empty[bs]), peer));
+                    if (++as == C::kAStages) { as = 0; aph ^= 1u; }
+                    if (++bs == C::kBStages) { bs = 0; bph ^= 1u; }
+                }
+                if (!ok) break;
+                umma_commit_pair(smem_u32(&acc_full[ac]));
+                umma_commit_pair(mapa_shared(smem_u32(&acc_full[ac]), peer));
+                if (++ac == 2) { ac = 0; acph ^= 1u; }
+            }
+        }
+        if (lane == 0 && rank == 1) {
+            // peer: forward each k-block's "A slot decoded" count to the leader
+            int as = 0;
+            uint32_t aph = 0;
+            bool ok = true;
+            for (int t = pair; t < p.tiles_total && ok; t += npairs) {
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!role_wait(&a_ready[as], aph, abort_flag)) { ok = false; break; }
+                    // the decoder warps fenced their tile for the async proxy before
+                    // their local arrival, which this thread has acquired
+                    mbar_arrive_cluster_relaxed(leader(&a_full[as]));
+                    if (++as == C::kAStages) { as = 0; aph ^= 1u; }
+                }
+            }
+        }
+    } else if (warp < 3 + kGemmDecWarps) {
+        // ------------------------------------------------------- decoders
+        // Two groups of 8 warps take alternate k-blocks, so two k-blocks are
+        // decoded at once.  Warp d of a group owns weight rows 16d..16d+15:
+        // two lanes per row (32 columns each of the 64-column k-block), and
+        // the patch record of that 16-row sub-tile, whose entries for the
+        // k-block are one contiguous range (records are sorted by 64-column
+        // quarter).  Everything a warp writes it also patches, so warps
+        // never wait for each other; each arrives on the MMA barrier on its
+        // own (count 8 per k-block, 16 per chunk for the W slot).
+        const int dg = (warp - 3) >> 3, d = (warp - 3) & 7;
+        const int hf = d / kSubsPerStage;              // which stage of the chunk holds my rows
+        const int lrow = 16 * (d % kSubsPerStage) + (lane >> 1);   // row inside that stage
+        const int row = 16 * d + (lane >> 1), hh = lane & 1;
+        int as = 0, wseq = 0;
+        uint32_t aph = 0;
+        bool ok = true;
+        for (int t = pair; t < p.tiles_total && ok; t += npairs) {
+            const int rt = t / p.tiles_n;
+            const int64_t t16 = (int64_t)rt * 16 + 8 * rank + d;     // this warp's 16-row sub-tile
+            const bool has_rec = t16 < p.n_tiles16;
+            for (int c = 0; c < p.nch && ok; ++c, wseq += kWHalves) {
+                const int wslot = (wseq + hf) % C::kWStages;
+                const uint32_t wpar = (uint32_t)(((wseq + hf) / C::kWStages) & 1);
+                const uint8_t *wst = smem + C::kWOff + wslot * kGemmWStage;
+                const uint32_t *rec = reinterpret_cast<const uint32_t *>(smem + C::kROff + wslot * C::kRecStage) +
+                                      (d % kSubsPerStage) * kGemmRecCap;
+                // this warp's patch entries for its two quarters of the chunk
+                // (k-blocks dg and dg+2): lane j holds entries j and 32+j of
+                // each, read from the staged record once the chunk has landed
+                int qlo[2] = {0, 0}, qn[2] = {0, 0};
+                uint32_t qe[2][2] = {{0u, 0u}, {0u, 0u}};
+                for (int kq = 0; kq < 4; ++kq) {
+                    const bool mine = (kq & 1) == dg;
+                    if (mine) {
+                        int w = 1;
+                        if (lane == 0) {
+                            if (kq == dg) w = role_wait(&w_full[wslot], wpar, abort_flag);
+                            w = w && role_wait(&a_empty[as], aph ^ 1u, abort_flag);
+                        }
+                        w = __shfl_sync(0xffffffffu, w, 0);
+                        if (!w) { ok = false; break; }
+                        if (kq == dg && has_rec) {
+                            // quarter boundaries 0 | n_q0 | n_low | n_q012 | n_all
+                            const uint32_t h0 = rec[0], h1 = rec[1];
+                            const int bq[5] = {0, (int)(h1 & 0xFFFFu), (int)(h0 & 0xFFFFu), (int)(h1 >> 16), (int)(h0 >> 16)};
+#pragma unroll
+                            for (int u = 0; u < 2; ++u) {
+                                const int q = dg + 2 * u;
+                                const int lo = q == 0 ? bq[0] : q == 1 ? bq[1] : q == 2 ? bq[2] : bq[3];
+                                const int hi = q == 0 ? bq[1] : q == 1 ? bq[2] : q == 2 ? bq[3] : bq[4];
+                                qlo[u] = lo;
+                                qn[u] = hi - lo;
+                                const int j0 = kRecHdrWords + lo + lane;
+                                qe[u][0] = (lane < qn[u] && j0 < kGemmRecCap) ? rec[j0] : 0u;
+                                qe[u][1] = (lane + 32 < qn[u] && j0 + 32 < kGemmRecCap) ? rec[j0 + 32] : 0u;
+                            }
+                        }
+                        uint8_t *ast = smem + C::kAOff + as * C::kAStage;
+                        {
+                            // row `row`, columns 64*kq + 32*hh .. +31 of the chunk
+                            uint32_t sm[8], dw[3], e2lo, e2hi;
+                            load_group(wst + lrow * kChunkBytes, 2 * kq + hh, sm, dw, e2lo, e2hi);
+                            GroupPairs gp;
+                            decode_pairs_from<0>(gp, sm, dw, e2lo, e2hi);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t col = 32u * hh + 8u * i;
+                                *reinterpret_cast<uint4 *>(ast + sw128_offset((uint32_t)row, col)) =
+                                    make_uint4(gp.w[4 * i], gp.w[4 * i + 1], gp.w[4 * i + 2], gp.w[4 * i + 3]);
+                            }
+                        }
+                        __syncwarp();
+                        if (has_rec) {
+                            // exact values of this sub-tile's patched weights in the k-block
+                            const int u = kq == dg ? 0 : 1;
+                            const int n = u ? qn[1] : qn[0], lo = u ? qlo[1] : qlo[0];
+                            auto put = [&](uint32_t ent) {
+                                uint32_t rr, cc;
+                                frag_position(ent, rr, cc);
+                                *reinterpret_cast<uint16_t *>(ast + sw128_offset(16u * d + rr, cc & 63u)) =
+                                    (uint16_t)(ent >> 16);
+                            };
+                            const int cap = kGemmRecCap - kRecHdrWords - lo;   // entries staged in shared memory
+                            if (lane < n && lane < cap) put(u ? qe[1][0] : qe[0][0]);
+                            if (lane + 32 < n && lane + 32 < cap) put(u ? qe[1][1] : qe[0][1]);
+                            if (n > 64 || cap < n) {
+                                // past the staged words or past 64 entries: from global memory
+                                const int32_t base = __ldg(p.ptile_off + t16 * p.nch + c);
+                                for (int j = lane; j < n; j += 32)
+                                    if (j >= 64 || j >= cap) put(__ldg(p.precs + base + kRecHdrWords + lo + j));
+                            }
+                        }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            // the leader's own warps arrive locally; the peer's across the pair
+                            mbar_arrive(rank == 0 ? &a_full[as] : &a_ready[as]);
+                        }
+                    }
+                    if (++as == C::kAStages) { as = 0; aph ^= 1u; }
+                }
+                if (!ok) break;
+                if (lane == 0) mbar_arrive(&w_empty[wslot]);
+            }
+        }
+    } else {
+        // ------------------------------------------------------- epilogue
+        const int qd = warp & 3;                       // TMEM lane quarter
+        int ac = 0;
+        uint32_t acph = 0;
+        for (int t = pair; t < p.tiles_total; t += npairs) {
+            if (!role_wait(&acc_full[ac], acph, abort_flag)) break;
+            tc_fence_after();
+            const int rt = t / p.tiles_n, nt = t % p.tiles_n;
+            const int64_t row = (int64_t)rt * 2 * kGemmBM + (int64_t)rank * kGemmBM + 32 * qd + lane;
+            const float bias = (p.bias && row < p.rows) ? bf16_bits_to_f32(__ldg(p.bias + row)) : 0.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem_base + ((uint32_t)(32 * qd) << 16) + (uint32_t)(ac * BN + c0), v);
+                if (row < p.rows) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int64_t n = (int64_t)nt * BN + c0 + i;
+                        if (n < p.M) {
+                            const float o = __uint_as_float(v[i]) + bias;
+                            if (p.y_f32) reinterpret_cast<float *>(p.y)[n * p.ldy + row] = o;
+                            else reinterpret_cast<uint16_t *>(p.y)[n * p.ldy + row] = f32_to_bf16_bits_rn(o);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (rank == 0) mbar_arrive(&acc_empty[ac]);
+                else mbar_arrive_cluster(leader(&acc_empty[ac]));
+            }
+            if (++ac == 2) { ac = 0; acph ^= 1u; }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    // neither CTA leaves (or frees tensor memory) while the other may still
+    // signal its barriers or read its operands
+    cluster_sync_all();
+    if (warp == 2) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;"
+                     :: "r"(tmem_base), "r"(C::kTmemCols) : "memory");
+    }
+}
+
+
 static int gemm_sms() {
     static int cache[64] = {0};
     int dev = 0;
@@ -460,6 +913,52 @@ static int launch_gemm(GemmParams &p, const uint8_t *layout, int64_t in_f, const
     return check_launch("bf16x_gemm");
 }
 
+// CTA-pair launch: tiles of 256 rows x 256 tokens, clusters of 2 CTAs.
+static int launch_gemm2sm(GemmParams &p, const uint8_t *layout, int64_t in_f, const uint16_t *x, int64_t ldx,
+                          cudaStream_t st) {
+    using C = Gemm2Cfg;
+    const cuuint64_t wdims[3] = {(cuuint64_t)(kChunkBytes / 4), (cuuint64_t)p.nch, (cuuint64_t)p.rows};
+    const cuuint64_t wstr[2] = {(cuuint64_t)kChunkBytes, (cuuint64_t)resident_row_bytes(in_f)};
+    const cuuint32_t wbox[3] = {(cuuint32_t)(kChunkBytes / 4), 1u, (cuuint32_t)kGemmWRows};
+    if (!encode_tiled(&p.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, layout, wdims, wstr, wbox))
+        return set_error(BF16X_ERR_CUDA, "bf16x_gemm: weight tensor map");
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t xdims[2] = {(cuuint64_t)in_f, (cuuint64_t)p.M};
+    const cuuint64_t xstr[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t xbox[2] = {(cuuint32_t)kGemmBK, 128u};      // each CTA stages half the 256-token tile
+    const cuuint32_t estr[2] = {1, 1};
+    if (fn(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), xdims, xstr, xbox, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return set_error(BF16X_ERR_CUDA, "bf16x_gemm: activation tensor map");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool attr_set[64] = {false};
+    if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: device index");
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm2sm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: smem attribute: %s", cudaGetErrorString(e));
+        attr_set[dev] = true;
+    }
+    const int pairs = std::max(1, std::min(p.tiles_total, gemm_sms() / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    cfg.blockDim = dim3((unsigned)kGemmThreads);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm2sm_kernel<256>, p);
+    if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: pair launch: %s", cudaGetErrorString(e));
+    return check_launch("bf16x_gemm");
+}
+
 }  // namespace bf16x
 
 using namespace bf16x;
@@ -494,6 +993,16 @@ extern "C" int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const
     // token tile: 256 when that still fills the GPU, else smaller
     int bn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
     if (bn == 256 && tiles_m * ((M + 255) / 256) < sms) bn = 128;
+#ifndef BF16X_GEMM_NO_PAIR
+    if (bn == 256) {
+        // CTA pairs: tiles of 256 rows x 256 tokens
+        p.tiles_n = (int)((M + 255) / 256);
+        const int64_t total2 = (rows + 2 * kGemmBM - 1) / (2 * kGemmBM) * p.tiles_n;
+        if (total2 > 0x7fffffffLL) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: too many tiles");
+        p.tiles_total = (int)total2;
+        return launch_gemm2sm(p, layout, in_f, x, ldx, st);
+    }
+#endif
     p.tiles_n = (int)((M + bn - 1) / bn);
     const int64_t total = tiles_m * p.tiles_n;
     if (total > 0x7fffffffLL) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: too many tiles");

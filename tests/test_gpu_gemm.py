@@ -68,3 +68,58 @@ def test_gemm_large_m_deterministic():
     assert torch.equal(a, b)
     ref = x.float() @ w.float().T
     assert float((a - ref).norm() / ref.norm()) < GATE
+
+
+def _dense_patch_weight(rows, in_f, seed):
+    # magnitudes spread over 2^-40..2^0: most weights sit more than 7 binades
+    # below their 16-column maximum, so records overflow every staging limit
+    g = torch.Generator().manual_seed(seed)
+    e = torch.randint(-40, 1, (rows, in_f), generator=g).float()
+    m = 1.0 + torch.rand(rows, in_f, generator=g)
+    s = torch.where(torch.rand(rows, in_f, generator=g) < 0.5, -1.0, 1.0)
+    return bits_of((s * m * torch.exp2(e)).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("shape,M", [((256, 512), 200), ((300, 1536), 64)])
+def test_gemm_dense_patches(shape, M):
+    wb = _dense_patch_weight(*shape, seed=7)
+    p = oracle_dict(wb)
+    rw = ResidentWeight.from_packed(p, device="cuda")
+    assert rw.n_patches > wb.size // 2
+    assert np.array_equal(bits_of(rw.decode()), wb)
+    x = synthetic_activation(M, shape[1], seed=3)
+    y = rw.gemm(x.cuda(), out_dtype=torch.float32).cpu().numpy()
+    ref = oracle.matmul_bf16w(x.float().numpy(), wb)
+    assert rel_l2(y, ref) < GATE
+    _lib.check_device_status()
+
+
+# Shapes with at least 148 tiles of 128 rows x 256 tokens run the CTA-pair
+# kernel (tiles of 256 rows x 256 tokens, cluster of 2).
+def test_gemm_pair_identity_probe():
+    rows, in_f, M = 8192, 1024, 1024
+    wb = bits_of(synthetic_weight(rows, in_f, seed=21))
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    x = torch.eye(M, in_f, dtype=torch.bfloat16)
+    y = rw.gemm(x.cuda(), out_dtype=torch.float32).cpu().numpy()
+    expect = oracle.bf16_bits_to_f32(wb)[:, :M].T
+    assert np.array_equal(y.view(np.uint32), np.ascontiguousarray(expect).view(np.uint32))
+    _lib.check_device_status()
+
+
+@pytest.mark.parametrize("dense", [False, True])
+def test_gemm_pair_ragged_vs_oracle(dense):
+    # 4196 rows: the last pair tile has 100 rows (all in the leader CTA);
+    # 2597 tokens: the last token tile is ragged in both CTAs' halves
+    rows, in_f, M = 4196, 1024, 2597
+    wb = _dense_patch_weight(rows, in_f, seed=5) if dense else bits_of(synthetic_weight(rows, in_f, seed=23))
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    bias = (torch.randn(rows, generator=torch.Generator().manual_seed(1)) * 0.1).to(torch.bfloat16)
+    x = synthetic_activation(M, in_f, seed=29)
+    ref = oracle.matmul_bf16w(x.float().numpy(), wb, bias.float().numpy())
+    y = rw.gemm(x.cuda(), bias=bias.cuda(), out_dtype=torch.float32).cpu().numpy()
+    assert rel_l2(y, ref) < GATE
+    y16 = rw.gemm(x.cuda(), bias=bias.cuda(), out_dtype=torch.bfloat16).float().cpu().numpy()
+    ref16 = torch.from_numpy(ref).to(torch.bfloat16).float().numpy()
+    assert rel_l2(y16, ref16) < GATE
+    _lib.check_device_status()

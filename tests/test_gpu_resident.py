@@ -144,3 +144,14 @@ def test_repack_filtered_table():
     rw = ResidentWeight.from_packed(p, device="cuda")
     assert np.array_equal(bits_of(rw.decode()), w)
     _lib.check_device_status()
+
+
+@pytest.mark.parametrize("b", [1, 8])
+def test_gemv_dense_patches(b):
+    from tests.test_gpu_gemm import _dense_patch_weight
+    wb = _dense_patch_weight(300, 1536, seed=9)
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    assert rw.n_patches > wb.size // 2
+    x = synthetic_activation(b, 1536, seed=5)
+    _gemv_check(wb, x, rw)
+    _lib.check_device_status()
