@@ -62,6 +62,15 @@ def parse_args():
     return ap.parse_args()
 
 
+def gemm_kernel_name(rows, M, sms):
+    """Which GEMM kernel bf16x_gemm launches for (rows, M): the CTA-pair
+    kernel for 256-token tiles that fill the GPU, else the single-CTA one."""
+    bn = 64 if M <= 64 else 128 if M <= 128 else 256
+    if bn == 256 and (rows + 127) // 128 * ((M + 255) // 256) < sms:
+        bn = 128
+    return "gemm2sm_kernel" if bn == 256 else f"gemm_kernel<{bn}>"
+
+
 def make_resident(w, fmt, dev):
     """The fused kernels' resident weight built from `w` through the chosen format."""
     from bfloat16x_b200.opqk_linear import bf16x_quantize
@@ -566,7 +575,8 @@ def run_gemm(args):
             "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per_layer[i], 4) for i, L in enumerate(layers)},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(ach / peak_tf, 4), "peak_source": peak_kind,
-                         "kernel": f"gemm_kernel {Ld['rows']}x{Ld['in_f']} M={M}", "traffic": None},
+                         "kernel": f"{gemm_kernel_name(Ld['rows'], M, torch.cuda.get_device_properties(dev).multi_processor_count)} "
+                                   f"{Ld['rows']}x{Ld['in_f']} M={M}", "traffic": None},
             "gpu_launches": args.steps * len(layers), "clocks": clocks, "cublas_bf16": cublas,
         }
         print(json.dumps(line), flush=True)

@@ -500,7 +500,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_a
 }
 
 // Tiled TMA load into this CTA's shared memory whose completion is counted
-// on a barrier of the leader CTA of the pair (no multicast).
+// on a barrier of the leader CTA of the pair (a plain load of this CTA's half).
 __device__ __forceinline__ void tma_load_2d_pair(void *dst, const void *map, int c0, int c1, uint32_t bar_cluster) {
     asm volatile(
         "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
