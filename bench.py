@@ -53,8 +53,12 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--mode", choices=["gemv", "gemm"], default="gemv",
-                    help="gemv: decode+GEMV sweep (the headline); gemm: decode+GEMM prefill TFLOPS")
+    ap.add_argument("--mode", choices=["gemv", "gemm", "e2e"], default="gemv",
+                    help="gemv: decode+GEMV sweep (the headline); gemm: decode+GEMM prefill TFLOPS; "
+                         "e2e: Llama-style decoder, ms per generated token against bf16 weights")
+    ap.add_argument("--model", choices=["1b", "8b", "tiny"], default="1b", help="decoder for --mode e2e")
+    ap.add_argument("--prompt", type=int, default=512, help="prompt tokens for --mode e2e")
+    ap.add_argument("--new", type=int, default=128, help="generated tokens for --mode e2e")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens M for --mode gemm")
     ap.add_argument("--format", choices=["flat", "gguf", "gguf-lossless"], default="flat",
                     help="weight source: the bf16x_quantize dict (flat), the 11.5-bpw GGUF blocks "
@@ -585,10 +589,54 @@ def run_gemm(args):
         dist.destroy_process_group()
 
 
+def run_e2e(args):
+    """BASELINE configs 4/5 on one GPU: greedy decode after a prompt prefill,
+    ms per generated token with BF16X weights (every projection and lm_head
+    through the fused kernels) and with the same weights in plain bf16."""
+    import torch
+
+    from bfloat16x_b200 import _lib
+    from bfloat16x_b200.llama_e2e import CONFIGS, LlamaModel, generate, pack_model
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.model]
+    max_seq = args.prompt + args.new + 8
+    g = torch.Generator(device="cpu").manual_seed(7)
+    prompt = torch.randint(0, cfg.vocab, (1, args.prompt), generator=g).to(dev)
+    model = LlamaModel(cfg, max_seq, dev, seed=0)
+    n_w = sum(m.weight.numel() for m in model.modules() if isinstance(m, torch.nn.Linear))
+    generate(model, prompt, 4)                                   # warm-up
+    ref_tok, ref_pre, ref_ms = generate(model, prompt, args.new)
+    nbytes, _ = pack_model(model)
+    generate(model, prompt, 4)
+    clock = ClockSampler(dev.index)
+    clock.start()
+    tok, pre, ms = generate(model, prompt, args.new)
+    clocks = clock.stop()
+    _lib.check_device_status(dev.index)
+    same = int((tok == ref_tok).cumprod(0).sum().item())
+    line = {
+        "metric": f"e2e greedy decode ms/token ({args.model} Llama-style, batch 1)", "value": round(ms, 4),
+        "unit": "ms/token", "higher_is_better": False, "n_gpus": 1, "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) weights, random prompt ids)",
+        "config": {"workload": f"configs[{3 if args.model == '1b' else 4}] {args.model}: prompt {args.prompt}, "
+                               f"{args.new} new tokens, every projection and lm_head BF16X-packed",
+                   "hidden": cfg.hidden, "layers": cfg.layers, "vocab": cfg.vocab},
+        "bf16_ms_per_token": round(ref_ms, 4), "speedup_vs_bf16": round(ref_ms / ms, 3),
+        "prefill_ms": round(pre, 3), "bf16_prefill_ms": round(ref_pre, 3),
+        "linear_weight_bytes": {"bf16x_resident": nbytes, "bf16": 2 * n_w},
+        "tokens_equal_to_bf16_run": same, "timing": "decode step as one CUDA graph replayed per token",
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "e2e":
+        run_e2e(args)
     elif args.mode == "gemm":
         run_gemm(args)
     else:
