@@ -5,6 +5,7 @@ the reference algorithms (dfytensor/bfloat16x):
 
 * ``quantize``      -> ``bf16x_quantize``            opqk_linear.py:291-324
 * ``decode``        -> ``BF16XLinear._decode_tile``  opqk_linear.py:360-377
+* ``decode_scatter``-> ``bf16x_decode_triton``       bf16x_triton_test.py:11-108
 * ``linear``        -> ``BF16XLinear.forward``       opqk_linear.py:390-404
 * ``gguf_*``        -> ``bf16x_gguf_block``          bf16x_gguf_block.py:44-187
 
@@ -113,6 +114,28 @@ def decode(p: dict, row_start: int = 0, row_end: int | None = None, sub: int = 1
         lib().oracle_decode(_ptr(s), s.size, _ptr(m), m.size, _ptr(d), d.size, _ptr(e),
                             _ptr(oi), _ptr(ov), oi.size, sub, row_start * in_f, cnt, _ptr(out))
     return out.reshape(row_end - row_start, in_f)
+
+
+def decode_scatter(p: dict, sub: int = 16) -> np.ndarray:
+    """The reference's two-kernel decode (bf16x_triton_test.py:11-108):
+    every element decodes with its stream delta (7 = saturated), then each
+    overflow entry rewrites the exponent of the element at its own index,
+    exp = clamp(emax - val, 0, 255) (_bf16x_fix_ovf_kernel, :55-77).  Unlike
+    ``decode`` (searchsorted), it is exact for a table reduced to the
+    entries with delta > 7, as the on-disk format stores it
+    (pack_to_disk.py:62-66).  Returns uint16 bits [out_f, in_f]."""
+    q = dict(p)
+    q["delta_ovf_idx"] = np.zeros(0, np.int32)
+    q["delta_ovf_val"] = np.zeros(0, np.uint8)
+    out = decode(q, sub=sub).reshape(-1)
+    oi = np.asarray(p["delta_ovf_idx"]).astype(np.int64)
+    ov = np.asarray(p["delta_ovf_val"]).astype(np.int64)
+    if oi.size:
+        e = np.asarray(p["emax"]).astype(np.int64)[oi // sub]
+        ex = np.clip(e - ov, 0, 255).astype(np.uint16)
+        cur = out[oi]
+        out[oi] = (cur & np.uint16(0x807F)) | (ex << np.uint16(7))
+    return out.reshape(int(p["out_f"]), int(p["in_f"]))
 
 
 def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:

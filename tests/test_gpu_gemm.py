@@ -95,9 +95,9 @@ def test_gemm_dense_patches(shape, M):
 
 
 # Shapes with at least 148 tiles of 128 rows x 256 tokens run the CTA-pair
-# kernel (tiles of 256 rows x 256 tokens, cluster of 2).
-def test_gemm_pair_identity_probe():
-    rows, in_f, M = 8192, 1024, 1024
+# kernel (cluster of 2, tiles of 256 rows x 256 tokens).
+@pytest.mark.parametrize("rows,in_f,M", [(8192, 1024, 768), (8192, 1024, 1024), (8192, 2048, 2048)])
+def test_gemm_pair_identity_probe(rows, in_f, M):
     wb = bits_of(synthetic_weight(rows, in_f, seed=21))
     rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
     x = torch.eye(M, in_f, dtype=torch.bfloat16)
@@ -107,11 +107,13 @@ def test_gemm_pair_identity_probe():
     _lib.check_device_status()
 
 
+# 4196 rows: the last pair tile has 100 rows (all in the leader CTA); 2597
+# tokens: the last token tile is ragged in both CTAs' halves; 8100 rows at
+# 700 tokens: ragged in rows and in tokens with 96 tiles
+@pytest.mark.parametrize("rows,M", [(4196, 2597), (8100, 700)])
 @pytest.mark.parametrize("dense", [False, True])
-def test_gemm_pair_ragged_vs_oracle(dense):
-    # 4196 rows: the last pair tile has 100 rows (all in the leader CTA);
-    # 2597 tokens: the last token tile is ragged in both CTAs' halves
-    rows, in_f, M = 4196, 1024, 2597
+def test_gemm_pair_ragged_vs_oracle(rows, M, dense):
+    in_f = 1024
     wb = _dense_patch_weight(rows, in_f, seed=5) if dense else bits_of(synthetic_weight(rows, in_f, seed=23))
     rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
     bias = (torch.randn(rows, generator=torch.Generator().manual_seed(1)) * 0.1).to(torch.bfloat16)
