@@ -59,6 +59,7 @@ def parse_args():
     ap.add_argument("--model", choices=["1b", "8b", "tiny"], default="1b", help="decoder for --mode e2e")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens for --mode e2e")
     ap.add_argument("--new", type=int, default=128, help="generated tokens for --mode e2e")
+    ap.add_argument("--seqs", type=int, default=1, help="sequences decoded together for --mode e2e (batch)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens M for --mode gemm")
     ap.add_argument("--format", choices=["flat", "gguf", "gguf-lossless"], default="flat",
                     help="weight source: the bf16x_quantize dict (flat), the 11.5-bpw GGUF blocks "
@@ -66,9 +67,13 @@ def parse_args():
     return ap.parse_args()
 
 
-def gemm_kernel_name(rows, M, sms):
-    """Which GEMM kernel bf16x_gemm launches for (rows, M): the CTA-pair
+def gemm_kernel_name(rows, in_f, M, sms):
+    """Which GEMM kernel ResidentWeight.gemm launches for (rows, in_f, M):
+    the slab kernel when the shape takes a workspace, else the CTA-pair
     kernel for 256-token tiles that fill the GPU, else the single-CTA one."""
+    from bfloat16x_b200 import _lib
+    if _lib.lib().bf16x_gemm_workspace_bytes(rows, in_f, M) > 0:
+        return "gemm_slab_kernel"
     bn = 64 if M <= 64 else 128 if M <= 128 else 256
     if bn == 256 and (rows + 127) // 128 * ((M + 255) // 256) < sms:
         bn = 128
@@ -579,7 +584,7 @@ def run_gemm(args):
             "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per_layer[i], 4) for i, L in enumerate(layers)},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(ach / peak_tf, 4), "peak_source": peak_kind,
-                         "kernel": f"{gemm_kernel_name(Ld['rows'], M, torch.cuda.get_device_properties(dev).multi_processor_count)} "
+                         "kernel": f"{gemm_kernel_name(Ld['rows'], Ld['in_f'], M, torch.cuda.get_device_properties(dev).multi_processor_count)} "
                                    f"{Ld['rows']}x{Ld['in_f']} M={M}", "traffic": None},
             "gpu_launches": args.steps * len(layers), "clocks": clocks, "cublas_bf16": cublas,
         }
@@ -590,20 +595,26 @@ def run_gemm(args):
 
 
 def run_e2e(args):
-    """BASELINE configs 4/5 on one GPU: greedy decode after a prompt prefill,
-    ms per generated token with BF16X weights (every projection and lm_head
-    through the fused kernels) and with the same weights in plain bf16."""
+    """BASELINE configs 4/5: greedy decode after a prompt prefill, ms per
+    generated token with BF16X weights (every projection and lm_head through
+    the fused kernels) and with the same weights in plain bf16.  Under
+    torchrun the model is tensor-parallel over the ranks (one GPU each)."""
     import torch
+    import torch.distributed as dist
 
     from bfloat16x_b200 import _lib
     from bfloat16x_b200.llama_e2e import CONFIGS, LlamaModel, generate, pack_model
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     cfg = CONFIGS[args.model]
     max_seq = args.prompt + args.new + 8
     g = torch.Generator(device="cpu").manual_seed(7)
-    prompt = torch.randint(0, cfg.vocab, (1, args.prompt), generator=g).to(dev)
-    model = LlamaModel(cfg, max_seq, dev, seed=0)
+    prompt = torch.randint(0, cfg.vocab, (args.seqs, args.prompt), generator=g).to(dev)
+    model = LlamaModel(cfg, max_seq, dev, seed=0, tp=world, batch=args.seqs)
     n_w = sum(m.weight.numel() for m in model.modules() if isinstance(m, torch.nn.Linear))
     generate(model, prompt, 4)                                   # warm-up
     ref_tok, ref_pre, ref_ms = generate(model, prompt, args.new)
@@ -614,21 +625,36 @@ def run_e2e(args):
     tok, pre, ms = generate(model, prompt, args.new)
     clocks = clock.stop()
     _lib.check_device_status(dev.index)
-    same = int((tok == ref_tok).cumprod(0).sum().item())
-    line = {
-        "metric": f"e2e greedy decode ms/token ({args.model} Llama-style, batch 1)", "value": round(ms, 4),
-        "unit": "ms/token", "higher_is_better": False, "n_gpus": 1, "dtype": "bf16",
-        "data": "synthetic (random-init N(0,0.02) weights, random prompt ids)",
-        "config": {"workload": f"configs[{3 if args.model == '1b' else 4}] {args.model}: prompt {args.prompt}, "
-                               f"{args.new} new tokens, every projection and lm_head BF16X-packed",
-                   "hidden": cfg.hidden, "layers": cfg.layers, "vocab": cfg.vocab},
-        "bf16_ms_per_token": round(ref_ms, 4), "speedup_vs_bf16": round(ref_ms / ms, 3),
-        "prefill_ms": round(pre, 3), "bf16_prefill_ms": round(ref_pre, 3),
-        "linear_weight_bytes": {"bf16x_resident": nbytes, "bf16": 2 * n_w},
-        "tokens_equal_to_bf16_run": same, "timing": "decode step as one CUDA graph replayed per token",
-        "clocks": clocks,
-    }
-    print(json.dumps(line), flush=True)
+    t = torch.tensor([ms, ref_ms, pre, ref_pre, float(nbytes), float(n_w)], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t[:4].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t[4:].clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        t = torch.cat([mx, sm])
+    ms, ref_ms, pre, ref_pre, nbytes, n_w = (float(v) for v in t.tolist())
+    same = int((tok == ref_tok).all(dim=1).int().cumprod(0).sum().item())
+    if rank == 0:
+        line = {
+            "metric": f"e2e greedy decode ms/token ({args.model} Llama-style, batch {args.seqs})", "value": round(ms, 4),
+            "unit": "ms/token", "higher_is_better": False, "n_gpus": world, "dtype": "bf16",
+            "data": "synthetic (random-init N(0,0.02) weights, random prompt ids)",
+            "config": {"workload": f"configs[{3 if args.model == '1b' else 4}] {args.model}: prompt {args.prompt}, "
+                                   f"{args.new} new tokens, batch {args.seqs}, every projection and lm_head "
+                                   f"BF16X-packed" + (f", tensor-parallel over {world} GPUs" if world > 1 else ""),
+                       "hidden": cfg.hidden, "layers": cfg.layers, "vocab": cfg.vocab, "tp": world,
+                       "parallelism": f"tp{world}"},
+            "bf16_ms_per_token": round(ref_ms, 4), "speedup_vs_bf16": round(ref_ms / ms, 3),
+            "prefill_ms": round(pre, 3), "bf16_prefill_ms": round(ref_pre, 3),
+            "linear_weight_bytes": {"bf16x_resident": int(nbytes), "bf16": int(2 * n_w)},
+            "tokens_equal_to_bf16_run": same,
+            "timing": "decode step as one CUDA graph replayed per token; max over ranks",
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():

@@ -867,6 +867,355 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
 }
 
 
+// ------------------------------------------------ slab kernel (large M)
+// For many tokens the weight is decoded ONCE per 256-row slab instead of once
+// per token tile: the pairs that first need a slab decode it (their share of
+// its 16-row tiles, chunk by chunk) into a ring of bf16 slabs in global
+// memory, small enough to stay in L2, and every token tile of the slab then
+// streams it back with TMA, exactly like the activations.  The MMA pipeline
+// is therefore a plain two-operand TMA pipeline (one barrier per stage, no
+// per-k-block hand-off between decoder warps and the MMA issuer), and the
+// decode work per flop drops by the number of token tiles per slab.
+//
+// Synchronisation between CTAs goes through two counters per (slab slot,
+// chunk position) in the workspace, both monotonic within a launch:
+//   ready   -- 16-row tiles decoded into that position (a slab's chunk is
+//              readable once all of its tiles are in);
+//   release -- token tiles that have finished loading that position (it may
+//              be overwritten once every token tile of its slab is done).
+// A slot holds a window of `wring` chunks of its slab; chunk c lives at
+// position c % wring.  Every wait is bounded and raises the abort flag and
+// the timeout status instead of hanging.  Slot reuse only waits on token
+// tiles that precede the waiting decoder's tile in the pair-strided tile
+// order, and decode shares belong to a slab's first tiles in that order, so
+// the dependencies cannot form a cycle when all CTAs are resident (the grid
+// never exceeds the SM count, one CTA per SM).
+struct SlabCfg {
+    static constexpr int kStages = 6;
+    static constexpr int kAStage = 128 * 128;       // 16 KB: 128 rows x 64 columns of the slab
+    static constexpr int kBStage = 128 * 128;       // 16 KB: this CTA's 128 tokens x 64 columns
+    static constexpr int kStage = kAStage + kBStage;
+#ifndef BF16X_SLAB_DEC
+#define BF16X_SLAB_DEC 8
+#endif
+    static constexpr int kDecWarps = BF16X_SLAB_DEC;
+    static constexpr int kFirstDec = 6;             // warps: producer, MMA, 4 epilogue, decoders
+    static constexpr int kThreads = (kFirstDec + kDecWarps) * 32;
+    static constexpr int kBarOff = kStages * kStage;
+    static constexpr int kNumBars = 2 * kStages + 4;
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+    static constexpr int kSmem = kMiscOff + 16 + 1024;
+    static_assert(kSmem <= 227 * 1024, "shared memory");
+};
+
+struct SlabParams {
+    CUtensorMap amap;          // slab ring [nslot * 256 rows][wring * 256] bf16, box 64 x 128, 128B swizzle
+    CUtensorMap xmap;          // activations [M][in_f] bf16, box 64 x 128, 128B swizzle
+    const uint8_t *layout;
+    const int32_t *ptile_off;
+    const uint32_t *precs;
+    int64_t rows, M, row_bytes;
+    int nch, n_tiles16, tiles_n, tiles_total, npairs;
+    int nslot, wring;
+    uint16_t *ring;            // [nslot][256][wring * 256]
+    uint32_t *ready;           // [nslot][wring]
+    uint32_t *release;         // [nslot][wring]
+    const uint16_t *bias;
+    void *y;
+    int y_f32;
+    int64_t ldy;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Wait until *ctr >= target (another CTA's progress); bounded like role_wait.
+__device__ __forceinline__ bool counter_wait(const uint32_t *ctr, uint32_t target, volatile int *abort_flag) {
+    if (ld_acquire_gpu(ctr) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (*abort_flag) return false;
+        __nanosleep(64);
+        if (ld_acquire_gpu(ctr) >= target) return true;
+        if ((i & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_status, kErrWaitTimeout);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+// Slab geometry shared by all roles.
+struct SlabTile {
+    int rt, nt;          // slab (256-row group) and token tile
+    int slot, gen;       // ring slot and how many earlier slabs used it
+    int n16;             // 16-row tiles in the slab
+};
+
+__device__ __forceinline__ SlabTile slab_tile(const SlabParams &p, int t) {
+    SlabTile s;
+    s.rt = t / p.tiles_n;
+    s.nt = t - s.rt * p.tiles_n;
+    s.slot = s.rt % p.nslot;
+    s.gen = s.rt / p.nslot;
+    s.n16 = min(16, p.n_tiles16 - 16 * s.rt);
+    return s;
+}
+
+// Earlier uses of the ring position of chunk c by this slot (all slabs of
+// earlier generations, then earlier laps of this slab), and the ready count
+// at which chunk c of this slab is complete: earlier slabs are whole (16
+// tiles; only the last slab can be shorter, and it is the last one to use
+// its slot), this slab's laps up to and including c hold n16 tiles each.
+__device__ __forceinline__ uint32_t slab_prior_uses(const SlabParams &p, const SlabTile &s, int c) {
+    const int pos = c % p.wring;
+    const int per_slab = (p.nch - 1 - pos) / p.wring + 1;
+    return (uint32_t)(s.gen * per_slab + c / p.wring);
+}
+
+__device__ __forceinline__ uint32_t slab_ready_target(const SlabParams &p, const SlabTile &s, int c) {
+    const int pos = c % p.wring;
+    const int per_slab = (p.nch - 1 - pos) / p.wring + 1;
+    return (uint32_t)(s.gen * per_slab * 16 + (c / p.wring + 1) * s.n16);
+}
+
+// The 16-row tiles [a, b) of its slab that token tile t decodes: a slab is
+// decoded by its token tiles that fall in the first pair-strided round
+// (wave) reaching the slab, its 16-row tiles dealt evenly among them.
+__device__ __forceinline__ void slab_share(const SlabParams &p, int t, int &a, int &b) {
+    const int rt = t / p.tiles_n, j = t - rt * p.tiles_n;
+    const int first = rt * p.tiles_n;
+    const int wave_end = (first / p.npairs + 1) * p.npairs;
+    const int k = min(p.tiles_n, wave_end - first);
+    const int n16 = min(16, p.n_tiles16 - 16 * rt);
+    if (j >= k) { a = b = 0; return; }
+    a = n16 * j / k;
+    b = n16 * (j + 1) / k;
+}
+
+__global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const __grid_constant__ SlabParams p) {
+    using C = SlabCfg;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
+    uint64_t *full = bars, *empty = bars + C::kStages;
+    uint64_t *acc_full = bars + 2 * C::kStages, *acc_empty = acc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = (int)(blockIdx.x >> 1);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        // acc_empty: the 4 epilogue warps of each CTA
+        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 8); }
+        abort_flag[0] = 0;
+        fence_mbar_init();
+    }
+    cluster_sync_all();
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(tmem_slot)), "r"(512) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    auto leader = [&](uint64_t *bar) { return mapa_shared(smem_u32(bar), 0u); };
+    const uint32_t tmem_base = *tmem_slot;
+    const int nkb = p.nch * 4;
+
+    if (warp == 0) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            prefetch_tensormap(&p.amap);
+            prefetch_tensormap(&p.xmap);
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = pair; t < p.tiles_total && ok; t += p.npairs) {
+                const SlabTile st = slab_tile(p, t);
+                for (int kb = 0; kb < nkb && ok; ++kb) {
+                    const int c = kb >> 2, pos = c % p.wring;
+                    if ((kb & 3) == 0) {
+                        // this chunk of the slab decoded by every CTA that shares it
+                        if (!counter_wait(p.ready + st.slot * p.wring + pos, slab_ready_target(p, st, c), abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        fence_proxy_async_global();
+                    }
+                    if (!role_wait(&empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+                    const uint32_t lb = leader(&full[s]);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * C::kStage));
+                    uint8_t *stg = smem + s * C::kStage;
+                    tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
+                                     st.slot * 256 + (int)rank * 128, lb);
+                    tma_load_2d_pair(stg + C::kAStage, &p.xmap, kb * kGemmBK, st.nt * 256 + (int)rank * 128, lb);
+                    if (++s == C::kStages) { s = 0; ph ^= 1u; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16_m<256, 256>();
+            int s = 0, ac = 0;
+            uint32_t ph = 0, acph = 0;
+            bool ok = true;
+            for (int t = pair; t < p.tiles_total && ok; t += p.npairs) {
+                const SlabTile st = slab_tile(p, t);
+                if (!role_wait(&acc_empty[ac], acph ^ 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(ac * 256);
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!role_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    if ((kb & 3) == 3 || kb == nkb - 1) {
+                        // both CTAs' copies of this chunk have landed: the pair no
+                        // longer reads its ring position
+                        atomicAdd(p.release + st.slot * p.wring + (kb >> 2) % p.wring, 1u);
+                    }
+                    const uint8_t *stg = smem + s * C::kStage;
+                    const uint64_t ad = umma_desc_sw128(smem_u32(stg));
+                    const uint64_t bd = umma_desc_sw128(smem_u32(stg + C::kAStage));
+#pragma unroll
+                    for (int k16 = 0; k16 < kGemmBK / 16; ++k16)
+                        umma_bf16_pair(d_tmem, ad + 2u * k16, bd + 2u * k16, idesc, (kb | k16) != 0);
+                    umma_commit_pair(smem_u32(&empty[s]));
+                    umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1u));
+                    if (++s == C::kStages) { s = 0; ph ^= 1u; }
+                }
+                if (!ok) break;
+                umma_commit_pair(smem_u32(&acc_full[ac]));
+                umma_commit_pair(mapa_shared(smem_u32(&acc_full[ac]), 1u));
+                if (++ac == 2) { ac = 0; acph ^= 1u; }
+            }
+        }
+    } else if (warp < C::kFirstDec) {
+        // ------------------------------------------------------- epilogue
+        const int qd = warp & 3;                       // TMEM lane quarter
+        int ac = 0;
+        uint32_t acph = 0;
+        for (int t = pair; t < p.tiles_total; t += p.npairs) {
+            if (!role_wait(&acc_full[ac], acph, abort_flag)) break;
+            tc_fence_after();
+            const SlabTile st = slab_tile(p, t);
+            const int64_t row = (int64_t)st.rt * 256 + (int64_t)rank * 128 + 32 * qd + lane;
+            const float bias = (p.bias && row < p.rows) ? bf16_bits_to_f32(__ldg(p.bias + row)) : 0.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < 256; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem_base + ((uint32_t)(32 * qd) << 16) + (uint32_t)(ac * 256 + c0), v);
+                if (row < p.rows) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int64_t n = (int64_t)st.nt * 256 + c0 + i;
+                        if (n < p.M) {
+                            const float o = __uint_as_float(v[i]) + bias;
+                            if (p.y_f32) reinterpret_cast<float *>(p.y)[n * p.ldy + row] = o;
+                            else reinterpret_cast<uint16_t *>(p.y)[n * p.ldy + row] = f32_to_bf16_bits_rn(o);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (rank == 0) mbar_arrive(&acc_empty[ac]);
+                else mbar_arrive_cluster(leader(&acc_empty[ac]));
+            }
+            if (++ac == 2) { ac = 0; acph ^= 1u; }
+        }
+    } else {
+        // ------------------------------------------------------- decoders
+        // An item is one 16-row tile x one chunk: lane (q = lane & 7, r =
+        // lane >> 3) decodes group q (32 columns) of rows r, r+4, r+8, r+12
+        // and stores them as bf16 into the slab ring; the item's patch
+        // entries are then written over their saturated values.
+        const int dw = warp - C::kFirstDec;
+        const int q = lane & 7, r0 = lane >> 3;
+        const int64_t ld = (int64_t)p.wring * kChunkElems;
+        bool ok = true;
+        for (int t = pair; t < p.tiles_total && ok; t += p.npairs) {
+            int a, b;
+            slab_share(p, t, a, b);
+            const int ra = a + (b - a) * (int)rank / 2, rb = a + (b - a) * ((int)rank + 1) / 2;
+            const int nr = rb - ra;
+            if (nr <= 0) continue;
+            const SlabTile st = slab_tile(p, t);
+            const uint32_t tn = (uint32_t)p.tiles_n;
+            for (int i = dw; i < p.nch * nr; i += C::kDecWarps) {
+                const int c = i / nr, rtile = ra + (i - c * nr);
+                const int pos = c % p.wring;
+                const uint32_t prior = slab_prior_uses(p, st, c);
+                if (prior > 0) {
+                    // every token tile of the position's previous content is done with it
+                    int w = 1;
+                    if (lane == 0) w = counter_wait(p.release + st.slot * p.wring + pos, prior * tn, abort_flag);
+                    if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+                }
+                const int64_t t16 = (int64_t)st.rt * 16 + rtile;
+                uint16_t *dst = p.ring + ((int64_t)st.slot * 256 + rtile * 16) * ld + (int64_t)pos * kChunkElems;
+                uint32_t sm[4][8], dd[4][3], elo[4], ehi[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int64_t row = t16 * 16 + r0 + 4 * k;
+                    if (row < p.rows) {
+                        load_group(p.layout + row * p.row_bytes + (int64_t)c * kChunkBytes, q, sm[k], dd[k], elo[k], ehi[k]);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) sm[k][u] = 0u;
+                        dd[k][0] = dd[k][1] = dd[k][2] = 0u;
+                        elo[k] = ehi[k] = 0u;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    GroupPairs gp;
+                    decode_pairs_from<0>(gp, sm[k], dd[k], elo[k], ehi[k]);
+                    uint4 *o = reinterpret_cast<uint4 *>(dst + (int64_t)(r0 + 4 * k) * ld + 32 * q);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        o[u] = make_uint4(gp.w[4 * u], gp.w[4 * u + 1], gp.w[4 * u + 2], gp.w[4 * u + 3]);
+                }
+                __syncwarp();
+                if (t16 < p.n_tiles16) {
+                    const int32_t off = __ldg(p.ptile_off + t16 * p.nch + c);
+                    const int n_all = (int)(__ldg(p.precs + off) >> 16);
+                    for (int j = lane; j < n_all; j += 32) {
+                        const uint32_t ent = __ldg(p.precs + off + kRecHdrWords + j);
+                        uint32_t rr, cc;
+                        frag_position(ent, rr, cc);
+                        dst[(int64_t)rr * ld + cc] = (uint16_t)(ent >> 16);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    // the item's stores before the count, for the other CTAs'
+                    // copy engines
+                    fence_proxy_async_global();
+                    __threadfence();
+                    atomicAdd(p.ready + st.slot * p.wring + pos, 1u);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(tmem_base), "r"(512) : "memory");
+    }
+}
+
 static int gemm_sms() {
     static int cache[64] = {0};
     int dev = 0;
@@ -959,13 +1308,148 @@ static int launch_gemm2sm(GemmParams &p, const uint8_t *layout, int64_t in_f, co
     return check_launch("bf16x_gemm");
 }
 
+// Slab-ring plan for a launch: used when every 256-row slab has at least 4
+// token tiles and the tiles fill every pair at least once.  The ring holds
+// the slabs of about two rounds of pairs, each as a window of at most the
+// whole K, so that it stays well inside L2.
+struct SlabPlan {
+    bool use;
+    int npairs, tiles_n, tiles_total, nslot, wring;
+    int64_t ring_bytes, counter_bytes;
+};
+
+#ifndef BF16X_SLAB_RING_MB
+#define BF16X_SLAB_RING_MB 64
+#endif
+constexpr int64_t kSlabRingMax = (int64_t)BF16X_SLAB_RING_MB << 20;
+
+static SlabPlan plan_slab(int64_t rows, int64_t in_f, int64_t M, int sms) {
+    SlabPlan s = {};
+    const int64_t nch = (in_f + kChunkElems - 1) / kChunkElems;
+    const int64_t tiles_m2 = (rows + 255) / 256;
+    const int64_t tn = (M + 255) / 256;
+    s.npairs = std::max(1, sms / 2);
+    if (tn < 4 || tiles_m2 * tn < s.npairs || tiles_m2 * tn > 0x7fffffffLL) return s;
+    s.tiles_n = (int)tn;
+    s.tiles_total = (int)(tiles_m2 * tn);
+#ifndef BF16X_SLAB_SLACK
+#define BF16X_SLAB_SLACK 1
+#endif
+    s.nslot = (int)std::min<int64_t>(tiles_m2, BF16X_SLAB_SLACK * ((s.npairs + tn - 1) / tn) + 2);
+    const int64_t slab_chunk_bytes = 256ll * kChunkElems * 2;      // one chunk of one slab
+    s.wring = (int)std::min<int64_t>(nch, std::max<int64_t>(4, kSlabRingMax / (s.nslot * slab_chunk_bytes)));
+    s.ring_bytes = (int64_t)s.nslot * s.wring * slab_chunk_bytes;
+    s.counter_bytes = ((int64_t)2 * s.nslot * s.wring * 4 + 255) / 256 * 256;
+    s.use = true;
+    return s;
+}
+
+static int launch_gemm_slab(const SlabPlan &pl, const uint8_t *layout, const int32_t *ptile_off,
+                            const uint32_t *precs, int64_t rows, int64_t in_f, const uint16_t *x, int64_t M,
+                            int64_t ldx, const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *ws,
+                            cudaStream_t st) {
+    SlabParams p;
+    p.layout = layout;
+    p.ptile_off = ptile_off;
+    p.precs = precs;
+    p.rows = rows;
+    p.M = M;
+    p.row_bytes = resident_row_bytes(in_f);
+    p.nch = (int)((in_f + kChunkElems - 1) / kChunkElems);
+    p.n_tiles16 = (int)((rows + kTileRows - 1) / kTileRows);
+    p.tiles_n = pl.tiles_n;
+    p.tiles_total = pl.tiles_total;
+    p.npairs = std::min(pl.npairs, pl.tiles_total);
+    p.nslot = pl.nslot;
+    p.wring = pl.wring;
+    uint8_t *base = static_cast<uint8_t *>(ws);
+    p.ready = reinterpret_cast<uint32_t *>(base);
+    p.release = p.ready + (int64_t)pl.nslot * pl.wring;
+    p.ring = reinterpret_cast<uint16_t *>(base + pl.counter_bytes);
+    p.bias = bias;
+    p.y = y;
+    p.y_f32 = y_dtype == BF16X_DTYPE_F32;
+    p.ldy = ldy;
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, 128u};
+    const cuuint32_t estr[2] = {1, 1};
+    const cuuint64_t adims[2] = {(cuuint64_t)pl.wring * kChunkElems, (cuuint64_t)pl.nslot * 256};
+    const cuuint64_t astr[1] = {(cuuint64_t)pl.wring * kChunkElems * 2};
+    if (fn(&p.amap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.ring, adims, astr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return set_error(BF16X_ERR_CUDA, "bf16x_gemm: slab tensor map");
+    const cuuint64_t xdims[2] = {(cuuint64_t)in_f, (cuuint64_t)M};
+    const cuuint64_t xstr[1] = {(cuuint64_t)ldx * 2};
+    if (fn(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), xdims, xstr, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return set_error(BF16X_ERR_CUDA, "bf16x_gemm: activation tensor map");
+    // counters start at zero in every launch
+    cudaError_t e = cudaMemsetAsync(base, 0, (size_t)pl.counter_bytes, st);
+    if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: clearing counters: %s", cudaGetErrorString(e));
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool attr_set[64] = {false};
+    if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: device index");
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(gemm_slab_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SlabCfg::kSmem);
+        if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: smem attribute: %s", cudaGetErrorString(e));
+        attr_set[dev] = true;
+    }
+    // the CTAs wait on one another's progress, so every pair must be resident
+    // at once: no more pairs than clusters of 2 that fit on the device
+    static int max_clusters[64] = {0};
+    if (!max_clusters[dev]) {
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3((unsigned)(2 * pl.npairs));
+        q.blockDim = dim3((unsigned)SlabCfg::kThreads);
+        q.dynamicSmemBytes = SlabCfg::kSmem;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = 2;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        q.attrs = qa;
+        q.numAttrs = 1;
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, gemm_slab_kernel, &q);
+        if (e != cudaSuccess || n < 1)
+            return set_error(BF16X_ERR_CUDA, "bf16x_gemm: cluster occupancy: %s", cudaGetErrorString(e));
+        max_clusters[dev] = n;
+    }
+    p.npairs = std::min(p.npairs, max_clusters[dev]);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * p.npairs));
+    cfg.blockDim = dim3((unsigned)SlabCfg::kThreads);
+    cfg.dynamicSmemBytes = SlabCfg::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, gemm_slab_kernel, p);
+    if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: slab launch: %s", cudaGetErrorString(e));
+    return check_launch("bf16x_gemm");
+}
+
 }  // namespace bf16x
 
 using namespace bf16x;
 
-extern "C" int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
-                          int64_t rows, int64_t in_f, const uint16_t *x, int64_t M, int64_t ldx,
-                          const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream) {
+extern "C" int64_t bf16x_gemm_workspace_bytes(int64_t rows, int64_t in_f, int64_t M) {
+    if (rows <= 0 || in_f <= 0 || M <= 0 || in_f > 65536) return 0;
+    const SlabPlan pl = plan_slab(rows, in_f, M, gemm_sms());
+    return pl.use ? pl.counter_bytes + pl.ring_bytes : 0;
+}
+
+extern "C" int bf16x_gemm_ws(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                             int64_t rows, int64_t in_f, const uint16_t *x, int64_t M, int64_t ldx,
+                             const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *workspace,
+                             int64_t workspace_bytes, void *stream) {
     if (rows < 0 || in_f <= 0 || M < 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemm: bad shape");
     if (in_f > 65536) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: in_f > 65536");
     if (y_dtype != BF16X_DTYPE_BF16 && y_dtype != BF16X_DTYPE_F32)
@@ -990,6 +1474,16 @@ extern "C" int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const
     const int64_t tiles_m = (rows + kGemmBM - 1) / kGemmBM;
     cudaStream_t st = (cudaStream_t)stream;
     const int sms = gemm_sms();
+    if (workspace) {
+        const SlabPlan pl = plan_slab(rows, in_f, M, sms);
+        if (pl.use) {
+            if (workspace_bytes < pl.counter_bytes + pl.ring_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+                return set_error(BF16X_ERR_INVALID, "bf16x_gemm: workspace of %lld bytes (256-byte aligned) needed",
+                                 (long long)(pl.counter_bytes + pl.ring_bytes));
+            return launch_gemm_slab(pl, layout, ptile_off, precs, rows, in_f, x, M, ldx, bias, y, y_dtype, ldy,
+                                    workspace, st);
+        }
+    }
     // token tile: 256 when that still fills the GPU, else smaller
     int bn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
     if (bn == 256 && tiles_m * ((M + 255) / 256) < sms) bn = 128;
@@ -1010,4 +1504,10 @@ extern "C" int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const
     if (bn == 64) return launch_gemm<64>(p, layout, in_f, x, ldx, st);
     if (bn == 128) return launch_gemm<128>(p, layout, in_f, x, ldx, st);
     return launch_gemm<256>(p, layout, in_f, x, ldx, st);
+}
+
+extern "C" int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                          int64_t rows, int64_t in_f, const uint16_t *x, int64_t M, int64_t ldx,
+                          const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream) {
+    return bf16x_gemm_ws(layout, ptile_off, precs, rows, in_f, x, M, ldx, bias, y, y_dtype, ldy, nullptr, 0, stream);
 }

@@ -62,6 +62,21 @@ def gemv_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
     return ws
 
 
+_GEMM_WS: dict = {}
+
+
+def gemm_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Slab-ring workspace of the GEMM for (device, current stream), grown on
+    demand; its contents never need initialising."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream)
+    ws = _GEMM_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _GEMM_WS[key] = ws
+    return ws
+
+
 _ALL_COUNTERS: list = []
 
 
@@ -219,8 +234,11 @@ class ResidentWeight:
         ydt = {torch.bfloat16: BF16X_DTYPE_BF16, torch.float32: BF16X_DTYPE_F32}[out.dtype]
         b = None if bias is None else bias.to(device=self.device, dtype=torch.bfloat16).contiguous()
         with torch.cuda.device(self.device):
-            call("bf16x_gemm", ptr(self.layout), ptr(self.ptile_off), ptr(self.precs), self.rows, self.in_f,
-                 ptr(x2), M, x2.stride(0), ptr(b), ptr(out), ydt, out.stride(0), self._stream())
+            need = int(_lib.lib().bf16x_gemm_workspace_bytes(self.rows, self.in_f, M))
+            ws = gemm_workspace(self.device, need) if need else None
+            call("bf16x_gemm_ws", ptr(self.layout), ptr(self.ptile_off), ptr(self.precs), self.rows, self.in_f,
+                 ptr(x2), M, x2.stride(0), ptr(b), ptr(out), ydt, out.stride(0),
+                 ptr(ws) if ws is not None else None, ws.numel() if ws is not None else 0, self._stream())
         return out
 
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None,
@@ -237,4 +255,5 @@ class ResidentWeight:
         return y.reshape(*x.shape[:-1], self.rows)
 
 
-__all__ = ["ResidentWeight", "flat_on_device", "flat_args", "gemv_scratch", "reset_workspaces", "GEMV_MAX_BATCH"]
+__all__ = ["ResidentWeight", "flat_on_device", "flat_args", "gemv_scratch", "gemm_workspace", "reset_workspaces",
+           "GEMV_MAX_BATCH"]

@@ -182,6 +182,20 @@ int bf16x_gemm(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *
                const uint16_t *x, int64_t M, int64_t ldx,
                const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream);
 
+/* Workspace that lets bf16x_gemm_ws decode each 256-row slab of the weight
+ * once for all token tiles (instead of once per tile): 0 when the shape does
+ * not use it (fewer than 1024 tokens, or fewer tiles than CTA pairs). */
+int64_t bf16x_gemm_workspace_bytes(int64_t rows, int64_t in_f, int64_t M);
+/* bf16x_gemm with a device workspace of bf16x_gemm_workspace_bytes(rows,
+ * in_f, M) bytes, 256-byte aligned, not shared with a call that may run at
+ * the same time; its contents need no initialisation.  NULL: same as
+ * bf16x_gemm. */
+int bf16x_gemm_ws(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                  int64_t rows, int64_t in_f,
+                  const uint16_t *x, int64_t M, int64_t ldx,
+                  const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
+                  void *workspace, int64_t workspace_bytes, void *stream);
+
 /* ---- GGUF BF16X block format (llama.cpp GGML_TYPE_BF16X) --------------- */
 /* 32 weights per 46-byte block: emax[2] (per 16-weight half, floored at 7),
  * sign[4], mant[28], delta[12]; delta 7 is the zero marker.  x_dtype:

@@ -125,3 +125,43 @@ def test_gemm_pair_ragged_vs_oracle(rows, M, dense):
     ref16 = torch.from_numpy(ref).to(torch.bfloat16).float().numpy()
     assert rel_l2(y16, ref16) < GATE
     _lib.check_device_status()
+
+
+# Slab path (bf16x_gemm_ws with a workspace, at least 4 token tiles per
+# 256-row slab): 16 slabs through a ring of 12 slots, and K = 14336 (56
+# chunks) through a 42-chunk window, so slots are reused and windows wrap.
+# x is a permuted one-hot matrix, so every output is one decoded weight and
+# the columns checked span every chunk.
+def test_gemm_slab_permuted_identity():
+    rows, in_f, M = 4096, 14336, 2048
+    assert _lib.lib().bf16x_gemm_workspace_bytes(rows, in_f, M) > 0
+    wb = bits_of(synthetic_weight(rows, in_f, seed=31))
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    cols = (np.arange(M) * 5 + 3) % in_f
+    x = torch.zeros(M, in_f, dtype=torch.bfloat16)
+    x[torch.arange(M), torch.from_numpy(cols)] = 1.0
+    y = rw.gemm(x.cuda(), out_dtype=torch.float32).cpu().numpy()
+    expect = oracle.bf16_bits_to_f32(wb)[:, cols].T
+    assert np.array_equal(y.view(np.uint32), np.ascontiguousarray(expect).view(np.uint32))
+    _lib.check_device_status()
+
+
+# Ragged everywhere on the slab path: 5000 rows (the last slab holds 136
+# rows in 9 tiles), in_f 11000 (ragged last chunk, window wraps), 1500
+# tokens; against the fp32 matmul of the decoded weight (bit-exact decode is
+# pinned by the decode tests), twice for determinism.
+def test_gemm_slab_ragged_vs_torch():
+    rows, in_f, M = 5000, 11000, 1500
+    assert _lib.lib().bf16x_gemm_workspace_bytes(rows, in_f, M) > 0
+    w = synthetic_weight(rows, in_f, seed=37, device="cuda")
+    rw = ResidentWeight.from_packed(oracle_dict(bits_of(w)), device="cuda")
+    assert torch.equal(rw.decode(), w)
+    x = synthetic_activation(M, in_f, seed=41, device="cuda")
+    bias = (torch.randn(rows, generator=torch.Generator().manual_seed(2)) * 0.1).to(torch.bfloat16).cuda()
+    ref = x.float() @ w.float().T + bias.float()
+    y = rw.gemm(x, bias=bias, out_dtype=torch.float32)
+    assert float((y - ref).norm() / ref.norm()) < GATE
+    assert torch.equal(y, rw.gemm(x, bias=bias, out_dtype=torch.float32))
+    y16 = rw.gemm(x, bias=bias, out_dtype=torch.bfloat16).float()
+    assert float((y16 - ref.to(torch.bfloat16).float()).norm() / ref.norm()) < GATE
+    _lib.check_device_status()
