@@ -885,11 +885,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
 //              be overwritten once every token tile of its slab is done).
 // A slot holds a window of `wring` chunks of its slab; chunk c lives at
 // position c % wring.  Every wait is bounded and raises the abort flag and
-// the timeout status instead of hanging.  Slot reuse only waits on token
-// tiles that precede the waiting decoder's tile in the pair-strided tile
-// order, and decode shares belong to a slab's first tiles in that order, so
-// the dependencies cannot form a cycle when all CTAs are resident (the grid
-// never exceeds the SM count, one CTA per SM).
+// the timeout status instead of hanging.  Each pair's decoder warps run
+// through the pair's tiles in order (slab indices only grow) independently
+// of its MMA, and a slot is reused only after slabs that lie about two
+// rounds of pairs earlier (the ring has at least 2 * pairs / tiles-per-slab
+// slots), so by induction on the slab index every wait ends when all CTAs
+// are resident (the grid never exceeds the clusters that fit at once).
 struct SlabCfg {
     static constexpr int kStages = 6;
     static constexpr int kAStage = 128 * 128;       // 16 KB: 128 rows x 64 columns of the slab
@@ -899,10 +900,12 @@ struct SlabCfg {
 #define BF16X_SLAB_DEC 8
 #endif
     static constexpr int kDecWarps = BF16X_SLAB_DEC;
-    static constexpr int kFirstDec = 6;             // warps: producer, MMA, 4 epilogue, decoders
+    static constexpr int kGateWarp = 6;             // warps: producer, MMA, 4 epilogue, gate, decoders
+    static constexpr int kFirstDec = 7;
     static constexpr int kThreads = (kFirstDec + kDecWarps) * 32;
+    static constexpr int kGates = 8;                // chunks the gate may run ahead of the producer
     static constexpr int kBarOff = kStages * kStage;
-    static constexpr int kNumBars = 2 * kStages + 4;
+    static constexpr int kNumBars = 2 * kStages + 4 + 2 * kGates;
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
     static constexpr int kSmem = kMiscOff + 16 + 1024;
     static_assert(kSmem <= 227 * 1024, "shared memory");
@@ -984,18 +987,14 @@ __device__ __forceinline__ uint32_t slab_ready_target(const SlabParams &p, const
     return (uint32_t)(s.gen * per_slab * 16 + (c / p.wring + 1) * s.n16);
 }
 
-// The 16-row tiles [a, b) of its slab that token tile t decodes: a slab is
-// decoded by its token tiles that fall in the first pair-strided round
-// (wave) reaching the slab, its 16-row tiles dealt evenly among them.
+// The 16-row tiles [a, b) of its slab that token tile t decodes: every
+// token tile of a slab decodes an equal share of its 16-row tiles, so the
+// decode work is the same for every tile whatever the wave it falls in.
 __device__ __forceinline__ void slab_share(const SlabParams &p, int t, int &a, int &b) {
     const int rt = t / p.tiles_n, j = t - rt * p.tiles_n;
-    const int first = rt * p.tiles_n;
-    const int wave_end = (first / p.npairs + 1) * p.npairs;
-    const int k = min(p.tiles_n, wave_end - first);
     const int n16 = min(16, p.n_tiles16 - 16 * rt);
-    if (j >= k) { a = b = 0; return; }
-    a = n16 * j / k;
-    b = n16 * (j + 1) / k;
+    a = n16 * j / p.tiles_n;
+    b = n16 * (j + 1) / p.tiles_n;
 }
 
 __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const __grid_constant__ SlabParams p) {
@@ -1005,6 +1004,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
     uint64_t *full = bars, *empty = bars + C::kStages;
     uint64_t *acc_full = bars + 2 * C::kStages, *acc_empty = acc_full + 2;
+    uint64_t *gate_full = acc_empty + 2, *gate_free = gate_full + C::kGates;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1012,6 +1012,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
     const int pair = (int)(blockIdx.x >> 1);
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int g = 0; g < C::kGates; ++g) { mbar_init(&gate_full[g], 1); mbar_init(&gate_free[g], 1); }
         // acc_empty: the 4 epilogue warps of each CTA
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 8); }
         abort_flag[0] = 0;
@@ -1035,20 +1036,20 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
         if (lane == 0) {
             prefetch_tensormap(&p.amap);
             prefetch_tensormap(&p.xmap);
-            int s = 0;
-            uint32_t ph = 0;
+            int s = 0, g = 0;
+            uint32_t ph = 0, gph = 0;
             bool ok = true;
             for (int t = pair; t < p.tiles_total && ok; t += p.npairs) {
                 const SlabTile st = slab_tile(p, t);
                 for (int kb = 0; kb < nkb && ok; ++kb) {
                     const int c = kb >> 2, pos = c % p.wring;
                     if ((kb & 3) == 0) {
-                        // this chunk of the slab decoded by every CTA that shares it
-                        if (!counter_wait(p.ready + st.slot * p.wring + pos, slab_ready_target(p, st, c), abort_flag)) {
-                            ok = false;
-                            break;
-                        }
+                        // this chunk of the slab decoded by every CTA that shares
+                        // it: the gate warp has seen its ready count
+                        if (!role_wait(&gate_full[g], gph, abort_flag)) { ok = false; break; }
                         fence_proxy_async_global();
+                        mbar_arrive(&gate_free[g]);
+                        if (++g == C::kGates) { g = 0; gph ^= 1u; }
                     }
                     if (!role_wait(&empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
                     const uint32_t lb = leader(&full[s]);
@@ -1097,7 +1098,29 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                 if (++ac == 2) { ac = 0; acph ^= 1u; }
             }
         }
-    } else if (warp < C::kFirstDec) {
+    } else if (warp == C::kGateWarp) {
+        // ------------------------------------------------------- gate
+        // Polls the ready counters of the producer's coming chunks (a
+        // global acquire load takes about a microsecond) and passes each
+        // on through a local barrier, so the producer never waits on L2.
+        if (lane == 0) {
+            int g = 0;
+            uint32_t gph = 0;
+            bool ok = true;
+            for (int t = pair; t < p.tiles_total && ok; t += p.npairs) {
+                const SlabTile st = slab_tile(p, t);
+                for (int c = 0; c < p.nch; ++c) {
+                    if (!role_wait(&gate_free[g], gph ^ 1u, abort_flag) ||
+                        !counter_wait(p.ready + st.slot * p.wring + c % p.wring, slab_ready_target(p, st, c), abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive(&gate_full[g]);
+                    if (++g == C::kGates) { g = 0; gph ^= 1u; }
+                }
+            }
+        }
+    } else if (warp < C::kGateWarp) {
         // ------------------------------------------------------- epilogue
         const int qd = warp & 3;                       // TMEM lane quarter
         int ac = 0;
@@ -1162,6 +1185,9 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                 }
                 const int64_t t16 = (int64_t)st.rt * 16 + rtile;
                 uint16_t *dst = p.ring + ((int64_t)st.slot * 256 + rtile * 16) * ld + (int64_t)pos * kChunkElems;
+                // the record's offset first: its header load then overlaps the data's
+                const bool has_rec = t16 < p.n_tiles16;
+                const int32_t roff = has_rec ? __ldg(p.ptile_off + t16 * p.nch + c) : 0;
                 uint32_t sm[4][8], dd[4][3], elo[4], ehi[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
@@ -1175,6 +1201,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                         elo[k] = ehi[k] = 0u;
                     }
                 }
+                const int n_all = has_rec ? (int)(__ldg(p.precs + roff) >> 16) : 0;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     GroupPairs gp;
@@ -1185,11 +1212,9 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                         o[u] = make_uint4(gp.w[4 * u], gp.w[4 * u + 1], gp.w[4 * u + 2], gp.w[4 * u + 3]);
                 }
                 __syncwarp();
-                if (t16 < p.n_tiles16) {
-                    const int32_t off = __ldg(p.ptile_off + t16 * p.nch + c);
-                    const int n_all = (int)(__ldg(p.precs + off) >> 16);
+                if (has_rec) {
                     for (int j = lane; j < n_all; j += 32) {
-                        const uint32_t ent = __ldg(p.precs + off + kRecHdrWords + j);
+                        const uint32_t ent = __ldg(p.precs + roff + kRecHdrWords + j);
                         uint32_t rr, cc;
                         frag_position(ent, rr, cc);
                         dst[(int64_t)rr * ld + cc] = (uint16_t)(ent >> 16);
@@ -1335,7 +1360,7 @@ static SlabPlan plan_slab(int64_t rows, int64_t in_f, int64_t M, int sms) {
 #ifndef BF16X_SLAB_SLACK
 #define BF16X_SLAB_SLACK 1
 #endif
-    s.nslot = (int)std::min<int64_t>(tiles_m2, BF16X_SLAB_SLACK * ((s.npairs + tn - 1) / tn) + 2);
+    s.nslot = (int)std::min<int64_t>(tiles_m2, BF16X_SLAB_SLACK * ((2 * s.npairs + tn - 1) / tn) + 2);
     const int64_t slab_chunk_bytes = 256ll * kChunkElems * 2;      // one chunk of one slab
     s.wring = (int)std::min<int64_t>(nch, std::max<int64_t>(4, kSlabRingMax / (s.nslot * slab_chunk_bytes)));
     s.ring_bytes = (int64_t)s.nslot * s.wring * slab_chunk_bytes;

@@ -1,13 +1,21 @@
 """End-to-end decoder for the BF16X path: a Llama-style model whose linear
 layers (attention and MLP projections and lm_head) are BF16X-packed and run
-through the fused decode+GEMV (one token) and decode+GEMM (prefill) kernels.
+through the fused decode+GEMV (up to 8 tokens) and decode+GEMM (more tokens)
+kernels.
 
 It exists to measure the hot path inside a model: ms per generated token
-against the same model with plain bf16 weights (cuBLAS), at batch 1 after a
-prompt prefill, for the two decoder configurations of the benchmark
-(``CONFIGS``).  Weights are random N(0, 0.02) (no checkpoints); attention
-uses torch's scaled_dot_product_attention over a static KV cache, so one
-decode step has static shapes and is replayed as a CUDA graph.
+against the same model with plain bf16 weights (cuBLAS), after a prompt
+prefill, for the two decoder configurations of the benchmark (``CONFIGS``).
+Weights are random N(0, 0.02) (no checkpoints), drawn per weight from a
+seeded generator so that every tensor-parallel degree builds the same model;
+attention uses torch's scaled_dot_product_attention over a static KV cache,
+so one decode step has static shapes and is replayed as a CUDA graph.
+
+Tensor parallelism (``tp`` ranks of a process group, Megatron pairing): each
+rank holds its query/key/value heads and its slice of the MLP's hidden units
+(rows of the fused qkv and gate/up weights), the matching input columns of
+o_proj and down_proj (partial outputs summed by an all-reduce) and a vocab
+slice of lm_head (logits all-gathered); embeddings and norms are replicated.
 
 """
 from __future__ import annotations
@@ -15,6 +23,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
@@ -69,14 +78,77 @@ def _apply_rope(x, cos, sin):
     return y.to(x.dtype)
 
 
-class Attention(nn.Module):
-    def __init__(self, cfg: LlamaConfig, tp: int = 1):
+def _rand_weight(out_f: int, in_f: int, seed: int, device) -> torch.Tensor:
+    """bf16 N(0, 0.02) weight [out_f, in_f] from its own seeded generator."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(out_f, in_f, generator=g, device=device, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+
+
+def _linear_from(w: torch.Tensor) -> nn.Linear:
+    lin = nn.Linear(w.shape[1], w.shape[0], bias=False, device=w.device, dtype=w.dtype)
+    lin.weight.data = w.contiguous()
+    return lin
+
+
+class ColumnShard(nn.Module):
+    """The input-column slice of a linear: this rank's partial outputs,
+    summed over the group (fp32 all-reduce)."""
+
+    def __init__(self, lin: nn.Module, group=None, tp: int = 1):
         super().__init__()
+        self.lin, self.group, self.tp = lin, group, tp
+
+    def forward(self, x):
+        y = self.lin(x)
+        if self.tp == 1:
+            return y
+        acc = y.float()
+        dist.all_reduce(acc, group=self.group)
+        return acc.to(y.dtype)
+
+
+class VocabShard(nn.Module):
+    """Rows [r0, r1) of lm_head on this rank; the logits of all ranks are
+    all-gathered (equal pieces of ``piece`` rows, the last one padded)."""
+
+    def __init__(self, lin: nn.Module, vocab: int, piece: int, group=None, tp: int = 1):
+        super().__init__()
+        self.lin, self.vocab, self.piece, self.group, self.tp = lin, vocab, piece, group, tp
+
+    def forward(self, x):
+        y = self.lin(x)
+        if self.tp == 1:
+            return y
+        y2 = y.reshape(-1, y.shape[-1])
+        buf = torch.zeros((y2.shape[0], self.piece), dtype=y2.dtype, device=y2.device)
+        buf[:, : y2.shape[1]] = y2
+        out = torch.empty((self.tp * y2.shape[0], self.piece), dtype=y2.dtype, device=y2.device)
+        dist.all_gather_into_tensor(out, buf, group=self.group)
+        full = out.view(self.tp, y2.shape[0], self.piece).permute(1, 0, 2).reshape(y2.shape[0], -1)
+        return full[:, : self.vocab].reshape(*y.shape[:-1], self.vocab)
+
+
+def _vocab_piece(vocab: int, tp: int) -> int:
+    return (vocab + tp - 1) // tp
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: LlamaConfig, layer: int, seed: int, device, tp: int = 1, rank: int = 0, group=None):
+        super().__init__()
+        if cfg.heads % tp or cfg.kv_heads % tp:
+            raise ValueError("heads and kv_heads must divide by the tensor-parallel degree")
         self.cfg, self.tp = cfg, tp
         self.h, self.kvh, self.d = cfg.heads // tp, cfg.kv_heads // tp, cfg.head_dim
-        # q, k and v projections as one [q; k; v] weight: one GEMV per step
-        self.qkv_proj = nn.Linear(cfg.hidden, (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim, bias=False)
-        self.o_proj = nn.Linear(cfg.heads * cfg.head_dim, cfg.hidden, bias=False)
+        d, H, KV = cfg.head_dim, cfg.heads, cfg.kv_heads
+        # q, k and v projections as one [q; k; v] weight (this rank's heads): one GEMV per step
+        w = _rand_weight((H + 2 * KV) * d, cfg.hidden, seed + 1000 * layer + 1, device)
+        q = w[rank * self.h * d:(rank + 1) * self.h * d]
+        k = w[H * d + rank * self.kvh * d:H * d + (rank + 1) * self.kvh * d]
+        v = w[(H + KV) * d + rank * self.kvh * d:(H + KV) * d + (rank + 1) * self.kvh * d]
+        self.qkv_proj = _linear_from(torch.cat([q, k, v]))
+        del w
+        w = _rand_weight(cfg.hidden, H * d, seed + 1000 * layer + 2, device)
+        self.o_proj = ColumnShard(_linear_from(w[:, rank * self.h * d:(rank + 1) * self.h * d]), group, tp)
 
     def forward(self, x, pos0, cache_k, cache_v, cos, sin, mask):
         B, T, _ = x.shape
@@ -97,12 +169,18 @@ class Attention(nn.Module):
 
 
 class MLP(nn.Module):
-    def __init__(self, cfg: LlamaConfig, tp: int = 1):
+    def __init__(self, cfg: LlamaConfig, layer: int, seed: int, device, tp: int = 1, rank: int = 0, group=None):
         super().__init__()
-        # gate and up projections as one [gate; up] weight
-        self.ffn = cfg.ffn
-        self.gate_up_proj = nn.Linear(cfg.hidden, 2 * cfg.ffn, bias=False)
-        self.down_proj = nn.Linear(cfg.ffn, cfg.hidden, bias=False)
+        if cfg.ffn % tp:
+            raise ValueError("ffn must divide by the tensor-parallel degree")
+        self.ffn = cfg.ffn // tp
+        f0, f1 = rank * self.ffn, (rank + 1) * self.ffn
+        # gate and up projections as one [gate; up] weight (this rank's hidden units)
+        w = _rand_weight(2 * cfg.ffn, cfg.hidden, seed + 1000 * layer + 3, device)
+        self.gate_up_proj = _linear_from(torch.cat([w[f0:f1], w[cfg.ffn + f0:cfg.ffn + f1]]))
+        del w
+        w = _rand_weight(cfg.hidden, cfg.ffn, seed + 1000 * layer + 4, device)
+        self.down_proj = ColumnShard(_linear_from(w[:, f0:f1]), group, tp)
 
     def forward(self, x):
         gu = self.gate_up_proj(x)
@@ -110,12 +188,12 @@ class MLP(nn.Module):
 
 
 class Block(nn.Module):
-    def __init__(self, cfg: LlamaConfig, tp: int = 1):
+    def __init__(self, cfg: LlamaConfig, layer: int, seed: int, device, tp: int = 1, rank: int = 0, group=None):
         super().__init__()
         self.input_layernorm = RMSNorm(cfg.hidden, cfg.eps)
-        self.self_attn = Attention(cfg, tp)
+        self.self_attn = Attention(cfg, layer, seed, device, tp, rank, group)
         self.post_attention_layernorm = RMSNorm(cfg.hidden, cfg.eps)
-        self.mlp = MLP(cfg, tp)
+        self.mlp = MLP(cfg, layer, seed, device, tp, rank, group)
 
     def forward(self, x, pos0, ck, cv, cos, sin, mask):
         x = x + self.self_attn(self.input_layernorm(x), pos0, ck, cv, cos, sin, mask)
@@ -123,32 +201,40 @@ class Block(nn.Module):
 
 
 class LlamaModel(nn.Module):
-    """Llama-style decoder with a static KV cache of ``max_seq`` positions."""
+    """Llama-style decoder with a static KV cache of ``max_seq`` positions for
+    ``batch`` sequences; ``tp`` > 1 builds this rank's shard (``group``: the
+    tensor-parallel process group, default the world)."""
 
-    def __init__(self, cfg: LlamaConfig, max_seq: int, device, seed: int = 0, tp: int = 1):
+    def __init__(self, cfg: LlamaConfig, max_seq: int, device, seed: int = 0, tp: int = 1, group=None,
+                 batch: int = 1):
         super().__init__()
-        if tp != 1:
-            raise NotImplementedError("the end-to-end decoder runs on one GPU")
-        self.cfg, self.max_seq, self.tp = cfg, max_seq, tp
-        self.embed_tokens = nn.Embedding(cfg.vocab, cfg.hidden)
-        self.layers = nn.ModuleList([Block(cfg, tp) for _ in range(cfg.layers)])
+        device = torch.device(device)
+        rank = dist.get_rank(group) if tp > 1 else 0
+        if tp > 1 and dist.get_world_size(group) != tp:
+            raise ValueError("tp must equal the size of the process group")
+        self.cfg, self.max_seq, self.tp, self.batch = cfg, max_seq, tp, batch
+        self.embed_tokens = nn.Embedding(cfg.vocab, cfg.hidden, device=device, dtype=torch.bfloat16)
+        self.embed_tokens.weight.data = _rand_weight(cfg.vocab, cfg.hidden, seed + 7, device)
+        self.layers = nn.ModuleList([Block(cfg, i, seed, device, tp, rank, group) for i in range(cfg.layers)])
         self.norm = RMSNorm(cfg.hidden, cfg.eps)
-        self.lm_head = nn.Linear(cfg.hidden, cfg.vocab, bias=False)
-        self.to(device=device, dtype=torch.bfloat16)
-        gd = torch.Generator(device=device).manual_seed(seed)
-        with torch.no_grad():
-            for p in self.parameters():
-                if p.dim() == 2:
-                    p.normal_(0.0, 0.02, generator=gd)
+        w = _rand_weight(cfg.vocab, cfg.hidden, seed + 11, device)
+        piece = _vocab_piece(cfg.vocab, tp)
+        self.lm_head = VocabShard(_linear_from(w[rank * piece:min((rank + 1) * piece, cfg.vocab)]), cfg.vocab, piece,
+                                  group, tp)
+        del w
+        self.norm.to(device)
+        for blk in self.layers:
+            blk.input_layernorm.to(device)
+            blk.post_attention_layernorm.to(device)
         self.cos, self.sin = _rope_tables(cfg.head_dim, max_seq, cfg.rope_theta, device)
         kvh = cfg.kv_heads // tp
-        self.cache_k = torch.zeros(cfg.layers, 1, max_seq, kvh, cfg.head_dim, dtype=torch.bfloat16, device=device)
+        self.cache_k = torch.zeros(cfg.layers, batch, max_seq, kvh, cfg.head_dim, dtype=torch.bfloat16, device=device)
         self.cache_v = torch.zeros_like(self.cache_k)
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, pos0: torch.Tensor) -> torch.Tensor:
-        """ids [1, T] at positions pos0 .. pos0+T-1 (pos0: 0-d int64 device
-        tensor); returns logits of the last position [1, vocab]."""
+        """ids [batch, T] at positions pos0 .. pos0+T-1 (pos0: 0-d int64 device
+        tensor); returns logits of the last position [batch, vocab]."""
         T = ids.shape[1]
         x = self.embed_tokens(ids)
         pos = pos0 + torch.arange(T, device=ids.device)
@@ -158,7 +244,7 @@ class LlamaModel(nn.Module):
         for i, blk in enumerate(self.layers):
             x = blk(x, pos0, self.cache_k[i], self.cache_v[i], cos, sin, mask)
         h = self.norm(x[:, -1:, :])
-        return self.lm_head(h).float().reshape(1, -1)
+        return self.lm_head(h).float().reshape(ids.shape[0], -1)
 
 
 class ResidentLinear(nn.Module):
@@ -202,14 +288,14 @@ class GraphDecoder:
     CUDA graph and replayed; the position lives in a device tensor."""
 
     def __init__(self, model: LlamaModel, tok: torch.Tensor, pos: int):
-        """tok [1, 1]: the first token to feed, at position ``pos``.  The
+        """tok [batch, 1]: the first tokens to feed, at position ``pos``.  The
         warm-up and capture write the cache row at ``pos`` only, which the
         first replay writes again."""
         self.model = model
         dev = model.cache_k.device
-        self.tok = tok.reshape(1, 1).clone()
+        self.tok = tok.reshape(-1, 1).clone()
         self.pos = torch.tensor(pos, dtype=torch.long, device=dev)
-        self.next = torch.zeros(1, 1, dtype=torch.long, device=dev)
+        self.next = torch.zeros_like(self.tok)
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
@@ -233,8 +319,9 @@ class GraphDecoder:
 
 @torch.no_grad()
 def generate(model: LlamaModel, prompt: torch.Tensor, new_tokens: int, use_graph: bool = True):
-    """Greedy generation: prefill ``prompt`` [1, P], then ``new_tokens``
-    decode steps.  Returns (tokens [new_tokens], prefill ms, decode ms/token)."""
+    """Greedy generation: prefill ``prompt`` [batch, P], then ``new_tokens``
+    decode steps.  Returns (tokens [new_tokens, batch], prefill ms, decode
+    ms/token)."""
     dev = prompt.device
     P = prompt.shape[1]
     pos0 = torch.zeros((), dtype=torch.long, device=dev)
@@ -262,7 +349,8 @@ def generate(model: LlamaModel, prompt: torch.Tensor, new_tokens: int, use_graph
             pos = pos + 1
         b.record()
     torch.cuda.synchronize(dev)
-    return torch.cat(out).reshape(-1), prefill_ms, a.elapsed_time(b) / max(new_tokens, 1)
+    return torch.cat(out, dim=1).t().contiguous(), prefill_ms, a.elapsed_time(b) / max(new_tokens, 1)
 
 
-__all__ = ["LlamaConfig", "CONFIGS", "LlamaModel", "ResidentLinear", "pack_model", "GraphDecoder", "generate"]
+__all__ = ["LlamaConfig", "CONFIGS", "LlamaModel", "ColumnShard", "VocabShard", "ResidentLinear", "pack_model",
+           "GraphDecoder", "generate"]
