@@ -891,18 +891,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
 // rounds of pairs earlier (the ring has at least 2 * pairs / tiles-per-slab
 // slots), so by induction on the slab index every wait ends when all CTAs
 // are resident (the grid never exceeds the clusters that fit at once).
+#ifndef BF16X_SLAB_STAGES
+#define BF16X_SLAB_STAGES 6
+#endif
 struct SlabCfg {
-    static constexpr int kStages = 6;
+    static constexpr int kStages = BF16X_SLAB_STAGES;
     static constexpr int kAStage = 128 * 128;       // 16 KB: 128 rows x 64 columns of the slab
     static constexpr int kBStage = 128 * 128;       // 16 KB: this CTA's 128 tokens x 64 columns
     static constexpr int kStage = kAStage + kBStage;
-#ifndef BF16X_SLAB_DEC
-#define BF16X_SLAB_DEC 8
-#endif
-    static constexpr int kDecWarps = BF16X_SLAB_DEC;
-    static constexpr int kGateWarp = 6;             // warps: producer, MMA, 4 epilogue, gate, decoders
-    static constexpr int kFirstDec = 7;
-    static constexpr int kThreads = (kFirstDec + kDecWarps) * 32;
+    // Warp roles, by warp index (a warp runs on sub-partition index % 4):
+    // the MMA issuer shares its sub-partition only with the epilogue warp
+    // of its TMEM lane quarter and two idle warps, away from the decoders.
+    //   0 producer, 1 gate, 3 MMA issuer, 4..7 epilogue (lane quarter = index % 4),
+    //   2, 8, 9, 10, 12, 13, 14 decoders, 11 and 15 idle.
+    static constexpr int kWarps = 16;
+    static constexpr int kThreads = kWarps * 32;
+    static constexpr int kDecWarps = 7;
+    static constexpr int kProducerWarp = 0, kGateWarp = 1, kMmaWarp = 3, kFirstEpi = 4;
+    __host__ __device__ static constexpr int dec_index(int w) {
+        return w == 2 ? 0 : (w >= 8 && w <= 10) ? w - 7 : (w >= 12 && w <= 14) ? w - 8 : -1;
+    }
     static constexpr int kGates = 8;                // chunks the gate may run ahead of the producer
     static constexpr int kBarOff = kStages * kStage;
     static constexpr int kNumBars = 2 * kStages + 4 + 2 * kGates;
@@ -951,6 +959,23 @@ __device__ __forceinline__ bool counter_wait(const uint32_t *ctr, uint32_t targe
             return false;
         }
     }
+}
+
+// load_group for the compressed weight in global memory, read once per
+// launch: evict-first loads, so the stream of compressed weights does not
+// push the decoded slabs and the activations (re-read by every tile) out of
+// L2.
+__device__ __forceinline__ void load_group_stream(const uint8_t *chunk, int q, uint32_t (&sm)[8], uint32_t (&dw)[3],
+                                                  uint32_t &e2lo, uint32_t &e2hi) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4 *>(chunk + kSmOff + 32 * q));
+    const uint4 b = __ldcs(reinterpret_cast<const uint4 *>(chunk + kSmOff + 32 * q + 16));
+    sm[0] = a.x; sm[1] = a.y; sm[2] = a.z; sm[3] = a.w;
+    sm[4] = b.x; sm[5] = b.y; sm[6] = b.z; sm[7] = b.w;
+    const uint32_t *d = reinterpret_cast<const uint32_t *>(chunk + kDOff + 12 * q);
+    dw[0] = __ldcs(d); dw[1] = __ldcs(d + 1); dw[2] = __ldcs(d + 2);
+    const uint32_t e = __ldcs(reinterpret_cast<const uint16_t *>(chunk + kEOff + 2 * q));
+    e2lo = (e & 0xFFu) * 0x00800080u;
+    e2hi = (e >> 8) * 0x00800080u;
 }
 
 // Slab geometry shared by all roles.
@@ -1019,7 +1044,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
         fence_mbar_init();
     }
     cluster_sync_all();
-    if (warp == 1) {
+    if (warp == C::kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_u32(tmem_slot)), "r"(512) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
@@ -1031,7 +1056,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
     const uint32_t tmem_base = *tmem_slot;
     const int nkb = p.nch * 4;
 
-    if (warp == 0) {
+    if (warp == C::kProducerWarp) {
         // ------------------------------------------------------- producer
         if (lane == 0) {
             prefetch_tensormap(&p.amap);
@@ -1055,14 +1080,14 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                     const uint32_t lb = leader(&full[s]);
                     if (rank == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * C::kStage));
                     uint8_t *stg = smem + s * C::kStage;
-                    tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
+tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
                                      st.slot * 256 + (int)rank * 128, lb);
                     tma_load_2d_pair(stg + C::kAStage, &p.xmap, kb * kGemmBK, st.nt * 256 + (int)rank * 128, lb);
                     if (++s == C::kStages) { s = 0; ph ^= 1u; }
                 }
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == C::kMmaWarp) {
         // ------------------------------------------------------- MMA issuer
         if (lane == 0 && rank == 0) {
             constexpr uint32_t idesc = umma_idesc_bf16_m<256, 256>();
@@ -1120,7 +1145,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                 }
             }
         }
-    } else if (warp < C::kGateWarp) {
+    } else if (warp >= C::kFirstEpi && warp < C::kFirstEpi + 4) {
         // ------------------------------------------------------- epilogue
         const int qd = warp & 3;                       // TMEM lane quarter
         int ac = 0;
@@ -1141,7 +1166,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                         const int64_t n = (int64_t)st.nt * 256 + c0 + i;
                         if (n < p.M) {
                             const float o = __uint_as_float(v[i]) + bias;
-                            if (p.y_f32) reinterpret_cast<float *>(p.y)[n * p.ldy + row] = o;
+if (p.y_f32) reinterpret_cast<float *>(p.y)[n * p.ldy + row] = o;
                             else reinterpret_cast<uint16_t *>(p.y)[n * p.ldy + row] = f32_to_bf16_bits_rn(o);
                         }
                     }
@@ -1155,13 +1180,13 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
             }
             if (++ac == 2) { ac = 0; acph ^= 1u; }
         }
-    } else {
+    } else if (C::dec_index(warp) >= 0) {
         // ------------------------------------------------------- decoders
         // An item is one 16-row tile x one chunk: lane (q = lane & 7, r =
         // lane >> 3) decodes group q (32 columns) of rows r, r+4, r+8, r+12
         // and stores them as bf16 into the slab ring; the item's patch
         // entries are then written over their saturated values.
-        const int dw = warp - C::kFirstDec;
+        const int dw = C::dec_index(warp);
         const int q = lane & 7, r0 = lane >> 3;
         const int64_t ld = (int64_t)p.wring * kChunkElems;
         bool ok = true;
@@ -1193,7 +1218,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                 for (int k = 0; k < 4; ++k) {
                     const int64_t row = t16 * 16 + r0 + 4 * k;
                     if (row < p.rows) {
-                        load_group(p.layout + row * p.row_bytes + (int64_t)c * kChunkBytes, q, sm[k], dd[k], elo[k], ehi[k]);
+                        load_group_stream(p.layout + row * p.row_bytes + (int64_t)c * kChunkBytes, q, sm[k], dd[k], elo[k], ehi[k]);
                     } else {
 #pragma unroll
                         for (int u = 0; u < 8; ++u) sm[k][u] = 0u;
@@ -1214,7 +1239,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                 __syncwarp();
                 if (has_rec) {
                     for (int j = lane; j < n_all; j += 32) {
-                        const uint32_t ent = __ldg(p.precs + roff + kRecHdrWords + j);
+                        const uint32_t ent = __ldcs(p.precs + roff + kRecHdrWords + j);
                         uint32_t rr, cc;
                         frag_position(ent, rr, cc);
                         dst[(int64_t)rr * ld + cc] = (uint16_t)(ent >> 16);
@@ -1235,7 +1260,7 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
     tc_fence_before();
     __syncthreads();
     cluster_sync_all();
-    if (warp == 1) {
+    if (warp == C::kMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(tmem_base), "r"(512) : "memory");
     }
