@@ -891,13 +891,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
 // rounds of pairs earlier (the ring has at least 2 * pairs / tiles-per-slab
 // slots), so by induction on the slab index every wait ends when all CTAs
 // are resident (the grid never exceeds the clusters that fit at once).
-#ifndef BF16X_SLAB_STAGES
-#define BF16X_SLAB_STAGES 6
-#endif
+//
+// NH = 256-token halves per tile.  NH = 1: tiles of 256 rows x 256 tokens,
+// two accumulators in tensor memory (the epilogue of one tile overlaps the
+// next tile's MMAs).  NH = 2: tiles of 256 rows x 512 tokens, each staged
+// slab k-block feeding two N=256 MMAs (a quarter less L2 traffic per flop);
+// the one 512-column accumulator is handed back to the MMA issuer in two
+// halves, so the next tile's first MMAs only wait for the first half of the
+// epilogue.
+template <int NH>
 struct SlabCfg {
-    static constexpr int kStages = BF16X_SLAB_STAGES;
+    static constexpr int kStages = NH == 1 ? 6 : 4;
     static constexpr int kAStage = 128 * 128;       // 16 KB: 128 rows x 64 columns of the slab
-    static constexpr int kBStage = 128 * 128;       // 16 KB: this CTA's 128 tokens x 64 columns
+    static constexpr int kBHalf = 128 * 128;        // 16 KB: this CTA's 128 tokens of a half x 64 columns
+    static constexpr int kBStage = NH * kBHalf;
     static constexpr int kStage = kAStage + kBStage;
     // Warp roles, by warp index (a warp runs on sub-partition index % 4):
     // the MMA issuer shares its sub-partition only with the epilogue warp
@@ -1022,8 +1029,10 @@ __device__ __forceinline__ void slab_share(const SlabParams &p, int t, int &a, i
     b = n16 * (j + 1) / p.tiles_n;
 }
 
-__global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const __grid_constant__ SlabParams p) {
-    using C = SlabCfg;
+template <int NH>
+__global__ void __launch_bounds__(SlabCfg<NH>::kThreads, 1) gemm_slab_kernel(const __grid_constant__ SlabParams p) {
+    using C = SlabCfg<NH>;
+    constexpr int BN = 256 * NH;                   // tokens per tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
@@ -1082,7 +1091,10 @@ __global__ void __launch_bounds__(SlabCfg::kThreads, 1) gemm_slab_kernel(const _
                     uint8_t *stg = smem + s * C::kStage;
 tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
                                      st.slot * 256 + (int)rank * 128, lb);
-                    tma_load_2d_pair(stg + C::kAStage, &p.xmap, kb * kGemmBK, st.nt * 256 + (int)rank * 128, lb);
+#pragma unroll
+                    for (int j = 0; j < NH; ++j)
+                        tma_load_2d_pair(stg + C::kAStage + j * C::kBHalf, &p.xmap, kb * kGemmBK,
+                                         st.nt * BN + 256 * j + (int)rank * 128, lb);
                     if (++s == C::kStages) { s = 0; ph ^= 1u; }
                 }
             }
@@ -1096,8 +1108,10 @@ tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
             bool ok = true;
             for (int t = pair; t < p.tiles_total && ok; t += p.npairs) {
                 const SlabTile st = slab_tile(p, t);
-                if (!role_wait(&acc_empty[ac], acph ^ 1u, abort_flag)) break;
-                tc_fence_after();
+                if constexpr (NH == 1) {
+                    if (!role_wait(&acc_empty[ac], acph ^ 1u, abort_flag)) break;
+                    tc_fence_after();
+                }
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ac * 256);
                 for (int kb = 0; kb < nkb; ++kb) {
                     if (!role_wait(&full[s], ph, abort_flag)) { ok = false; break; }
@@ -1109,10 +1123,19 @@ tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
                     }
                     const uint8_t *stg = smem + s * C::kStage;
                     const uint64_t ad = umma_desc_sw128(smem_u32(stg));
-                    const uint64_t bd = umma_desc_sw128(smem_u32(stg + C::kAStage));
 #pragma unroll
-                    for (int k16 = 0; k16 < kGemmBK / 16; ++k16)
-                        umma_bf16_pair(d_tmem, ad + 2u * k16, bd + 2u * k16, idesc, (kb | k16) != 0);
+                    for (int j = 0; j < NH; ++j) {
+                        if (NH == 2 && kb == 0) {
+                            // the epilogue has drained this half of the accumulator
+                            if (!role_wait(&acc_empty[j], acph ^ 1u, abort_flag)) { ok = false; break; }
+                            tc_fence_after();
+                        }
+                        const uint64_t bd = umma_desc_sw128(smem_u32(stg + C::kAStage + j * C::kBHalf));
+#pragma unroll
+                        for (int k16 = 0; k16 < kGemmBK / 16; ++k16)
+                            umma_bf16_pair(d_tmem + 256u * j, ad + 2u * k16, bd + 2u * k16, idesc, (kb | k16) != 0);
+                    }
+                    if (!ok) break;
                     umma_commit_pair(smem_u32(&empty[s]));
                     umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1u));
                     if (++s == C::kStages) { s = 0; ph ^= 1u; }
@@ -1120,7 +1143,11 @@ tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
                 if (!ok) break;
                 umma_commit_pair(smem_u32(&acc_full[ac]));
                 umma_commit_pair(mapa_shared(smem_u32(&acc_full[ac]), 1u));
-                if (++ac == 2) { ac = 0; acph ^= 1u; }
+                if (NH == 1) {
+                    if (++ac == 2) { ac = 0; acph ^= 1u; }
+                } else {
+                    acph ^= 1u;
+                }
             }
         }
     } else if (warp == C::kGateWarp) {
@@ -1157,13 +1184,22 @@ tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
             const int64_t row = (int64_t)st.rt * 256 + (int64_t)rank * 128 + 32 * qd + lane;
             const float bias = (p.bias && row < p.rows) ? bf16_bits_to_f32(__ldg(p.bias + row)) : 0.f;
 #pragma unroll 1
-            for (int c0 = 0; c0 < 256; c0 += 16) {
+            for (int c0 = 0; c0 < BN; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem_base + ((uint32_t)(32 * qd) << 16) + (uint32_t)(ac * 256 + c0), v);
+                if (NH == 2 && c0 == 256 - 16) {
+                    // first half drained: hand it back to the MMA issuer
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (rank == 0) mbar_arrive(&acc_empty[0]);
+                        else mbar_arrive_cluster(leader(&acc_empty[0]));
+                    }
+                }
                 if (row < p.rows) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const int64_t n = (int64_t)st.nt * 256 + c0 + i;
+                        const int64_t n = (int64_t)st.nt * BN + c0 + i;
                         if (n < p.M) {
                             const float o = __uint_as_float(v[i]) + bias;
 if (p.y_f32) reinterpret_cast<float *>(p.y)[n * p.ldy + row] = o;
@@ -1175,10 +1211,15 @@ if (p.y_f32) reinterpret_cast<float *>(p.y)[n * p.ldy + row] = o;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                if (rank == 0) mbar_arrive(&acc_empty[ac]);
-                else mbar_arrive_cluster(leader(&acc_empty[ac]));
+                uint64_t *bar = &acc_empty[NH == 1 ? ac : 1];
+                if (rank == 0) mbar_arrive(bar);
+                else mbar_arrive_cluster(leader(bar));
             }
-            if (++ac == 2) { ac = 0; acph ^= 1u; }
+            if (NH == 1) {
+                if (++ac == 2) { ac = 0; acph ^= 1u; }
+            } else {
+                acph ^= 1u;
+            }
         }
     } else if (C::dec_index(warp) >= 0) {
         // ------------------------------------------------------- decoders
@@ -1364,6 +1405,7 @@ static int launch_gemm2sm(GemmParams &p, const uint8_t *layout, int64_t in_f, co
 // whole K, so that it stays well inside L2.
 struct SlabPlan {
     bool use;
+    int nh;                                         // 256-token halves per tile (1 or 2)
     int npairs, tiles_n, tiles_total, nslot, wring;
     int64_t ring_bytes, counter_bytes;
 };
@@ -1373,13 +1415,28 @@ struct SlabPlan {
 #endif
 constexpr int64_t kSlabRingMax = (int64_t)BF16X_SLAB_RING_MB << 20;
 
+#ifndef BF16X_SLAB_WIDE
+#define BF16X_SLAB_WIDE 1
+#endif
 static SlabPlan plan_slab(int64_t rows, int64_t in_f, int64_t M, int sms) {
     SlabPlan s = {};
     const int64_t nch = (in_f + kChunkElems - 1) / kChunkElems;
     const int64_t tiles_m2 = (rows + 255) / 256;
-    const int64_t tn = (M + 255) / 256;
     s.npairs = std::max(1, sms / 2);
-    if (tn < 4 || tiles_m2 * tn < s.npairs || tiles_m2 * tn > 0x7fffffffLL) return s;
+    // 512-token tiles move a quarter less data per flop but expose half an
+    // epilogue per tile; measured, they pay for long K only (K >= 8192), and
+    // then only when their last round of pairs is not much emptier than with
+    // 256-token tiles (wave efficiency x 1.15 against wave efficiency)
+    auto wave_eff = [&](int64_t tiles) {
+        return (double)tiles / (double)(((tiles + s.npairs - 1) / s.npairs) * s.npairs);
+    };
+    const int64_t tn1 = (M + 255) / 256, tn2 = (M + 511) / 512;
+    const bool ok1 = tn1 >= 4 && tiles_m2 * tn1 >= s.npairs;
+    const bool ok2 = BF16X_SLAB_WIDE && nch >= 32 && tn2 >= 2 && tiles_m2 * tn2 >= s.npairs;
+    if (!ok1 && !ok2) return s;
+    s.nh = (ok2 && (!ok1 || 1.15 * wave_eff(tiles_m2 * tn2) >= wave_eff(tiles_m2 * tn1))) ? 2 : 1;
+    const int64_t tn = s.nh == 2 ? tn2 : tn1;
+    if (tiles_m2 * tn > 0x7fffffffLL) return s;
     s.tiles_n = (int)tn;
     s.tiles_total = (int)(tiles_m2 * tn);
 #ifndef BF16X_SLAB_SLACK
@@ -1437,24 +1494,28 @@ static int launch_gemm_slab(const SlabPlan &pl, const uint8_t *layout, const int
         return set_error(BF16X_ERR_CUDA, "bf16x_gemm: activation tensor map");
     // counters start at zero in every launch
     cudaError_t e = cudaMemsetAsync(base, 0, (size_t)pl.counter_bytes, st);
+    void (*kern)(SlabParams) = pl.nh == 2 ? gemm_slab_kernel<2> : gemm_slab_kernel<1>;
+    const int smem_bytes = pl.nh == 2 ? SlabCfg<2>::kSmem : SlabCfg<1>::kSmem;
+    const int threads = SlabCfg<1>::kThreads;
     if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: clearing counters: %s", cudaGetErrorString(e));
     int dev = 0;
     cudaGetDevice(&dev);
-    static bool attr_set[64] = {false};
+    static bool attr_set[64][2] = {};
     if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: device index");
-    if (!attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_slab_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SlabCfg::kSmem);
+    const int vi = pl.nh - 1;
+    if (!attr_set[dev][vi]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
         if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: smem attribute: %s", cudaGetErrorString(e));
-        attr_set[dev] = true;
+        attr_set[dev][vi] = true;
     }
     // the CTAs wait on one another's progress, so every pair must be resident
     // at once: no more pairs than clusters of 2 that fit on the device
-    static int max_clusters[64] = {0};
-    if (!max_clusters[dev]) {
+    static int max_clusters[64][2] = {};
+    if (!max_clusters[dev][vi]) {
         cudaLaunchConfig_t q = {};
         q.gridDim = dim3((unsigned)(2 * pl.npairs));
-        q.blockDim = dim3((unsigned)SlabCfg::kThreads);
-        q.dynamicSmemBytes = SlabCfg::kSmem;
+        q.blockDim = dim3((unsigned)threads);
+        q.dynamicSmemBytes = smem_bytes;
         cudaLaunchAttribute qa[1];
         qa[0].id = cudaLaunchAttributeClusterDimension;
         qa[0].val.clusterDim.x = 2;
@@ -1463,16 +1524,16 @@ static int launch_gemm_slab(const SlabPlan &pl, const uint8_t *layout, const int
         q.attrs = qa;
         q.numAttrs = 1;
         int n = 0;
-        e = cudaOccupancyMaxActiveClusters(&n, gemm_slab_kernel, &q);
+        e = cudaOccupancyMaxActiveClusters(&n, kern, &q);
         if (e != cudaSuccess || n < 1)
             return set_error(BF16X_ERR_CUDA, "bf16x_gemm: cluster occupancy: %s", cudaGetErrorString(e));
-        max_clusters[dev] = n;
+        max_clusters[dev][vi] = n;
     }
-    p.npairs = std::min(p.npairs, max_clusters[dev]);
+    p.npairs = std::min(p.npairs, max_clusters[dev][vi]);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * p.npairs));
-    cfg.blockDim = dim3((unsigned)SlabCfg::kThreads);
-    cfg.dynamicSmemBytes = SlabCfg::kSmem;
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1481,7 +1542,7 @@ static int launch_gemm_slab(const SlabPlan &pl, const uint8_t *layout, const int
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, gemm_slab_kernel, p);
+    e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: slab launch: %s", cudaGetErrorString(e));
     return check_launch("bf16x_gemm");
 }

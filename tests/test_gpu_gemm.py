@@ -165,3 +165,21 @@ def test_gemm_slab_ragged_vs_torch():
     y16 = rw.gemm(x, bias=bias, out_dtype=torch.bfloat16).float()
     assert float((y16 - ref.to(torch.bfloat16).float()).norm() / ref.norm()) < GATE
     _lib.check_device_status()
+
+
+# Slab path with 512-token tiles (two N=256 MMAs per staged k-block, the
+# accumulator handed back in halves; chosen for K >= 8192): 4500 rows (the
+# last slab holds 148 rows), in_f 8300 (ragged last chunk), 4200 tokens (the
+# last tile holds 104, all in the first half of the leader CTA).
+def test_gemm_slab_wide_ragged_vs_torch():
+    rows, in_f, M = 4500, 8300, 4200
+    assert _lib.lib().bf16x_gemm_workspace_bytes(rows, in_f, M) > 0
+    w = synthetic_weight(rows, in_f, seed=43, device="cuda")
+    rw = ResidentWeight.from_packed(oracle_dict(bits_of(w)), device="cuda")
+    x = synthetic_activation(M, in_f, seed=47, device="cuda")
+    bias = (torch.randn(rows, generator=torch.Generator().manual_seed(3)) * 0.1).to(torch.bfloat16).cuda()
+    ref = x.float() @ w.float().T + bias.float()
+    y = rw.gemm(x, bias=bias, out_dtype=torch.float32)
+    assert float((y - ref).norm() / ref.norm()) < GATE
+    assert torch.equal(y, rw.gemm(x, bias=bias, out_dtype=torch.float32))
+    _lib.check_device_status()
