@@ -1,6 +1,7 @@
 """Tensor-parallel BF16X layers on 2 GPUs over NCCL: row-sharded (all-gather)
 and column-sharded (all-reduce) layers against the CPU oracle within the 1e-3
-relative-L2 gate.  Skipped with fewer than 2 GPUs."""
+relative-L2 gate, and the tensor-parallel decoder with packed shards.
+Skipped with fewer than 2 GPUs."""
 import datetime
 import os
 
@@ -64,6 +65,7 @@ def test_tp_row_and_column_nccl():
 
 def _decoder_worker(rank, world, port, q):
     try:
+        import torch.distributed as dist
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dev = torch.device("cuda", rank)
