@@ -9,7 +9,7 @@
   ``__init__`` the same way).  ``r``, ``bk``, ``group`` and ``num_warps`` are
   Triton tuning knobs of the reference kernel; they are accepted and ignored.
 * ``Bf16xFused`` -- the three-mode Linear (bf16x_fused.py:149-229):
-  ``'fused'`` runs the fused kernels (decode+GEMV for up to 8 rows of
+  ``'fused'`` runs the fused kernels (decode+GEMV for up to 16 rows of
   activations, the tcgen05 decode+GEMM above that; the reference falls back
   to decode + F.linear for more than one row), ``'opt'`` decodes into a
   process-wide shared buffer and calls F.linear, ``'repo'`` runs the

@@ -1,7 +1,8 @@
-// bf16x_gemv.cu -- fused BF16X decode + GEMV for batch 1..8 (sm_100a).
+// bf16x_gemv.cu -- fused BF16X decode + GEMV for batch 1..16 (sm_100a).
 //
 // Replaces _bf16x_gemv_fused_kernel / bf16x_fused_gemv (bf16x_fused.py:32-127)
-// and generalises it from batch 1 to batch <= 8.
+// and generalises it from batch 1 to batch <= 16 (above 8 each decoded
+// fragment feeds two mma, one per group of 8 activation rows).
 //
 // Design (HBM-bound: the only large stream is the compressed weight):
 //   * work items are (16-row tile, 256-column chunk) pairs in tile-major
@@ -133,6 +134,21 @@ __device__ __forceinline__ void frag_mma(const uint4 *frag, int lane, const uint
     if constexpr (J + 1 < 8) frag_mma<J + 1>(frag, lane, xq, ce, co);
 }
 
+// The same for 9..16 rows of activations: each A fragment feeds two mma,
+// one per group of 8 activation rows (x rows g and 8+g).
+template <int J>
+__device__ __forceinline__ void frag_mma2(const uint4 *frag, int lane, const uint16_t *xq, const uint16_t *xq2,
+                                          float (&ce)[4], float (&co)[4], float (&de)[4], float (&dd)[4]) {
+    const uint4 a = frag[J * 32 + lane];
+    const uint2 b = *reinterpret_cast<const uint2 *>(xq + 4 * J);
+    const uint2 b2 = *reinterpret_cast<const uint2 *>(xq2 + 4 * J);
+    float(&c)[4] = (J & 1) ? co : ce;
+    float(&d)[4] = (J & 1) ? dd : de;
+    mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, b.x, b.y);
+    mma_bf16_16816(d[0], d[1], d[2], d[3], a.x, a.y, a.z, a.w, b2.x, b2.y);
+    if constexpr (J + 1 < 8) frag_mma2<J + 1>(frag, lane, xq, xq2, ce, co, de, dd);
+}
+
 // Warp w of the partition owns items [T*w/W, T*(w+1)/W); item i belongs to
 // warp floor(((i+1)*W - 1) / T).
 __device__ __forceinline__ int64_t item_lo(int64_t w, int64_t T, int64_t W) { return T * w / W; }
@@ -230,7 +246,10 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
     }
 
     const int g = lane >> 2, t = lane & 3;
+    constexpr int BW = BMAX > 8 ? 16 : 8;           // activation rows per partial-sum row
+    constexpr int PW = 16 * BW;                     // floats per partial
     float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
+    float de[4] = {0.f, 0.f, 0.f, 0.f}, dd[4] = {0.f, 0.f, 0.f, 0.f};   // rows 8..15 (BMAX > 8)
     int64_t tile = first_tile;
     int c = (int)(lo - first_tile * p.nch);
     int tile_c0 = c;                                // first chunk of the current tile in this range
@@ -250,32 +269,33 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         // w_first's piece is in its slot 1 when its range began in an earlier
         // tile; every later warp's range begins in this tile: slot 0
         const int sl_first = item_lo(w_first, p.T, p.W) < tl * p.nch ? 1 : 0;
-        float o4[4];
+        constexpr int KN = PW / 32;                 // values per lane
+        float o4[KN];
         {
-            const float *src = p.partials + (w_first * 2 + sl_first) * 128 + lane;
+            const float *src = p.partials + (w_first * 2 + sl_first) * PW + lane;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) o4[k] = __ldcg(src + 32 * k);
+            for (int k = 0; k < KN; ++k) o4[k] = __ldcg(src + 32 * k);
         }
         int64_t w2 = w_first + 1;
         for (; w2 + 1 <= w_last; w2 += 2) {
-            const float *a = p.partials + (w2 * 2) * 128 + lane;
-            const float *b2 = a + 2 * 128;
-            float va[4], vb[4];
+            const float *a = p.partials + (w2 * 2) * PW + lane;
+            const float *b2 = a + 2 * PW;
+            float va[KN], vb[KN];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) { va[k] = __ldcg(a + 32 * k); vb[k] = __ldcg(b2 + 32 * k); }
+            for (int k = 0; k < KN; ++k) { va[k] = __ldcg(a + 32 * k); vb[k] = __ldcg(b2 + 32 * k); }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) { o4[k] += va[k]; o4[k] += vb[k]; }
+            for (int k = 0; k < KN; ++k) { o4[k] += va[k]; o4[k] += vb[k]; }
         }
         if (w2 <= w_last) {
-            const float *a = p.partials + (w2 * 2) * 128 + lane;
+            const float *a = p.partials + (w2 * 2) * PW + lane;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) o4[k] += __ldcg(a + 32 * k);
+            for (int k = 0; k < KN; ++k) o4[k] += __ldcg(a + 32 * k);
         }
         const int64_t row0 = tl * kTileRows;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < KN; ++k) {
             const int idx = lane + 32 * k;
-            const int rr = idx >> 3, b = idx & 7;
+            const int rr = idx / BW, b = idx % BW;
             float o = o4[k];
             const int64_t row = row0 + rr;
             if (b < p.batch && row < p.rows) {
@@ -340,7 +360,12 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                         frag16[ent & 0x7FFu] = (uint16_t)(ent >> 16);
                     }
                     __syncwarp();
-                    frag_mma<0>(frag, lane, xg + 32 * q, ce, co);
+                    if constexpr (BMAX > 8) {
+                        const uint16_t *xg2 = xs + (8 + g) * kChunkElems;
+                        frag_mma2<0>(frag, lane, xg + 32 * q, xg2 + 32 * q, ce, co, de, dd);
+                    } else {
+                        frag_mma<0>(frag, lane, xg + 32 * q, ce, co);
+                    }
                     __syncwarp();
                 }
             } else {
@@ -361,7 +386,13 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                 __syncwarp();
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
-                    frag_mma<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), ce, co);
+                    if constexpr (BMAX > 8) {
+                        const uint16_t *xg2 = xs + (8 + g) * kChunkElems;
+                        frag_mma2<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), xg2 + 32 * (4 * h + t),
+                                     ce, co, de, dd);
+                    } else {
+                        frag_mma<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), ce, co);
+                    }
                 __syncwarp();
             }
         }
@@ -379,14 +410,15 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         // ---- tile finished (or range ends inside it)
         if (c == p.nch - 1 || it == hi - 1) {
             const float c0 = ce[0] + co[0], c1 = ce[1] + co[1], c2 = ce[2] + co[2], c3 = ce[3] + co[3];
+            const float d0 = de[0] + dd[0], d1 = de[1] + dd[1], d2 = de[2] + dd[2], d3 = de[3] + dd[3];
             const int64_t row0 = tile * kTileRows;
             const bool whole = tile_c0 == 0 && c == p.nch - 1;
             if (whole) {
-                const float v[4] = {c0, c1, c2, c3};
+                const float v[8] = {c0, c1, c2, c3, d0, d1, d2, d3};
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int64_t row = row0 + g + 8 * (k >> 1);
-                    const int b = 2 * t + (k & 1);
+                for (int k = 0; k < (BMAX > 8 ? 8 : 4); ++k) {
+                    const int64_t row = row0 + g + 8 * ((k >> 1) & 1);
+                    const int b = 2 * t + (k & 1) + 8 * (k >> 2);
                     if (b < p.batch && row < p.rows) {
                         float o = v[k];
                         if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
@@ -397,11 +429,17 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
             } else {
                 // partial tile: publish this piece, the last arriving warp reduces
                 const int pslot = tile == first_tile ? 0 : 1;
-                float *mine = p.partials + (gw * 2 + pslot) * 128;
-                mine[g * 8 + 2 * t] = c0;
-                mine[g * 8 + 2 * t + 1] = c1;
-                mine[(g + 8) * 8 + 2 * t] = c2;
-                mine[(g + 8) * 8 + 2 * t + 1] = c3;
+                float *mine = p.partials + (gw * 2 + pslot) * PW;
+                mine[g * BW + 2 * t] = c0;
+                mine[g * BW + 2 * t + 1] = c1;
+                mine[(g + 8) * BW + 2 * t] = c2;
+                mine[(g + 8) * BW + 2 * t + 1] = c3;
+                if constexpr (BMAX > 8) {
+                    mine[g * BW + 8 + 2 * t] = d0;
+                    mine[g * BW + 8 + 2 * t + 1] = d1;
+                    mine[(g + 8) * BW + 8 + 2 * t] = d2;
+                    mine[(g + 8) * BW + 8 + 2 * t + 1] = d3;
+                }
                 __threadfence();
                 __syncwarp();
                 int old = 0;
@@ -409,7 +447,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                 if (__shfl_sync(0xffffffffu, old, 0) == pieces_before(tile)) reduce_split(tile);
             }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) ce[k] = co[k] = 0.f;
+            for (int k = 0; k < 4; ++k) ce[k] = co[k] = de[k] = dd[k] = 0.f;
             tile_c0 = 0;
         }
         if (++s == S) { s = 0; parity ^= 1u; }
@@ -500,10 +538,12 @@ static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
     if (batch == 1) return wide ? GemvCfg<1, 12>::kWarps : GemvCfg<1, 8>::kWarps;
     if (batch == 2) return wide ? GemvCfg<2, 12>::kWarps : GemvCfg<2, 8>::kWarps;
     if (batch <= 4) return GemvCfg<4, 8>::kWarps;
-    return GemvCfg<8, 8>::kWarps;
+    if (batch <= 8) return GemvCfg<8, 8>::kWarps;
+    return GemvCfg<16, 8>::kWarps;
 }
 
-static int64_t scratch_need(const GemvLaunch &L) { return L.W * 2 * 128 * 4; }
+// partial sums: per unit two [16][8] (batch <= 8) or [16][16] fp32 slots
+static int64_t scratch_need(const GemvLaunch &L, int64_t batch) { return L.W * 2 * 16 * (batch > 8 ? 16 : 8) * 4; }
 
 template <int BMAX, int NW>
 static int launch_gemv(const GemvParams &p, const GemvLaunch &L, cudaStream_t st) {
@@ -541,7 +581,7 @@ using namespace bf16x;
 extern "C" int64_t bf16x_gemv_scratch_bytes(int64_t rows, int64_t in_f) {
     if (rows <= 0 || in_f <= 0) return 0;
     int64_t need = 0;
-    for (int b : {1, 2, 4, 8}) need = std::max(need, scratch_need(plan_gemv(rows, in_f, warps_for(b, rows, in_f))));
+    for (int b : {1, 2, 4, 8, 16}) need = std::max(need, scratch_need(plan_gemv(rows, in_f, warps_for(b, rows, in_f)), b));
     return need;
 }
 
@@ -551,7 +591,7 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
                           int32_t *tile_counters, void *scratch, int64_t scratch_bytes, void *stream) {
     if (rows < 0 || in_f <= 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: bad shape");
     if (in_f > 65536) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv: in_f > 65536");
-    if (batch < 1 || batch > 8) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: batch must be 1..8 (got %lld)", (long long)batch);
+    if (batch < 1 || batch > 16) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: batch must be 1..16 (got %lld)", (long long)batch);
     if (y_dtype != BF16X_DTYPE_BF16 && y_dtype != BF16X_DTYPE_F32)
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: bad y_dtype");
     if (rows == 0) return BF16X_OK;
@@ -565,15 +605,15 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
     const int nw = warps_for(batch, rows, in_f);
     const GemvLaunch L = plan_gemv(rows, in_f, nw);
     if (!tile_counters) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: tile_counters (ceil(rows/16) zeroed int32) missing");
-    if (!scratch || scratch_bytes < scratch_need(L))
-        return set_error(BF16X_ERR_INVALID, "bf16x_gemv: scratch of %lld bytes needed", (long long)scratch_need(L));
+    if (!scratch || scratch_bytes < scratch_need(L, batch))
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv: scratch of %lld bytes needed", (long long)scratch_need(L, batch));
     if (reinterpret_cast<uintptr_t>(scratch) & 15u)
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: scratch must be 16-byte aligned");
     GemvParams p;
     {
         int dev = 0;
         cudaGetDevice(&dev);
-        const int64_t bmax = batch == 1 ? 1 : batch == 2 ? 2 : batch <= 4 ? 4 : 8;
+        const int64_t bmax = batch == 1 ? 1 : batch == 2 ? 2 : batch <= 4 ? 4 : batch <= 8 ? 8 : 16;
         if (!cached_map(&p.wmap, MapKey{layout, rows, in_f, 0, dev}, make_wmap))
             return set_error(BF16X_ERR_CUDA, "bf16x_gemv: weight tensor map");
         if (!cached_map(&p.xmap, MapKey{x, in_pad, batch, ldx | (bmax << 40), dev}, make_xmap))
@@ -590,7 +630,8 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
     if (batch == 1) return nw > 8 ? launch_gemv<1, 12>(p, L, st) : launch_gemv<1, 8>(p, L, st);
     if (batch == 2) return nw > 8 ? launch_gemv<2, 12>(p, L, st) : launch_gemv<2, 8>(p, L, st);
     if (batch <= 4) return launch_gemv<4, 8>(p, L, st);
-    return launch_gemv<8, 8>(p, L, st);
+    if (batch <= 8) return launch_gemv<8, 8>(p, L, st);
+    return launch_gemv<16, 8>(p, L, st);
 }
 
 // ------------------------------------------------ no-allocation GEMV entry
@@ -645,7 +686,7 @@ extern "C" int bf16x_gemv_noalloc(const uint8_t *layout, const int32_t *ptile_of
     if (n_tiles > kNoAllocMaxTiles)
         return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv_noalloc: rows %lld exceed the fixed scratch limit of %lld",
                          (long long)rows, (long long)(kNoAllocMaxTiles * kTileRows));
-    const int64_t need = scratch_need(plan_gemv(rows, in_f, warps_for(batch, rows, in_f)));
+    const int64_t need = scratch_need(plan_gemv(rows, in_f, warps_for(batch, rows, in_f)), batch);
     if (need > kNoAllocPartialBytes)
         return set_error(BF16X_ERR_UNSUPPORTED,
                          "bf16x_gemv_noalloc: %lld bytes of partial sums needed, fixed scratch holds %lld",

@@ -1,6 +1,6 @@
 """End-to-end decoder for the BF16X path: a Llama-style model whose linear
 layers (attention and MLP projections and lm_head) are BF16X-packed and run
-through the fused decode+GEMV (up to 8 tokens) and decode+GEMM (more tokens)
+through the fused decode+GEMV (up to 16 tokens) and decode+GEMM (more tokens)
 kernels.
 
 It exists to measure the hot path inside a model: ms per generated token
@@ -249,7 +249,7 @@ class LlamaModel(nn.Module):
 
 class ResidentLinear(nn.Module):
     """A Linear whose weight is only the resident BF16X layout on the GPU:
-    the fused GEMV for up to 8 rows of activations, the GEMM above."""
+    the fused GEMV for up to 16 rows of activations, the GEMM above."""
 
     def __init__(self, rw):
         super().__init__()

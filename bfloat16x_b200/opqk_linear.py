@@ -85,7 +85,7 @@ def packed_nbytes(p: dict) -> int:
 class BF16XLinear(nn.Module):
     """Decode+matmul Linear on a BF16X dict (opqk_linear.py:327-407), GPU-only.
 
-    ``forward`` runs the fused decode+GEMV (<= 8 rows of activations) or
+    ``forward`` runs the fused decode+GEMV (<= 16 rows of activations) or
     decode+GEMM kernel on the resident layout; ``decode_to_bf16`` caches the
     exact bf16 weight, after which ``forward`` is a plain ``F.linear`` as in
     the reference."""

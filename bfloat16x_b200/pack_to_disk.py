@@ -19,7 +19,7 @@ weight as soon as it is packed.  ``replace_linears_from_packed`` maps the
 blob (safetensors mmap), copies each layer's flat streams to the GPU and
 builds the resident layout there with the device repack -- no
 re-quantisation -- then swaps the layer for a ``Bf16xStreamLinear``, which
-runs the fused decode+GEMV (up to 8 rows) or decode+GEMM (more rows) on the
+runs the fused decode+GEMV (up to 16 rows) or decode+GEMM (more rows) on the
 exact weights.  ``resident=False`` keeps the resident layout in pinned host
 memory and stages it to the device on every forward, as ``Bf16xGemmLinear``
 does.

@@ -19,7 +19,7 @@ from ._lib import BF16X_DTYPE_BF16, BF16X_DTYPE_F32, CHUNK_BYTES, CHUNK_ELEMS, T
 
 _FLAT = ("sign_packed", "mant_packed", "delta_packed", "emax", "delta_ovf_idx", "delta_ovf_val")
 
-GEMV_MAX_BATCH = 8
+GEMV_MAX_BATCH = 16
 
 
 def _as_dev(t: torch.Tensor, dtype, dev) -> torch.Tensor:
@@ -195,7 +195,7 @@ class ResidentWeight:
 
     def gemv(self, x: torch.Tensor, bias: torch.Tensor | None = None,
              out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
-        """y[b, n] = sum_k W[n, k] x[b, k] (+ bias) for a batch of <= 8 rows."""
+        """y[b, n] = sum_k W[n, k] x[b, k] (+ bias) for a batch of <= 16 rows."""
         _lib.require_cuda(x, "x")
         x2 = x.reshape(-1, self.in_f)
         B = x2.shape[0]
@@ -243,7 +243,7 @@ class ResidentWeight:
 
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None,
                out_dtype: torch.dtype | None = None) -> torch.Tensor:
-        """x[..., in_f] -> [..., rows]: the GEMV kernel for up to 8 rows of
+        """x[..., in_f] -> [..., rows]: the GEMV kernel for up to 16 rows of
         activations, the tensor-core GEMM above that."""
         od = out_dtype or (x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.bfloat16)
         x2 = x.reshape(-1, self.in_f)

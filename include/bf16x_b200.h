@@ -129,9 +129,9 @@ int bf16x_resident_decode(const uint8_t *layout, const int32_t *ptile_off,
                           const uint32_t *precs, int64_t rows, int64_t in_f,
                           uint16_t *out, int64_t ld_out, void *stream);
 
-/* ---- fused decode + GEMV (batch 1..8) ----------------------------------- */
+/* ---- fused decode + GEMV (batch 1..16) ---------------------------------- */
 /* Replaces bf16x_fused_gemv / _bf16x_gemv_fused_kernel (bf16x_fused.py:32-127):
- * y[b][n] = sum_k W[n][k] * x[b][k] (+ bias[n]) for b < batch <= 8, with W
+ * y[b][n] = sum_k W[n][k] * x[b][k] (+ bias[n]) for b < batch <= 16, with W
  * read from the resident layout and decoded in registers, patches applied
  * exactly, fp32 accumulation, deterministic.  x: bf16 [batch][ldx],
  * ldx >= ceil(in_f/256)*256 elements with zeros past in_f, rows 16-byte

@@ -57,7 +57,7 @@ def _err(L):
 
 def test_invalid_arguments_rejected_on_host(L):
     # batch out of range
-    rc = L.bf16x_gemv(None, None, None, 16, 256, None, 9, 256, None, None, 0, 16, None, None, 0, None)
+    rc = L.bf16x_gemv(None, None, None, 16, 256, None, 17, 256, None, None, 0, 16, None, None, 0, None)
     assert rc == -1
     assert "batch" in _err(L)
     # in_f too large for the resident layout

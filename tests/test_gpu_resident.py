@@ -77,7 +77,7 @@ def test_gemv_matches_reference(case, b):
 
 @pytest.mark.parametrize("shape", [(16, 256), (17, 256), (100, 512), (33, 96), (5, 300), (1000, 1536),
                                    (64, 14336), (4096, 4096)])
-@pytest.mark.parametrize("b", [1, 2, 4, 5, 8])
+@pytest.mark.parametrize("b", [1, 2, 4, 5, 8, 9, 16])
 def test_gemv_vs_oracle(shape, b):
     w = synthetic_weight(*shape, seed=29)
     wb = bits_of(w)
@@ -146,7 +146,7 @@ def test_repack_filtered_table():
     _lib.check_device_status()
 
 
-@pytest.mark.parametrize("b", [1, 8])
+@pytest.mark.parametrize("b", [1, 8, 13])
 def test_gemv_dense_patches(b):
     from tests.test_gpu_gemm import _dense_patch_weight
     wb = _dense_patch_weight(300, 1536, seed=9)
