@@ -110,28 +110,38 @@ __device__ __forceinline__ void mma_bf16_16816(float &c0, float &c1, float &c2, 
 // Decode step J of one group: k-slots (2t, 2t+1 | 2t+8, 2t+9) of mma step J
 // carry the group's columns 4J..4J+3, i.e. pairs 2J (a0/a1) and 2J+1 (a2/a3)
 // of rows g (a0/a2) and g+8 (a1/a3).  The lane stores them as one 16-byte
-// fragment at frag[J][lane].
+// fragment at frag[J][lane ^ J] (the slot order of frag_index).
 template <int J>
 __device__ __forceinline__ void group_to_frag(const uint32_t (&smA)[8], const uint32_t (&dA)[3], uint32_t eAlo,
                                               uint32_t eAhi, const uint32_t (&smB)[8], const uint32_t (&dB)[3],
                                               uint32_t eBlo, uint32_t eBhi, uint4 *frag, int lane) {
     const uint32_t eA = J < 4 ? eAlo : eAhi, eB = J < 4 ? eBlo : eBhi;
-    frag[J * 32 + lane] = make_uint4(decode_pair<2 * J>(smA, dA, eA), decode_pair<2 * J>(smB, dB, eB),
+    frag[J * 32 + (lane ^ J)] = make_uint4(decode_pair<2 * J>(smA, dA, eA), decode_pair<2 * J>(smB, dB, eB),
                                      decode_pair<2 * J + 1>(smA, dA, eA), decode_pair<2 * J + 1>(smB, dB, eB));
     if constexpr (J + 1 < 8) group_to_frag<J + 1>(smA, dA, eAlo, eAhi, smB, dB, eBlo, eBhi, frag, lane);
 }
 
+// 8-byte shared-memory load by the lanes whose predicate is set; the others
+// get zeros without touching shared memory (no wavefront for them).
+__device__ __forceinline__ uint2 lds64_if(const void *ptr, bool pred) {
+    uint2 v = make_uint2(0u, 0u);
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q ld.shared.v2.u32 {%0, %1}, [%2];\n\t}"
+                 : "+r"(v.x), "+r"(v.y) : "r"(smem_u32(ptr)), "r"((int)pred) : "memory");
+    return v;
+}
+
 // mma steps of one half chunk: A from the fragment buffer, B = x[g][group +
-// 4J .. +3] (one 8-byte load).  Even and odd steps accumulate separately: two
-// independent mma chains.
+// 4J .. +3] (one 8-byte load, by the lanes whose activation row g exists;
+// the B operand of the others is zero).  Even and odd steps accumulate
+// separately: two independent mma chains.
 template <int J>
-__device__ __forceinline__ void frag_mma(const uint4 *frag, int lane, const uint16_t *xq, float (&ce)[4],
-                                         float (&co)[4]) {
-    const uint4 a = frag[J * 32 + lane];
-    const uint2 b = *reinterpret_cast<const uint2 *>(xq + 4 * J);
+__device__ __forceinline__ void frag_mma(const uint4 *frag, int lane, const uint16_t *xq, bool hasx,
+                                         float (&ce)[4], float (&co)[4]) {
+    const uint4 a = frag[J * 32 + (lane ^ J)];
+    const uint2 b = lds64_if(xq + 4 * J, hasx);
     float(&c)[4] = (J & 1) ? co : ce;
     mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, b.x, b.y);
-    if constexpr (J + 1 < 8) frag_mma<J + 1>(frag, lane, xq, ce, co);
+    if constexpr (J + 1 < 8) frag_mma<J + 1>(frag, lane, xq, hasx, ce, co);
 }
 
 // The same for 9..16 rows of activations: each A fragment feeds two mma,
@@ -139,7 +149,7 @@ __device__ __forceinline__ void frag_mma(const uint4 *frag, int lane, const uint
 template <int J>
 __device__ __forceinline__ void frag_mma2(const uint4 *frag, int lane, const uint16_t *xq, const uint16_t *xq2,
                                           float (&ce)[4], float (&co)[4], float (&de)[4], float (&dd)[4]) {
-    const uint4 a = frag[J * 32 + lane];
+    const uint4 a = frag[J * 32 + (lane ^ J)];
     const uint2 b = *reinterpret_cast<const uint2 *>(xq + 4 * J);
     const uint2 b2 = *reinterpret_cast<const uint2 *>(xq2 + 4 * J);
     float(&c)[4] = (J & 1) ? co : ce;
@@ -364,7 +374,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                         const uint16_t *xg2 = xs + (8 + g) * kChunkElems;
                         frag_mma2<0>(frag, lane, xg + 32 * q, xg2 + 32 * q, ce, co, de, dd);
                     } else {
-                        frag_mma<0>(frag, lane, xg + 32 * q, ce, co);
+                        frag_mma<0>(frag, lane, xg + 32 * q, g < BMAX, ce, co);
                     }
                     __syncwarp();
                 }
@@ -391,7 +401,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                         frag_mma2<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), xg2 + 32 * (4 * h + t),
                                      ce, co, de, dd);
                     } else {
-                        frag_mma<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), ce, co);
+                        frag_mma<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), g < BMAX, ce, co);
                     }
                 __syncwarp();
             }

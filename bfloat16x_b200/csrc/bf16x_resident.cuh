@@ -112,19 +112,23 @@ __device__ __forceinline__ void load_group(const uint8_t *chunk, int q, uint32_t
 // mma.m16n8k16 A-fragment buffer of its half (128 columns): 8 steps x 32
 // lanes x 4 registers x 2 halves of 16 bits.  Lane (g, t) holds rows g and
 // g+8 of the 32-column group t; step J carries group columns 4J..4J+3 as
-// pairs 2J (registers 0/1: rows g/g+8) and 2J+1 (registers 2/3).
+// pairs 2J (registers 0/1: rows g/g+8) and 2J+1 (registers 2/3).  The lane's
+// 16 bytes of step J sit at slot J * 32 + (lane ^ J): a permutation within
+// the step, so the fragment stores and loads stay conflict-free, that spreads
+// the patch entries of a 64-column quarter over all 32 shared-memory banks.
 __host__ __device__ inline uint32_t frag_index(uint32_t row, uint32_t col) {
     const uint32_t kk = col & 127u;
     const uint32_t owner = 4u * (row & 7u) + (kk >> 5);
     const uint32_t step = (kk >> 2) & 7u;
     const uint32_t reg = (row >> 3) + 2u * ((kk >> 1) & 1u);
-    return (step * 32u + owner) * 8u + reg * 2u + (kk & 1u);
+    return (step * 32u + (owner ^ step)) * 8u + reg * 2u + (kk & 1u);
 }
 
 // Inverse of frag_index: (row, col) from a patch entry.
 __host__ __device__ inline void frag_position(uint32_t entry, uint32_t &row, uint32_t &col) {
     const uint32_t idx = entry & 0x7FFu, half = (entry >> 11) & 1u;
-    const uint32_t hw = idx & 1u, reg = (idx >> 1) & 3u, owner = (idx >> 3) & 31u, step = idx >> 8;
+    const uint32_t step = idx >> 8;
+    const uint32_t hw = idx & 1u, reg = (idx >> 1) & 3u, owner = ((idx >> 3) & 31u) ^ step;
     row = (owner >> 2) + 8u * (reg & 1u);
     col = 128u * half + 32u * (owner & 3u) + 4u * step + 2u * (reg >> 1) + hw;
 }
