@@ -121,27 +121,28 @@ __device__ __forceinline__ void group_to_frag(const uint32_t (&smA)[8], const ui
     if constexpr (J + 1 < 8) group_to_frag<J + 1>(smA, dA, eAlo, eAhi, smB, dB, eBlo, eBhi, frag, lane);
 }
 
-// 8-byte shared-memory load by the lanes whose predicate is set; the others
+// 16-byte shared-memory load by the lanes whose predicate is set; the others
 // get zeros without touching shared memory (no wavefront for them).
-__device__ __forceinline__ uint2 lds64_if(const void *ptr, bool pred) {
-    uint2 v = make_uint2(0u, 0u);
-    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q ld.shared.v2.u32 {%0, %1}, [%2];\n\t}"
-                 : "+r"(v.x), "+r"(v.y) : "r"(smem_u32(ptr)), "r"((int)pred) : "memory");
+__device__ __forceinline__ uint4 lds128_if(const void *ptr, bool pred) {
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t@q ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n\t}"
+                 : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w) : "r"(smem_u32(ptr)), "r"((int)pred) : "memory");
     return v;
 }
 
 // mma steps of one half chunk: A from the fragment buffer, B = x[g][group +
-// 4J .. +3] (one 8-byte load, by the lanes whose activation row g exists;
-// the B operand of the others is zero).  Even and odd steps accumulate
-// separately: two independent mma chains.
+// 4J .. +3], loaded 16 bytes at a time for steps J and J+1 by the lanes whose
+// activation row g exists (the B operand of the others is zero).  Even and
+// odd steps accumulate separately: two independent mma chains.
 template <int J>
 __device__ __forceinline__ void frag_mma(const uint4 *frag, int lane, const uint16_t *xq, bool hasx,
-                                         float (&ce)[4], float (&co)[4]) {
+                                         float (&ce)[4], float (&co)[4], uint4 bx = uint4{}) {
+    if constexpr ((J & 1) == 0) bx = lds128_if(xq + 4 * J, hasx);
     const uint4 a = frag[J * 32 + (lane ^ J)];
-    const uint2 b = lds64_if(xq + 4 * J, hasx);
     float(&c)[4] = (J & 1) ? co : ce;
-    mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, b.x, b.y);
-    if constexpr (J + 1 < 8) frag_mma<J + 1>(frag, lane, xq, hasx, ce, co);
+    if constexpr ((J & 1) == 0) mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, bx.x, bx.y);
+    else mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, bx.z, bx.w);
+    if constexpr (J + 1 < 8) frag_mma<J + 1>(frag, lane, xq, hasx, ce, co, bx);
 }
 
 // The same for 9..16 rows of activations: each A fragment feeds two mma,

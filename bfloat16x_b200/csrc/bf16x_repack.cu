@@ -141,7 +141,8 @@ repack_count_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int
 
 // One CTA per 16-row tile: pass A counts each row's patches per chunk and
 // quarter (64-column block), pass B writes the resident chunks, the record
-// headers and the entries sorted by (quarter, row, column).
+// headers and the entries sorted by (quarter, row, column); repack_order_kernel
+// then reorders each quarter for the GEMV's shared-memory banks.
 __global__ void __launch_bounds__(kTileRows * 32)
 repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int nch,
                     const int32_t *__restrict__ ptile_off, uint8_t *__restrict__ layout,
@@ -238,6 +239,56 @@ repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int
                 *dst++ = frag_index((uint32_t)warp, col) | ((col >> 7) << 11) | (bits << 16);
             }
         }
+    }
+}
+
+// Orders the entries of every (tile, chunk, quarter) for the GEMV's patch
+// stores: 32 lanes store 32 consecutive entries at once, and entries whose
+// fragment words share a shared-memory bank serialise.  Within each quarter
+// (the GEMM reads a quarter's entries as one range, in any order) the
+// entries are dealt bank by bank: the r-th entry of every bank comes before
+// the (r+1)-th of any, banks in increasing order, ties in their previous
+// (row, column) order -- deterministic.  One warp per quarter.
+__global__ void __launch_bounds__(128) repack_order_kernel(const int32_t *__restrict__ ptile_off,
+                                                           uint32_t *__restrict__ precs) {
+    __shared__ uint32_t ent[4][kTileRows * 64];     // a quarter holds at most 16 x 64 entries
+    __shared__ uint16_t rnk[4][kTileRows * 64];
+    __shared__ int cnt[4][32];
+    const int q = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t *rec = precs + ptile_off[blockIdx.x];
+    const uint32_t h0 = rec[0], h1 = rec[1];
+    const int bq[5] = {0, (int)(h1 & 0xFFFFu), (int)(h0 & 0xFFFFu), (int)(h1 >> 16), (int)(h0 >> 16)};
+    const int lo = bq[q], n = bq[q + 1] - bq[q];
+    if (n <= 1) return;
+    uint32_t *src = rec + kRecHdrWords + lo;
+    cnt[q][lane] = 0;
+    __syncwarp();
+    for (int b0 = 0; b0 < n; b0 += 32) {
+        const int i = b0 + lane;
+        const bool on = i < n;
+        const uint32_t e = on ? src[i] : 0u;
+        const uint32_t bank = ((e & 0x7FFu) >> 1) & 31u;
+        const uint32_t act = __ballot_sync(0xffffffffu, on);
+        const uint32_t same = __match_any_sync(0xffffffffu, on ? bank : 32u + lane) & act;
+        const int before = __popc(same & ((1u << lane) - 1u));
+        if (on) {
+            ent[q][i] = e;
+            rnk[q][i] = (uint16_t)(cnt[q][bank] + before);
+        }
+        __syncwarp();
+        if (on && before == 0) cnt[q][bank] += __popc(same);   // the first lane of each bank group
+        __syncwarp();
+    }
+    for (int i = lane; i < n; i += 32) {
+        const uint32_t e = ent[q][i];
+        const int bank = (int)(((e & 0x7FFu) >> 1) & 31u), r = rnk[q][i];
+        int pos = 0;
+        for (int b = 0; b < 32; ++b) {
+            const int c = cnt[q][b];
+            pos += c < r ? c : r;                   // rank < r of every bank
+            if (b < bank && c > r) ++pos;           // rank r of the lower banks
+        }
+        src[pos] = e;
     }
 }
 
@@ -371,7 +422,11 @@ extern "C" int bf16x_repack(const uint32_t *sign, int64_t n_sign_words,
     const int64_t n_tiles = (rows + kTileRows - 1) / kTileRows;
     repack_write_kernel<<<(unsigned)n_tiles, kTileRows * 32, 4 * kTileRows * nch * sizeof(uint16_t),
                           (cudaStream_t)stream>>>(f, in_f, row0, row1, nch, ptile_off, layout, precs);
-    return check_launch("repack_write_kernel");
+    if (int rc2 = check_launch("repack_write_kernel")) return rc2;
+    const int64_t n_rec = n_tiles * nch;
+    if (n_rec > 0x7fffffffLL) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_repack: too many records");
+    repack_order_kernel<<<(unsigned)n_rec, 128, 0, (cudaStream_t)stream>>>(ptile_off, precs);
+    return check_launch("repack_order_kernel");
 }
 
 extern "C" int bf16x_resident_decode(const uint8_t *layout, const int32_t *ptile_off,

@@ -32,7 +32,9 @@
 //                n_all (bits 16..31): all entries
 //   word 1       n_q0 (bits 0..15): entries in columns 0..63,
 //                n_q012 (bits 16..31): entries in columns 0..191
-//   words 2..    entries sorted by (column / 64, row, column), u32 each:
+//   words 2..    entries grouped by 64-column quarter (in quarter order;
+//                within a quarter dealt round-robin over the shared-memory
+//                banks of their fragment words), u32 each:
 //                frag (bits 0..10) | half (bit 11) | exact bf16 bits << 16
 //                where half = column >= 128 and frag is the element's 16-bit
 //                slot in the mma fragment order of its half chunk (see
