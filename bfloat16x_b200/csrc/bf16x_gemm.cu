@@ -1431,7 +1431,10 @@ static SlabPlan plan_slab(int64_t rows, int64_t in_f, int64_t M, int sms) {
         return (double)tiles / (double)(((tiles + s.npairs - 1) / s.npairs) * s.npairs);
     };
     const int64_t tn1 = (M + 255) / 256, tn2 = (M + 511) / 512;
-    const bool ok1 = tn1 >= 4 && tiles_m2 * tn1 >= s.npairs;
+#ifndef BF16X_SLAB_MIN_TN
+#define BF16X_SLAB_MIN_TN 4
+#endif
+    const bool ok1 = tn1 >= BF16X_SLAB_MIN_TN && tiles_m2 * tn1 >= s.npairs;
     const bool ok2 = BF16X_SLAB_WIDE && nch >= 32 && tn2 >= 2 && tiles_m2 * tn2 >= s.npairs;
     if (!ok1 && !ok2) return s;
     s.nh = (ok2 && (!ok1 || 1.15 * wave_eff(tiles_m2 * tn2) >= wave_eff(tiles_m2 * tn1))) ? 2 : 1;
