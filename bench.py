@@ -160,20 +160,24 @@ def workload_bytes(weight_bytes, rows, in_f, batch, y_bytes=2):
 
 
 def stored_weight_bytes(p, rows, in_f):
-    """ResidentWeight.nbytes of a flat dict, computed on the host: 368 B per
-    256-column chunk of each row, one patch record per (16-row tile, chunk) of
-    2 header words + one word per delta > 7 entry padded to 4 words, and
-    tiles x chunks + 1 record offsets.  Exact when in_f % 16 == 0 (the row-local
-    sub-blocks are then the flat ones)."""
+    """ResidentWeight.nbytes of a flat dict, computed on the host from its
+    exact decode: 384 B per 256-column chunk of each row; one record per
+    (16-row tile, chunk) of 32 emax words, 2 header words and one word per
+    weight whose exponent is more than 15 below the largest of its row-local
+    32-column group, padded to 4 words; tiles x chunks + 1 record offsets."""
     import numpy as np
+    from oracle import oracle
     nch = (in_f + 255) // 256
     n_tiles = (rows + 15) // 16
-    idx = np.asarray(p["delta_ovf_idx"]).astype(np.int64)
-    big = idx[np.asarray(p["delta_ovf_val"]) > 7]
-    rec = (big // in_f) // 16 * nch + (big % in_f) // 256
-    counts = np.bincount(rec, minlength=n_tiles * nch)
-    rec_words = int(((2 + counts + 3) // 4 * 4).sum())
-    return rows * nch * 368 + 4 * rec_words + 4 * (n_tiles * nch + 1)
+    e = np.zeros((n_tiles * 16, nch * 256), dtype=np.int16)
+    e[:rows, :in_f] = ((oracle.decode(p).reshape(rows, in_f) >> 7) & 0xFF).astype(np.int16)
+    valid = np.zeros_like(e, dtype=bool)
+    valid[:rows, :in_f] = True
+    g = e.reshape(n_tiles * 16, nch * 8, 32)
+    patch = ((g.max(axis=2, keepdims=True) - g) > 15) & valid.reshape(g.shape)
+    counts = patch.reshape(n_tiles, 16, nch, 256).sum(axis=(1, 3))
+    rec_words = int(((34 + counts + 3) // 4 * 4).sum())
+    return rows * nch * 384 + 4 * rec_words + 4 * (n_tiles * nch + 1)
 
 
 def run_reference(args):

@@ -18,8 +18,10 @@ BF16X_DTYPE_BF16 = 0
 BF16X_DTYPE_F32 = 1
 BF16X_DTYPE_F32_TRUNC = 2
 CHUNK_ELEMS = 256
-CHUNK_BYTES = 368
+CHUNK_BYTES = 384
 TILE_ROWS = 16
+REC_HDR_WORD = 32       # record word holding n_low | n_all << 16 (after 128 bytes of emax)
+REC_ENTRY_WORD = 34     # first patch entry of a record
 
 
 class Bf16xError(RuntimeError):

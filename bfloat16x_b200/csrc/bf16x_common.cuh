@@ -152,6 +152,13 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *map, int c0, 
         :: "r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)) : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void *dst, const void *map, int c0, int c1, int c2, int c3,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        :: "r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)) : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory accesses with later
 // async-proxy ones (TMA writes, tensor-core reads) of the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -13,9 +13,10 @@
 // 128-byte-swizzled in shared memory, D in tensor memory.
 //
 // Warp roles (23 warps):
-//   0      W producer: per 256-column chunk, TMAs of kGemmWRows rows x 368
+//   0      W producer: per 256-column chunk, TMAs of kGemmWRows rows x 384
 //          bytes of the resident layout (128 rows by default: one stage per
-//          chunk, in a ring of stages) + the 16-row patch records of the stage
+//          chunk, in a ring of stages; 128-byte swizzled) + the 16-row patch
+//          records of the stage (the groups' emax and the patch entries)
 //   1      B producer: one swizzled TMA per k-block (BN rows x 64 columns)
 //   2      MMA issuer: TMEM allocation, 4 x tcgen05.mma (K=16) per k-block,
 //          tcgen05.commit to release the A and B slots and to publish a tile
@@ -76,7 +77,7 @@ struct GemmCfg {
 };
 
 struct GemmParams {
-    CUtensorMap wmap;    // resident layout [rows][chunks][92 words], box 64 rows x 1 chunk
+    CUtensorMap wmap;    // resident layout [rows][chunks][3 lines], box kGemmWRows rows x 1 chunk, 128B swizzle
     CUtensorMap xmap;    // activations [M][in_f] bf16, box BN rows x 64 columns, 128B swizzle
     const int32_t *ptile_off;
     const uint32_t *precs;
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 load_offsets(t, c, hf);
                 if (!role_wait(&w_empty[ws], wph ^ 1u, abort_flag)) break;
                 mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(kGemmWStage + total * 4));
-                tma_load_3d(smem + C::kWOff + ws * kGemmWStage, &p.wmap, 0, cc, rt * kGemmBM + kGemmWRows * hh,
+                tma_load_4d(smem + C::kWOff + ws * kGemmWStage, &p.wmap, 0, 0, cc, rt * kGemmBM + kGemmWRows * hh,
                             &w_full[ws]);
                 uint8_t *rec = smem + C::kROff + ws * C::kRecStage;
 #pragma unroll
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                         if (!w) { ok = false; break; }
                         if (kq == dg && has_rec) {
                             // quarter boundaries 0 | n_q0 | n_low | n_q012 | n_all
-                            const uint32_t h0 = rec[0], h1 = rec[1];
+                            const uint32_t h0 = rec[kRecHdr], h1 = rec[kRecHdr + 1];
                             const int bq[5] = {0, (int)(h1 & 0xFFFFu), (int)(h0 & 0xFFFFu), (int)(h1 >> 16), (int)(h0 >> 16)};
 #pragma unroll
                             for (int u = 0; u < 2; ++u) {
@@ -365,10 +366,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                         uint8_t *ast = smem + C::kAOff + as * C::kAStage;
                         {
                             // row `row`, columns 64*kq + 32*hh .. +31 of the chunk
-                            uint32_t sm[8], dw[3], e2lo, e2hi;
-                            load_group(wst + lrow * kChunkBytes, 2 * kq + hh, sm, dw, e2lo, e2hi);
+                            uint32_t sm[8], dw[4];
+                            load_group_sw(wst, sw_group_offsets((uint32_t)lrow, (uint32_t)(2 * kq + hh)), sm, dw);
+                            const uint32_t e2 = has_rec ? emax_x2(rec_emax(rec, lane >> 1, 2 * kq + hh)) : 0u;
                             GroupPairs gp;
-                            decode_pairs_from<0>(gp, sm, dw, e2lo, e2hi);
+                            decode_pairs_from<0>(gp, sm, dw, e2);
 #pragma unroll
                             for (int i = 0; i < 4; ++i) {
                                 const uint32_t col = 32u * hh + 8u * i;
@@ -630,7 +632,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
                 load_offsets(t, c, hf);
                 if (!role_wait(&w_empty[ws], wph ^ 1u, abort_flag)) break;
                 mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(kGemmWStage + total * 4));
-                tma_load_3d(smem + C::kWOff + ws * kGemmWStage, &p.wmap, 0, cc,
+                tma_load_4d(smem + C::kWOff + ws * kGemmWStage, &p.wmap, 0, 0, cc,
                             rt * 2 * kGemmBM + (int)rank * kGemmBM + kGemmWRows * hh, &w_full[ws]);
                 uint8_t *rec = smem + C::kROff + ws * C::kRecStage;
 #pragma unroll
@@ -755,7 +757,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
                         if (!w) { ok = false; break; }
                         if (kq == dg && has_rec) {
                             // quarter boundaries 0 | n_q0 | n_low | n_q012 | n_all
-                            const uint32_t h0 = rec[0], h1 = rec[1];
+                            const uint32_t h0 = rec[kRecHdr], h1 = rec[kRecHdr + 1];
                             const int bq[5] = {0, (int)(h1 & 0xFFFFu), (int)(h0 & 0xFFFFu), (int)(h1 >> 16), (int)(h0 >> 16)};
 #pragma unroll
                             for (int u = 0; u < 2; ++u) {
@@ -772,10 +774,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
                         uint8_t *ast = smem + C::kAOff + as * C::kAStage;
                         {
                             // row `row`, columns 64*kq + 32*hh .. +31 of the chunk
-                            uint32_t sm[8], dw[3], e2lo, e2hi;
-                            load_group(wst + lrow * kChunkBytes, 2 * kq + hh, sm, dw, e2lo, e2hi);
+                            uint32_t sm[8], dw[4];
+                            load_group_sw(wst, sw_group_offsets((uint32_t)lrow, (uint32_t)(2 * kq + hh)), sm, dw);
+                            const uint32_t e2 = has_rec ? emax_x2(rec_emax(rec, lane >> 1, 2 * kq + hh)) : 0u;
                             GroupPairs gp;
-                            decode_pairs_from<0>(gp, sm, dw, e2lo, e2hi);
+                            decode_pairs_from<0>(gp, sm, dw, e2);
 #pragma unroll
                             for (int i = 0; i < 4; ++i) {
                                 const uint32_t col = 32u * hh + 8u * i;
@@ -972,17 +975,13 @@ __device__ __forceinline__ bool counter_wait(const uint32_t *ctr, uint32_t targe
 // launch: evict-first loads, so the stream of compressed weights does not
 // push the decoded slabs and the activations (re-read by every tile) out of
 // L2.
-__device__ __forceinline__ void load_group_stream(const uint8_t *chunk, int q, uint32_t (&sm)[8], uint32_t (&dw)[3],
-                                                  uint32_t &e2lo, uint32_t &e2hi) {
+__device__ __forceinline__ void load_group_stream(const uint8_t *chunk, int q, uint32_t (&sm)[8], uint32_t (&dw)[4]) {
     const uint4 a = __ldcs(reinterpret_cast<const uint4 *>(chunk + kSmOff + 32 * q));
     const uint4 b = __ldcs(reinterpret_cast<const uint4 *>(chunk + kSmOff + 32 * q + 16));
+    const uint4 d = __ldcs(reinterpret_cast<const uint4 *>(chunk + kDOff + 16 * q));
     sm[0] = a.x; sm[1] = a.y; sm[2] = a.z; sm[3] = a.w;
     sm[4] = b.x; sm[5] = b.y; sm[6] = b.z; sm[7] = b.w;
-    const uint32_t *d = reinterpret_cast<const uint32_t *>(chunk + kDOff + 12 * q);
-    dw[0] = __ldcs(d); dw[1] = __ldcs(d + 1); dw[2] = __ldcs(d + 2);
-    const uint32_t e = __ldcs(reinterpret_cast<const uint16_t *>(chunk + kEOff + 2 * q));
-    e2lo = (e & 0xFFu) * 0x00800080u;
-    e2hi = (e >> 8) * 0x00800080u;
+    dw[0] = d.x; dw[1] = d.y; dw[2] = d.z; dw[3] = d.w;
 }
 
 // Slab geometry shared by all roles.
@@ -1254,24 +1253,25 @@ if (p.y_f32) reinterpret_cast<float *>(p.y)[n * p.ldy + row] = o;
                 // the record's offset first: its header load then overlaps the data's
                 const bool has_rec = t16 < p.n_tiles16;
                 const int32_t roff = has_rec ? __ldg(p.ptile_off + t16 * p.nch + c) : 0;
-                uint32_t sm[4][8], dd[4][3], elo[4], ehi[4];
+                uint32_t sm[4][8], dd[4][4], e2[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const int64_t row = t16 * 16 + r0 + 4 * k;
                     if (row < p.rows) {
-                        load_group_stream(p.layout + row * p.row_bytes + (int64_t)c * kChunkBytes, q, sm[k], dd[k], elo[k], ehi[k]);
+                        load_group_stream(p.layout + row * p.row_bytes + (int64_t)c * kChunkBytes, q, sm[k], dd[k]);
+                        e2[k] = emax_x2(__ldg(reinterpret_cast<const uint8_t *>(p.precs + roff) + 8 * (r0 + 4 * k) + q));
                     } else {
 #pragma unroll
                         for (int u = 0; u < 8; ++u) sm[k][u] = 0u;
-                        dd[k][0] = dd[k][1] = dd[k][2] = 0u;
-                        elo[k] = ehi[k] = 0u;
+                        dd[k][0] = dd[k][1] = dd[k][2] = dd[k][3] = 0u;
+                        e2[k] = 0u;
                     }
                 }
-                const int n_all = has_rec ? (int)(__ldg(p.precs + roff) >> 16) : 0;
+                const int n_all = has_rec ? (int)(__ldg(p.precs + roff + kRecHdr) >> 16) : 0;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     GroupPairs gp;
-                    decode_pairs_from<0>(gp, sm[k], dd[k], elo[k], ehi[k]);
+                    decode_pairs_from<0>(gp, sm[k], dd[k], e2[k]);
                     uint4 *o = reinterpret_cast<uint4 *>(dst + (int64_t)(r0 + 4 * k) * ld + 32 * q);
 #pragma unroll
                     for (int u = 0; u < 4; ++u)
@@ -1324,10 +1324,7 @@ template <int BN>
 static int launch_gemm(GemmParams &p, const uint8_t *layout, int64_t in_f, const uint16_t *x, int64_t ldx,
                        cudaStream_t st) {
     using C = GemmCfg<BN>;
-    const cuuint64_t wdims[3] = {(cuuint64_t)(kChunkBytes / 4), (cuuint64_t)p.nch, (cuuint64_t)p.rows};
-    const cuuint64_t wstr[2] = {(cuuint64_t)kChunkBytes, (cuuint64_t)resident_row_bytes(in_f)};
-    const cuuint32_t wbox[3] = {(cuuint32_t)(kChunkBytes / 4), 1u, (cuuint32_t)kGemmWRows};
-    if (!encode_tiled(&p.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, layout, wdims, wstr, wbox))
+    if (!encode_resident_map(&p.wmap, layout, p.rows, p.nch, resident_row_bytes(in_f), kGemmWRows))
         return set_error(BF16X_ERR_CUDA, "bf16x_gemm: weight tensor map");
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: cuTensorMapEncodeTiled unavailable");
@@ -1357,10 +1354,7 @@ static int launch_gemm(GemmParams &p, const uint8_t *layout, int64_t in_f, const
 static int launch_gemm2sm(GemmParams &p, const uint8_t *layout, int64_t in_f, const uint16_t *x, int64_t ldx,
                           cudaStream_t st) {
     using C = Gemm2Cfg;
-    const cuuint64_t wdims[3] = {(cuuint64_t)(kChunkBytes / 4), (cuuint64_t)p.nch, (cuuint64_t)p.rows};
-    const cuuint64_t wstr[2] = {(cuuint64_t)kChunkBytes, (cuuint64_t)resident_row_bytes(in_f)};
-    const cuuint32_t wbox[3] = {(cuuint32_t)(kChunkBytes / 4), 1u, (cuuint32_t)kGemmWRows};
-    if (!encode_tiled(&p.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, layout, wdims, wstr, wbox))
+    if (!encode_resident_map(&p.wmap, layout, p.rows, p.nch, resident_row_bytes(in_f), kGemmWRows))
         return set_error(BF16X_ERR_CUDA, "bf16x_gemm: weight tensor map");
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: cuTensorMapEncodeTiled unavailable");

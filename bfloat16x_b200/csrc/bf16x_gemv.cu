@@ -9,19 +9,20 @@
 //     order; persistent CTAs of 8 warps split them stream-K style, every warp
 //     a contiguous, equal range, so every SM streams the same number of bytes
 //     whatever the shape;
-//   * each warp feeds itself: a ring of shared-memory slots filled by 1-D bulk
-//     copies (the TMA engine) -- 16 weight rows x 368 bytes, the activation
-//     slice, and the (tile, chunk) patch record -- completion counted on one
-//     mbarrier per slot; a slot is refilled right after it is consumed, so
-//     S items per warp are always in flight and no warp waits for another;
-//   * a lane decodes two 32-column groups (rows g and g+8) into bf16x2 pairs
-//     (about five integer ops per pair) and stores them, in mma fragment
-//     order, to a 4 KB per-warp buffer; the exact-delta patches of the item
-//     (delta > 7, ~3% of weights) are then scattered into that buffer as exact
-//     bf16 values, round-robin over all 32 lanes, and the fragments go to
-//     mma.m16n8k16 (rows x k) with the activations as the B operand
-//     (k x batch).  The tensor core does the multiply-accumulate, patches cost
-//     one 2-byte store each whatever the batch;
+//   * each warp feeds itself: a ring of shared-memory slots filled by the
+//     TMA engine -- 16 weight rows x 384 bytes (128-byte swizzled), the
+//     activation slice, and the (tile, chunk) patch record with the groups'
+//     emax -- completion counted on one mbarrier per slot; a slot is refilled
+//     right after it is consumed, so S items per warp are always in flight
+//     and no warp waits for another;
+//   * a lane decodes two 32-column groups (rows g and g+8) straight into the
+//     A fragments of mma.m16n8k16 (about five integer ops per pair of
+//     weights) and multiplies them with the activations as the B operand
+//     (k x batch): the tensor core does the multiply-accumulate.  The rare
+//     weights whose exponent is more than 15 below their group's largest
+//     enter the products saturated (exponent emax - 15); their record
+//     entries then add (exact - saturated) * x to the accumulators of their
+//     rows, so the sum is that of the exact weights;
 //   * a tile split between warps is finished by whichever warp arrives last
 //     (an atomic counter per tile in the workspace), summing the pieces in a
 //     fixed order, so results are deterministic and no warp ever waits;
@@ -42,43 +43,39 @@
 
 namespace bf16x {
 
-constexpr int kPcapWords = 192;      // patch-record words staged per slot (larger records: tail from L2)
-constexpr int kFragBytes = 8 * 32 * 16;   // one half chunk: 8 mma steps x 32 lanes x 4 registers
+constexpr int kPcapWords = 64;       // record words staged per slot: emax, header, 30 entries (more: from L2)
 constexpr int kXRowBytes = kChunkElems * 2;
 
-// Configuration per (batch bound, warps per CTA): ring depth per warp and
-// whether both half chunks are decoded before the patches and the mma (two
-// fragment buffers).  Long weights run 12 warps per SM with 2-slot rings;
-// short ones 8 warps with 3-slot rings (more bytes in flight per warp).
-#ifndef BF16X_GEMV_DUAL
-#define BF16X_GEMV_DUAL 0
-#endif
-
+// Configuration per (batch bound, warps per CTA).  Shared memory holds the
+// weight slots of all warps first (16 rows x 384 bytes each, 1024-byte
+// aligned for the 128-byte swizzle), then every warp's activation + record
+// slots, zeros, record offsets and mbarriers.  Long weights run 12 warps per
+// SM with 2-slot rings; short ones 8 warps with 3-slot rings (more bytes in
+// flight per warp).
 template <int BMAX, int NW>
 struct GemvCfg {
-    static constexpr bool kDual = BF16X_GEMV_DUAL != 0;
-    static constexpr int kWBytes = kTileRows * kChunkBytes;                 // 5888
-    static constexpr int kXOff = kWBytes;
-    static constexpr int kPOff = kXOff + BMAX * kXRowBytes;
-    static constexpr int kSlot = (kPOff + kPcapWords * 4 + 127) / 128 * 128;
-    static constexpr int kFrag = (kDual ? 2 : 1) * kFragBytes;
-    static constexpr int kBudget = 220 * 1024 - 1024;
-    static constexpr int kWarpsFit = kBudget / (2 * kSlot + kFrag);
+    static constexpr int kWBytes = kTileRows * kChunkBytes;                 // 6144
+    static constexpr int kPOff = BMAX * kXRowBytes;                         // record after the activations
+    static constexpr int kXRSlot = kPOff + kPcapWords * 4;
+    static constexpr int kPerSlot = kWBytes + kXRSlot;
+    static constexpr int kBudget = 220 * 1024 - 2048;
+    static constexpr int kWarpsFit = kBudget / (2 * kPerSlot);
     static constexpr int kWarps = NW < kWarpsFit ? NW : kWarpsFit;
-    static constexpr int kStagesFit = (kBudget / kWarps - kFrag) / kSlot;
+    static constexpr int kStagesFit = kBudget / kWarps / kPerSlot;
     static constexpr int kStages = kStagesFit < 3 ? kStagesFit : 3;
-    static constexpr int kWarpBytes = kStages * kSlot + kFrag;
-    static constexpr int kZeroOff = kWarps * kWarpBytes;                    // 512 zero bytes
-    static constexpr int kRecOff = kZeroOff + 512;                          // per slot record offset
+    static constexpr int kWOff = 0;                                          // [warp][stage] weight rows
+    static constexpr int kXROff = kWarps * kStages * kWBytes;                // [warp][stage] x + record
+    static constexpr int kZeroOff = kXROff + kWarps * kStages * kXRSlot;     // 512 zero bytes
+    static constexpr int kRecOff = kZeroOff + 512;                           // per slot record offset
     static constexpr int kBarOff = kRecOff + kWarps * kStages * 8;
-    static constexpr int kSmem = kBarOff + kWarps * kStages * 8;
+    static constexpr int kSmem = kBarOff + kWarps * kStages * 8 + 1024;      // + base alignment
     static_assert(kStages >= 2, "ring too shallow for this configuration");
-    static_assert(kSlot % 128 == 0 && kXOff % 128 == 0 && kPOff % 16 == 0, "slot alignment");
+    static_assert(kWBytes % 1024 == 0 && kXRSlot % 16 == 0 && kPOff % 16 == 0, "slot alignment");
     static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct GemvParams {
-    CUtensorMap wmap;   // resident layout as [rows][chunks][92 words], box 16 rows x 1 chunk
+    CUtensorMap wmap;   // resident layout [rows][chunks][3 lines], box 16 rows x 1 chunk, 128B swizzle
     CUtensorMap xmap;   // activations [batch][in_pad] bf16, box BMAX rows x 256 columns
     const uint8_t *layout;
     const int32_t *ptile_off;
@@ -107,18 +104,18 @@ __device__ __forceinline__ void mma_bf16_16816(float &c0, float &c1, float &c2, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Decode step J of one group: k-slots (2t, 2t+1 | 2t+8, 2t+9) of mma step J
-// carry the group's columns 4J..4J+3, i.e. pairs 2J (a0/a1) and 2J+1 (a2/a3)
-// of rows g (a0/a2) and g+8 (a1/a3).  The lane stores them as one 16-byte
-// fragment at frag[J][lane ^ J] (the slot order of frag_index).
+// Decode step J of one group pair: k-slots (2t, 2t+1 | 2t+8, 2t+9) of mma
+// step J carry the group's columns 4J..4J+3, i.e. pairs 2J (a0/a1) and 2J+1
+// (a2/a3) of rows g (a0/a2) and g+8 (a1/a3).
+struct StepFrag {
+    uint32_t a0, a1, a2, a3;
+};
+
 template <int J>
-__device__ __forceinline__ void group_to_frag(const uint32_t (&smA)[8], const uint32_t (&dA)[3], uint32_t eAlo,
-                                              uint32_t eAhi, const uint32_t (&smB)[8], const uint32_t (&dB)[3],
-                                              uint32_t eBlo, uint32_t eBhi, uint4 *frag, int lane) {
-    const uint32_t eA = J < 4 ? eAlo : eAhi, eB = J < 4 ? eBlo : eBhi;
-    frag[J * 32 + (lane ^ J)] = make_uint4(decode_pair<2 * J>(smA, dA, eA), decode_pair<2 * J>(smB, dB, eB),
-                                     decode_pair<2 * J + 1>(smA, dA, eA), decode_pair<2 * J + 1>(smB, dB, eB));
-    if constexpr (J + 1 < 8) group_to_frag<J + 1>(smA, dA, eAlo, eAhi, smB, dB, eBlo, eBhi, frag, lane);
+__device__ __forceinline__ StepFrag decode_step(const uint32_t (&smA)[8], const uint32_t (&dA)[4], uint32_t eA,
+                                                const uint32_t (&smB)[8], const uint32_t (&dB)[4], uint32_t eB) {
+    return StepFrag{decode_pair<2 * J>(smA, dA, eA), decode_pair<2 * J>(smB, dB, eB),
+                    decode_pair<2 * J + 1>(smA, dA, eA), decode_pair<2 * J + 1>(smB, dB, eB)};
 }
 
 // 16-byte shared-memory load by the lanes whose predicate is set; the others
@@ -130,34 +127,82 @@ __device__ __forceinline__ uint4 lds128_if(const void *ptr, bool pred) {
     return v;
 }
 
-// mma steps of one half chunk: A from the fragment buffer, B = x[g][group +
-// 4J .. +3], loaded 16 bytes at a time for steps J and J+1 by the lanes whose
+// The patch entries of the item: the first kPcapWords - kRecHdrWords are
+// staged in shared memory with the record, later ones are read from the
+// record in global memory (precs + *rof).
+struct ItemPatches {
+    const uint32_t *rec;
+    const uint32_t *precs;
+    const int64_t *rof;
+    __device__ __forceinline__ uint32_t entry(int j) const {
+        return kRecHdrWords + j < kPcapWords ? rec[kRecHdrWords + j] : __ldg(precs + *rof + kRecHdrWords + j);
+    }
+};
+
+// Correction of one patched weight (row rr, column cc of the item) in the
+// accumulators of the lane (g = rr % 8, t): its products went in with the
+// saturated value; add (exact - saturated) * x[b][cc] for the lane's batch
+// columns b = 2t, 2t+1 (and 8+2t, 8+2t+1 when BMAX > 8).
+template <int BMAX>
+__device__ __forceinline__ void correct_patch(uint32_t ent, uint32_t rr, uint32_t cc, const uint32_t *rec,
+                                              const uint16_t *xs, int t, float (&ce)[4], float (&de)[4]) {
+    const uint32_t ex = ent >> 16;
+    const uint32_t em = rec_emax(rec, (int)rr, (int)(cc >> 5));
+    const uint32_t sat = (ex & 0x807Fu) | (((em - kDeltaSat) & 0xFFu) << 7);
+    const float dv = bf16_bits_to_f32(ex) - bf16_bits_to_f32(sat);
+    const int b0 = 2 * t;
+    const bool top = rr < 8;                        // accumulator registers 0/1 (row g) or 2/3 (row g + 8)
+    const float x0 = b0 < BMAX ? bf16_bits_to_f32(xs[b0 * kChunkElems + cc]) : 0.f;
+    const float x1 = b0 + 1 < BMAX ? bf16_bits_to_f32(xs[(b0 + 1) * kChunkElems + cc]) : 0.f;
+    const float v0 = dv * x0, v1 = dv * x1;
+    ce[0] += top ? v0 : 0.f;
+    ce[1] += top ? v1 : 0.f;
+    ce[2] += top ? 0.f : v0;
+    ce[3] += top ? 0.f : v1;
+    if constexpr (BMAX > 8) {
+        const float v2 = dv * bf16_bits_to_f32(xs[(8 + b0) * kChunkElems + cc]);
+        const float v3 = dv * bf16_bits_to_f32(xs[(9 + b0) * kChunkElems + cc]);
+        de[0] += top ? v2 : 0.f;
+        de[1] += top ? v3 : 0.f;
+        de[2] += top ? 0.f : v2;
+        de[3] += top ? 0.f : v3;
+    }
+}
+
+template <int J>
+__device__ __forceinline__ void decode_half(StepFrag (&f)[8], const uint32_t (&smA)[8], const uint32_t (&dA)[4],
+                                            uint32_t eA, const uint32_t (&smB)[8], const uint32_t (&dB)[4],
+                                            uint32_t eB) {
+    f[J] = decode_step<J>(smA, dA, eA, smB, dB, eB);
+    if constexpr (J + 1 < 8) decode_half<J + 1>(f, smA, dA, eA, smB, dB, eB);
+}
+
+// mma steps J..7 of one half chunk, batch <= 8: B = x[g][group + 4J .. +3],
+// loaded 16 bytes at a time for steps J and J+1 by the lanes whose
 // activation row g exists (the B operand of the others is zero).  Even and
 // odd steps accumulate separately: two independent mma chains.
 template <int J>
-__device__ __forceinline__ void frag_mma(const uint4 *frag, int lane, const uint16_t *xq, bool hasx,
-                                         float (&ce)[4], float (&co)[4], uint4 bx = uint4{}) {
+__device__ __forceinline__ void half_mma(const StepFrag (&f)[8], const uint16_t *xq, bool hasx, float (&ce)[4],
+                                         float (&co)[4], uint4 bx = uint4{}) {
     if constexpr ((J & 1) == 0) bx = lds128_if(xq + 4 * J, hasx);
-    const uint4 a = frag[J * 32 + (lane ^ J)];
     float(&c)[4] = (J & 1) ? co : ce;
-    if constexpr ((J & 1) == 0) mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, bx.x, bx.y);
-    else mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, bx.z, bx.w);
-    if constexpr (J + 1 < 8) frag_mma<J + 1>(frag, lane, xq, hasx, ce, co, bx);
+    if constexpr ((J & 1) == 0) mma_bf16_16816(c[0], c[1], c[2], c[3], f[J].a0, f[J].a1, f[J].a2, f[J].a3, bx.x, bx.y);
+    else mma_bf16_16816(c[0], c[1], c[2], c[3], f[J].a0, f[J].a1, f[J].a2, f[J].a3, bx.z, bx.w);
+    if constexpr (J + 1 < 8) half_mma<J + 1>(f, xq, hasx, ce, co, bx);
 }
 
 // The same for 9..16 rows of activations: each A fragment feeds two mma,
 // one per group of 8 activation rows (x rows g and 8+g).
 template <int J>
-__device__ __forceinline__ void frag_mma2(const uint4 *frag, int lane, const uint16_t *xq, const uint16_t *xq2,
+__device__ __forceinline__ void half_mma2(const StepFrag (&f)[8], const uint16_t *xq, const uint16_t *xq2,
                                           float (&ce)[4], float (&co)[4], float (&de)[4], float (&dd)[4]) {
-    const uint4 a = frag[J * 32 + (lane ^ J)];
     const uint2 b = *reinterpret_cast<const uint2 *>(xq + 4 * J);
     const uint2 b2 = *reinterpret_cast<const uint2 *>(xq2 + 4 * J);
     float(&c)[4] = (J & 1) ? co : ce;
     float(&d)[4] = (J & 1) ? dd : de;
-    mma_bf16_16816(c[0], c[1], c[2], c[3], a.x, a.y, a.z, a.w, b.x, b.y);
-    mma_bf16_16816(d[0], d[1], d[2], d[3], a.x, a.y, a.z, a.w, b2.x, b2.y);
-    if constexpr (J + 1 < 8) frag_mma2<J + 1>(frag, lane, xq, xq2, ce, co, de, dd);
+    mma_bf16_16816(c[0], c[1], c[2], c[3], f[J].a0, f[J].a1, f[J].a2, f[J].a3, b.x, b.y);
+    mma_bf16_16816(d[0], d[1], d[2], d[3], f[J].a0, f[J].a1, f[J].a2, f[J].a3, b2.x, b2.y);
+    if constexpr (J + 1 < 8) half_mma2<J + 1>(f, xq, xq2, ce, co, de, dd);
 }
 
 // Warp w of the partition owns items [T*w/W, T*(w+1)/W); item i belongs to
@@ -169,7 +214,9 @@ template <int BMAX, int NW>
 __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     using C = GemvCfg<BMAX, NW>;
     constexpr int S = C::kStages;
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // the weight slots want a 1024-byte-aligned base (128-byte swizzle)
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff) + warp * S;
@@ -189,8 +236,8 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
     }
     const int64_t lo = item_lo(gw, p.T, p.W), hi = item_lo(gw + 1, p.T, p.W);
     const int64_t first_tile = lo / p.nch;
-    uint8_t *wsm = smem + warp * C::kWarpBytes;
-    uint4 *frag = reinterpret_cast<uint4 *>(wsm + S * C::kSlot);
+    uint8_t *wsm = smem + C::kWOff + warp * S * C::kWBytes;      // this warp's weight slots
+    uint8_t *xrs = smem + C::kXROff + warp * S * C::kXRSlot;     // its activation + record slots
     const uint16_t *zero_x = reinterpret_cast<const uint16_t *>(smem + C::kZeroOff);
 
     // ---- issue the copies of item (tile, c) into slot `s`: lane 0 alone,
@@ -198,12 +245,12 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
     auto issue = [&](int64_t tile, int c, int s, int32_t r_off, int32_t r_end) {
         if (lane == 0) {
             const int staged = min(r_end - r_off, kPcapWords);
-            uint8_t *slot = wsm + s * C::kSlot;
+            uint8_t *xr = xrs + s * C::kXRSlot;
             rec_of[s] = r_off;
             mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + BMAX * kXRowBytes + staged * 4));
-            tma_load_3d(slot, &p.wmap, 0, c, (int)(tile * kTileRows), &bars[s]);
-            tma_load_2d(slot + C::kXOff, &p.xmap, c * kChunkElems, 0, &bars[s]);
-            bulk_g2s(slot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
+            tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, c, (int)(tile * kTileRows), &bars[s]);
+            tma_load_2d(xr, &p.xmap, c * kChunkElems, 0, &bars[s]);
+            bulk_g2s(xr + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
         }
     };
 
@@ -235,12 +282,11 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         for (int s = 0; s < S && lo + s < hi; ++s) {
             const int32_t r_off = __shfl_sync(0xffffffffu, v, s), r_end = __shfl_sync(0xffffffffu, v, s + 1);
             if (lane == 0) {
-                uint8_t *slot = wsm + s * C::kSlot;
                 const int staged = min(r_end - r_off, kPcapWords);
                 rec_of[s] = r_off;
                 mbar_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
-                tma_load_3d(slot, &p.wmap, 0, cc, (int)(tl * kTileRows), &bars[s]);
-                bulk_g2s(slot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
+                tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, cc, (int)(tl * kTileRows), &bars[s]);
+                bulk_g2s(xrs + s * C::kXRSlot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
             }
             if (++cc == p.nch) { cc = 0; ++tl; }
         }
@@ -248,7 +294,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         for (int s = 0; s < S && i_it < hi; ++s) {
             if (lane == 0) {
                 mbar_arrive_expect_tx(&bars[s], (uint32_t)(BMAX * kXRowBytes));
-                tma_load_2d(wsm + s * C::kSlot + C::kXOff, &p.xmap, i_c * kChunkElems, 0, &bars[s]);
+                tma_load_2d(xrs + s * C::kXRSlot, &p.xmap, i_c * kChunkElems, 0, &bars[s]);
             }
             advance_issue();
         }
@@ -257,6 +303,10 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
     }
 
     const int g = lane >> 2, t = lane & 3;
+    // shared-memory offsets of this lane's groups t (half 0) and 4 + t
+    // (half 1) of row g in a staged item; row g + 8 is 8 x 384 bytes further
+    const GroupOffsets go[2] = {sw_group_offsets((uint32_t)g, (uint32_t)t), sw_group_offsets((uint32_t)g, 4u + t)};
+    constexpr int kRowB = 8 * kChunkBytes;
     constexpr int BW = BMAX > 8 ? 16 : 8;           // activation rows per partial-sum row
     constexpr int PW = 16 * BW;                     // floats per partial
     float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
@@ -320,91 +370,48 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
 
     for (int64_t it = lo; it < hi; ++it) {
         if (!mbar_wait(&bars[s], parity, &g_status)) return;
-        const uint8_t *slot = wsm + s * C::kSlot;
-        const uint16_t *xs = reinterpret_cast<const uint16_t *>(slot + C::kXOff);
-
-        // ---- per half chunk: decode to fragments, patch, multiply
+        const uint8_t *wsl = wsm + s * C::kWBytes;
+        const uint8_t *xr = xrs + s * C::kXRSlot;
+        const uint16_t *xs = reinterpret_cast<const uint16_t *>(xr);
         {
-            const uint32_t *rec = reinterpret_cast<const uint32_t *>(slot + C::kPOff);
-            const uint32_t hdr = rec[0];
-            // lane j holds record entries j, 32+j, 64+j, 96+j (zero past the end)
-            uint32_t pe[4];
-            {
-                const int n_all = (int)(hdr >> 16);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int j = 32 * k + lane;
-                    pe[k] = j < n_all ? rec[kRecHdrWords + j] : 0u;   // j < 128 <= staged capacity
-                }
-            }
-            const uint8_t *rowA = slot + g * kChunkBytes;
-            const uint8_t *rowB = rowA + 8 * kChunkBytes;
+            const uint32_t *rec = reinterpret_cast<const uint32_t *>(xr + C::kPOff);
+            const uint32_t hdr = rec[kRecHdr];
+            const uint2 ewA = *reinterpret_cast<const uint2 *>(rec + 2 * g);        // emax of row g, groups 0..7
+            const uint2 ewB = *reinterpret_cast<const uint2 *>(rec + 2 * g + 16);   // row g + 8
             const uint16_t *xg = g < BMAX ? xs + g * kChunkElems : zero_x;
             // both halves' compressed groups are read up front, so the
             // shared-memory latency overlaps the first half's decode
-            uint32_t smA[2][8], dA[2][3], eAlo[2], eAhi[2], smB[2][8], dB[2][3], eBlo[2], eBhi[2];
+            uint32_t smA[2][8], dA[2][4], smB[2][8], dB[2][4];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                load_group(rowA, 4 * h + t, smA[h], dA[h], eAlo[h], eAhi[h]);
-                load_group(rowB, 4 * h + t, smB[h], dB[h], eBlo[h], eBhi[h]);
+                load_group_sw(wsl, go[h], smA[h], dA[h]);
+                load_group_sw(wsl + kRowB, go[h], smB[h], dB[h]);
             }
-            if constexpr (!C::kDual) {
+            const ItemPatches ip{rec, p.precs, rec_of + s};
+            const int n_all = (int)(hdr >> 16);
+            const uint32_t pe0 = lane < n_all ? ip.entry(lane) : 0u;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int q = 4 * h + t;
-                    group_to_frag<0>(smA[h], dA[h], eAlo[h], eAhi[h], smB[h], dB[h], eBlo[h], eBhi[h], frag, lane);
-                    __syncwarp();
-                    // exact values of the patched weights of this half, stored
-                    // over their saturated decode: each entry carries its slot
-                    const int jlo = h ? (int)(hdr & 0xFFFFu) : 0;
-                    const int jhi = h ? (int)(hdr >> 16) : (int)(hdr & 0xFFFFu);
-                    uint16_t *frag16 = reinterpret_cast<uint16_t *>(frag);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int j = 32 * k + lane;
-                        if (j >= jlo && j < jhi) frag16[pe[k] & 0x7FFu] = (uint16_t)(pe[k] >> 16);
-                    }
-                    for (int j = (jlo > 128 ? jlo : 128) + lane; j < jhi; j += 32) {   // records past 128 entries
-                        const uint32_t ent = (kRecHdrWords + j < kPcapWords)
-                                                 ? rec[kRecHdrWords + j]
-                                                 : __ldg(p.precs + rec_of[s] + kRecHdrWords + j);
-                        frag16[ent & 0x7FFu] = (uint16_t)(ent >> 16);
-                    }
-                    __syncwarp();
-                    if constexpr (BMAX > 8) {
-                        const uint16_t *xg2 = xs + (8 + g) * kChunkElems;
-                        frag_mma2<0>(frag, lane, xg + 32 * q, xg2 + 32 * q, ce, co, de, dd);
-                    } else {
-                        frag_mma<0>(frag, lane, xg + 32 * q, g < BMAX, ce, co);
-                    }
-                    __syncwarp();
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t eA = emax_x2(((h ? ewA.y : ewA.x) >> (8 * t)) & 0xFFu);
+                const uint32_t eB = emax_x2(((h ? ewB.y : ewB.x) >> (8 * t)) & 0xFFu);
+                StepFrag f[8];
+                decode_half<0>(f, smA[h], dA[h], eA, smB[h], dB[h], eB);
+                const int q = 4 * h + t;
+                if constexpr (BMAX > 8) {
+                    half_mma2<0>(f, xg + 32 * q, xs + (8 + g) * kChunkElems + 32 * q, ce, co, de, dd);
+                } else {
+                    half_mma<0>(f, xg + 32 * q, g < BMAX, ce, co);
                 }
-            } else {
-                // both halves decoded first: 64 independent pairs per lane
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    group_to_frag<0>(smA[h], dA[h], eAlo[h], eAhi[h], smB[h], dB[h], eBlo[h], eBhi[h],
-                                     frag + h * (kFragBytes / 16), lane);
-                __syncwarp();
-                const int jhi = (int)(hdr >> 16);
-                uint16_t *frag16 = reinterpret_cast<uint16_t *>(frag);
-                for (int j = lane; j < jhi; j += 32) {
-                    const uint32_t ent = (kRecHdrWords + j < kPcapWords)
-                                             ? rec[kRecHdrWords + j]
-                                             : __ldg(p.precs + rec_of[s] + kRecHdrWords + j);
-                    frag16[ent & 0xFFFu] = (uint16_t)(ent >> 16);   // bit 11 = half selects the buffer
-                }
-                __syncwarp();
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    if constexpr (BMAX > 8) {
-                        const uint16_t *xg2 = xs + (8 + g) * kChunkElems;
-                        frag_mma2<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), xg2 + 32 * (4 * h + t),
-                                     ce, co, de, dd);
-                    } else {
-                        frag_mma<0>(frag + h * (kFragBytes / 16), lane, xg + 32 * (4 * h + t), g < BMAX, ce, co);
-                    }
-                __syncwarp();
+            }
+            // The patched weights entered the products with their saturated
+            // value (exponent emax - 15); add (exact - saturated) * x to the
+            // accumulators of their rows, in entry order (deterministic).
+            for (int e = 0; e < n_all; ++e) {
+                const uint32_t ent = e < 32 ? __shfl_sync(0xffffffffu, pe0, e) : ip.entry(e);
+                uint32_t rr, cc;
+                frag_position(ent, rr, cc);
+                if ((int)(rr & 7u) == g)
+                    correct_patch<BMAX>(ent, rr, cc, rec, xs, t, ce, de);
             }
         }
 
@@ -516,10 +523,7 @@ static bool cached_map(CUtensorMap *out, const MapKey &key, bool (*make)(CUtenso
 
 static bool make_wmap(CUtensorMap *m, const MapKey &k) {   // a = rows, b = in_f
     const int64_t nch = (k.b + kChunkElems - 1) / kChunkElems;
-    const cuuint64_t dims[3] = {(cuuint64_t)(kChunkBytes / 4), (cuuint64_t)nch, (cuuint64_t)k.a};
-    const cuuint64_t strides[2] = {(cuuint64_t)kChunkBytes, (cuuint64_t)resident_row_bytes(k.b)};
-    const cuuint32_t box[3] = {(cuuint32_t)(kChunkBytes / 4), 1u, (cuuint32_t)kTileRows};
-    return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, k.ptr, dims, strides, box);
+    return encode_resident_map(m, k.ptr, k.a, nch, resident_row_bytes(k.b), kTileRows);
 }
 
 static bool make_xmap(CUtensorMap *m, const MapKey &k) {   // a = in_pad, b = batch, c = ldx | bmax << 40

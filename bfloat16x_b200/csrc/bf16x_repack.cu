@@ -6,8 +6,9 @@
 // Bf16xGemmLinear.__init__ pads and stages them (bf16x_gemm_fused.py:163-184).
 // Here each row is decoded exactly from the flat streams (overflow table
 // applied with the reference decode's rule, opqk_linear.py:364-376) and
-// re-encoded with row-local 16-column sub-blocks, so any in_f works (the flat
-// sub-blocks of the dict may straddle rows when in_f % 16 != 0).
+// re-encoded with row-local 32-column groups and 4-bit deltas, so any in_f
+// works (the flat 16-element sub-blocks of the dict may straddle rows when
+// in_f % 16 != 0).
 //
 //   repack_count_kernel : CTA per 16-row tile, record sizes per (tile, chunk)
 //   scan_kernel         : exclusive scan of the sizes into ptile_off
@@ -33,13 +34,13 @@ __device__ __forceinline__ RowSlice row_ovf_slice(const FlatStreams &f, int64_t 
     return s;
 }
 
-// Re-encode the 8 columns [c*256 + 8*lane, +8) of one row.  Returns the
-// patch mask (bit i = column i needs a patch) and fills sm bytes, stored
-// deltas, exact deltas and the sub-block emax.
+// Re-encode the 8 columns [c*256 + 8*lane, +8) of one row (lanes 4q..4q+3
+// = group q).  Returns the patch mask (bit i = column i needs a patch) and
+// fills sm bytes, stored deltas, exact deltas and the group's emax.
 struct Enc8 {
     uint32_t sm[8];
     uint32_t d[8];       // exact delta (0..255)
-    uint32_t stored[8];  // min(delta, 7)
+    uint32_t stored[8];  // min(delta, 15)
     uint32_t emax;
     uint32_t pmask;
 };
@@ -56,7 +57,8 @@ __device__ __forceinline__ Enc8 encode8(const FlatStreams &f, int64_t pos0, int6
         bits[i] = k < in_f ? flat_exact_bits(f, pos0 + k, s.lo, s.hi, 16) : 0u;
         if (k < in_f) em = max(em, (bits[i] >> 7) & 0xFFu);
     }
-    em = max(em, __shfl_xor_sync(0xffffffffu, em, 1));   // lanes 2s, 2s+1 = sub-block s
+    em = max(em, __shfl_xor_sync(0xffffffffu, em, 1));   // lanes 4q..4q+3 = group q
+    em = max(em, __shfl_xor_sync(0xffffffffu, em, 2));
     r.emax = em;
     r.pmask = 0;
 #pragma unroll
@@ -66,12 +68,12 @@ __device__ __forceinline__ Enc8 encode8(const FlatStreams &f, int64_t pos0, int6
             const uint32_t ex = (bits[i] >> 7) & 0xFFu;
             r.d[i] = em - ex;
             r.sm[i] = ((bits[i] >> 8) & 0x80u) | (bits[i] & 0x7Fu);
-            if (r.d[i] > 7u) r.pmask |= 1u << i;
+            if (r.d[i] > kDeltaSat) r.pmask |= 1u << i;
         } else {
-            r.d[i] = min(em, 7u);   // padding column: finite, multiplied by a zero x
+            r.d[i] = min(em, kDeltaSat);   // padding column: finite, multiplied by a zero x
             r.sm[i] = 0u;
         }
-        r.stored[i] = min(r.d[i], 7u);
+        r.stored[i] = min(r.d[i], kDeltaSat);
     }
     return r;
 }
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(int32_t *a, int64_t n) {
 }
 
 // One CTA per 16-row tile, one warp per row.  Counts the patches (exact delta
-// > 7) of every (tile, chunk) and writes the record sizes in words.
+// > 15) of every (tile, chunk) and writes the record sizes in words.
 __global__ void __launch_bounds__(kTileRows * 32)
 repack_count_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int nch, int32_t *rec_sizes) {
     extern __shared__ int cnt[];   // [nch]
@@ -140,9 +142,8 @@ repack_count_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int
 }
 
 // One CTA per 16-row tile: pass A counts each row's patches per chunk and
-// quarter (64-column block), pass B writes the resident chunks, the record
-// headers and the entries sorted by (quarter, row, column); repack_order_kernel
-// then reorders each quarter for the GEMV's shared-memory banks.
+// quarter (64-column block), pass B writes the resident chunks, the records'
+// emax bytes and headers, and the entries sorted by (quarter, row, column).
 __global__ void __launch_bounds__(kTileRows * 32)
 repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int nch,
                     const int32_t *__restrict__ ptile_off, uint8_t *__restrict__ layout,
@@ -181,46 +182,31 @@ repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int
         const int n_q0 = qtot[0], n_low = qtot[0] + qtot[1], n_q012 = n_low + qtot[2], n_all = n_q012 + qtot[3];
         uint32_t *rec = precs + ptile_off[tile * nch + c];
         if (warp == 0 && lane == 0) {
-            rec[0] = (uint32_t)n_low | ((uint32_t)n_all << 16);
-            rec[1] = (uint32_t)n_q0 | ((uint32_t)n_q012 << 16);
+            rec[kRecHdr] = (uint32_t)n_low | ((uint32_t)n_all << 16);
+            rec[kRecHdr + 1] = (uint32_t)n_q0 | ((uint32_t)n_q012 << 16);
         }
         if (warp == kTileRows - 1) {
             const int64_t used = kRecHdrWords + n_all, words = rec_words(n_all);
             for (int64_t w = used + lane; w < words; w += 32) rec[w] = 0u;
         }
-        if (!valid) continue;
+        if (!valid) {
+            if (lane < 2) rec[2 * warp + lane] = 0u;   // emax of a row past the end
+            continue;
+        }
         const Enc8 e = encode8(f, pos0, in_f, c, s);
         uint8_t *chunk = row + (int64_t)c * kChunkBytes;
         uint2 smv;
         smv.x = e.sm[0] | (e.sm[1] << 8) | (e.sm[2] << 16) | (e.sm[3] << 24);
         smv.y = e.sm[4] | (e.sm[5] << 8) | (e.sm[6] << 16) | (e.sm[7] << 24);
         *reinterpret_cast<uint2 *>(chunk + kSmOff + 8 * lane) = smv;
-        uint32_t w0 = 0, w1 = 0, w2 = 0;
+        // the lane's 8 columns are pairs 4(lane&3)..+3 of group lane>>2: one
+        // delta word, at slot pp for its pair pp
+        uint32_t dword = 0;
 #pragma unroll
-        for (int pp = 0; pp < 4; ++pp) {
-            const int p = 4 * (lane & 3) + pp;
-            const uint32_t d0 = e.stored[2 * pp], d1 = e.stored[2 * pp + 1];
-            if (p < 15) {
-                const int slot = p % 5;
-                const uint32_t v = (d0 << (3 * slot)) | (d1 << (16 + 3 * slot));
-                if (p / 5 == 0) w0 |= v; else if (p / 5 == 1) w1 |= v; else w2 |= v;
-            } else {
-                w0 |= ((d0 & 1u) << 15) | ((d1 & 1u) << 31);
-                w1 |= (((d0 >> 1) & 1u) << 15) | (((d1 >> 1) & 1u) << 31);
-                w2 |= (((d0 >> 2) & 1u) << 15) | (((d1 >> 2) & 1u) << 31);
-            }
-        }
-#pragma unroll
-        for (int o = 1; o <= 2; o <<= 1) {
-            w0 |= __shfl_xor_sync(0xffffffffu, w0, o);
-            w1 |= __shfl_xor_sync(0xffffffffu, w1, o);
-            w2 |= __shfl_xor_sync(0xffffffffu, w2, o);
-        }
-        if ((lane & 3) == 0) {
-            uint32_t *dp = reinterpret_cast<uint32_t *>(chunk + kDOff + 12 * (lane >> 2));
-            dp[0] = w0; dp[1] = w1; dp[2] = w2;
-        }
-        if ((lane & 1) == 0) chunk[kEOff + (lane >> 1)] = (uint8_t)e.emax;
+        for (int pp = 0; pp < 4; ++pp)
+            dword |= (e.stored[2 * pp] << (4 * pp)) | (e.stored[2 * pp + 1] << (16 + 4 * pp));
+        *reinterpret_cast<uint32_t *>(chunk + kDOff + 4 * lane) = dword;
+        if ((lane & 3) == 0) reinterpret_cast<uint8_t *>(rec)[8 * warp + (lane >> 2)] = (uint8_t)e.emax;
         // ordered entries: exclusive prefix of the per-lane counts within the quarter
         const int n = __popc(e.pmask);
         int x = n;
@@ -242,56 +228,6 @@ repack_write_kernel(FlatStreams f, int64_t in_f, int64_t row0, int64_t row1, int
     }
 }
 
-// Orders the entries of every (tile, chunk, quarter) for the GEMV's patch
-// stores: 32 lanes store 32 consecutive entries at once, and entries whose
-// fragment words share a shared-memory bank serialise.  Within each quarter
-// (the GEMM reads a quarter's entries as one range, in any order) the
-// entries are dealt bank by bank: the r-th entry of every bank comes before
-// the (r+1)-th of any, banks in increasing order, ties in their previous
-// (row, column) order -- deterministic.  One warp per quarter.
-__global__ void __launch_bounds__(128) repack_order_kernel(const int32_t *__restrict__ ptile_off,
-                                                           uint32_t *__restrict__ precs) {
-    __shared__ uint32_t ent[4][kTileRows * 64];     // a quarter holds at most 16 x 64 entries
-    __shared__ uint16_t rnk[4][kTileRows * 64];
-    __shared__ int cnt[4][32];
-    const int q = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint32_t *rec = precs + ptile_off[blockIdx.x];
-    const uint32_t h0 = rec[0], h1 = rec[1];
-    const int bq[5] = {0, (int)(h1 & 0xFFFFu), (int)(h0 & 0xFFFFu), (int)(h1 >> 16), (int)(h0 >> 16)};
-    const int lo = bq[q], n = bq[q + 1] - bq[q];
-    if (n <= 1) return;
-    uint32_t *src = rec + kRecHdrWords + lo;
-    cnt[q][lane] = 0;
-    __syncwarp();
-    for (int b0 = 0; b0 < n; b0 += 32) {
-        const int i = b0 + lane;
-        const bool on = i < n;
-        const uint32_t e = on ? src[i] : 0u;
-        const uint32_t bank = ((e & 0x7FFu) >> 1) & 31u;
-        const uint32_t act = __ballot_sync(0xffffffffu, on);
-        const uint32_t same = __match_any_sync(0xffffffffu, on ? bank : 32u + lane) & act;
-        const int before = __popc(same & ((1u << lane) - 1u));
-        if (on) {
-            ent[q][i] = e;
-            rnk[q][i] = (uint16_t)(cnt[q][bank] + before);
-        }
-        __syncwarp();
-        if (on && before == 0) cnt[q][bank] += __popc(same);   // the first lane of each bank group
-        __syncwarp();
-    }
-    for (int i = lane; i < n; i += 32) {
-        const uint32_t e = ent[q][i];
-        const int bank = (int)(((e & 0x7FFu) >> 1) & 31u), r = rnk[q][i];
-        int pos = 0;
-        for (int b = 0; b < 32; ++b) {
-            const int c = cnt[q][b];
-            pos += c < r ? c : r;                   // rank < r of every bank
-            if (b < bank && c > r) ++pos;           // rank r of the lower banks
-        }
-        src[pos] = e;
-    }
-}
-
 // Checks that the overflow index is strictly ascending inside [0, n).
 __global__ void validate_ovf_kernel(const int32_t *idx, int64_t n_ovf, int64_t n) {
     for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n_ovf;
@@ -303,8 +239,8 @@ __global__ void validate_ovf_kernel(const int32_t *idx, int64_t n_ovf, int64_t n
 }
 
 // Resident layout -> bf16 bits.  One CTA per 16-row tile: warp w decodes row
-// w (lane = one 32-column group, lanes 8u..8u+7 cover chunk 4*it + u), then
-// the CTA applies the tile's patch records.
+// w (lane = one 32-column group, lanes 8u..8u+7 cover chunk 4*it + u, emax
+// from the chunk's record), then the CTA applies the tile's patch entries.
 __global__ void __launch_bounds__(kTileRows * 32)
 resident_decode_kernel(const uint8_t *__restrict__ layout, const int32_t *__restrict__ ptile_off,
                        const uint32_t *__restrict__ precs, int64_t rows, int64_t in_f,
@@ -319,10 +255,11 @@ resident_decode_kernel(const uint8_t *__restrict__ layout, const int32_t *__rest
         uint16_t *orow = out + r * ld_out;
         for (int c = lane >> 3; c < nch; c += 4) {
             const int q = lane & 7;
-            uint32_t sm[8], dw[3], e2lo, e2hi;
-            load_group(row + (int64_t)c * kChunkBytes, q, sm, dw, e2lo, e2hi);
+            uint32_t sm[8], dw[4];
+            load_group(row + (int64_t)c * kChunkBytes, q, sm, dw);
+            const uint32_t e2 = emax_x2(rec_emax(precs + ptile_off[tile * nch + c], warp, q));
             GroupPairs g;
-            decode_pairs_from<0>(g, sm, dw, e2lo, e2hi);
+            decode_pairs_from<0>(g, sm, dw, e2);
             const int64_t k0 = (int64_t)c * kChunkElems + 32 * q;
             if (k0 + 32 <= in_f && vec_ok) {
                 uint4 *dst = reinterpret_cast<uint4 *>(orow + k0);
@@ -339,7 +276,7 @@ resident_decode_kernel(const uint8_t *__restrict__ layout, const int32_t *__rest
     __syncthreads();
     for (int c = 0; c < nch; ++c) {
         const uint32_t *rec = precs + ptile_off[tile * nch + c];
-        const int n_all = (int)(rec[0] >> 16);
+        const int n_all = (int)(rec[kRecHdr] >> 16);
         for (int j = threadIdx.x; j < n_all; j += blockDim.x) {
             const uint32_t ent = rec[kRecHdrWords + j];
             uint32_t rt, cc;
@@ -422,11 +359,7 @@ extern "C" int bf16x_repack(const uint32_t *sign, int64_t n_sign_words,
     const int64_t n_tiles = (rows + kTileRows - 1) / kTileRows;
     repack_write_kernel<<<(unsigned)n_tiles, kTileRows * 32, 4 * kTileRows * nch * sizeof(uint16_t),
                           (cudaStream_t)stream>>>(f, in_f, row0, row1, nch, ptile_off, layout, precs);
-    if (int rc2 = check_launch("repack_write_kernel")) return rc2;
-    const int64_t n_rec = n_tiles * nch;
-    if (n_rec > 0x7fffffffLL) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_repack: too many records");
-    repack_order_kernel<<<(unsigned)n_rec, 128, 0, (cudaStream_t)stream>>>(ptile_off, precs);
-    return check_launch("repack_order_kernel");
+    return check_launch("repack_write_kernel");
 }
 
 extern "C" int bf16x_resident_decode(const uint8_t *layout, const int32_t *ptile_off,

@@ -1,10 +1,11 @@
 """Device-resident BF16X weights in the kernel layout.
 
 ``ResidentWeight`` is what the fused Linear modules hold: the weight rows in
-the resident layout (chunks of 256 columns, 368 bytes each: sign|mant bytes,
-pair-aligned 3-bit deltas, row-local emax -- 11.5 bits per weight) plus a
-patch record per (16-row tile, 256-column chunk) for the ~3% of weights whose
-exponent is more than 7 below their sub-block maximum.  It is built once from a
+the resident layout (chunks of 256 columns, 384 bytes each: sign|mant bytes
+and pair-aligned 4-bit deltas -- 12 bits per weight) plus a record per
+(16-row tile, 256-column chunk) holding the emax of every 32-column group of
+its rows (1/4 bit per weight) and the rare weights whose exponent is more
+than 15 below their group's largest.  It is built once from a
 bf16x_quantize dict by the ``bf16x_repack_count`` / ``bf16x_repack`` kernels
 (the counterpart of the reference modules' device preparation,
 bf16x_fused.py:154-192 and bf16x_gemm_fused.py:163-184) and can hold a row
@@ -15,7 +16,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import BF16X_DTYPE_BF16, BF16X_DTYPE_F32, CHUNK_BYTES, CHUNK_ELEMS, TILE_ROWS, call, ptr
+from ._lib import BF16X_DTYPE_BF16, BF16X_DTYPE_F32, CHUNK_BYTES, CHUNK_ELEMS, REC_HDR_WORD, TILE_ROWS, call, ptr
 
 _FLAT = ("sign_packed", "mant_packed", "delta_packed", "emax", "delta_ovf_idx", "delta_ovf_val")
 
@@ -159,7 +160,7 @@ class ResidentWeight:
     def n_patches(self) -> int:
         """Number of exact-delta patches (entries of all records)."""
         if self._n_patches is None:
-            offs = self.ptile_off[:-1].long()
+            offs = self.ptile_off[:-1].long() + REC_HDR_WORD
             n_all = self.precs.view(torch.int16)[offs * 2 + 1].to(torch.int32) & 0xFFFF
             self._n_patches = int(n_all.sum().item())
         return self._n_patches

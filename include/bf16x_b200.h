@@ -19,12 +19,13 @@
  *                    table idx (int32 ascending flat positions) + val (u8 true
  *                    delta, >= 7).
  *   resident layout: the kernel layout built once per weight by bf16x_repack:
- *                    rows of ceil(in_f/256) chunks of 368 bytes
- *                    ([256 B sign|mant bytes][96 B pair-aligned deltas][16 B emax]),
- *                    i.e. the same 11.5 bits per weight, plus one patch record
- *                    per (16-row tile, 256-column chunk) for the weights whose
- *                    exact exponent delta exceeds 7: two header words of
- *                    per-quarter entry counts, then u32 entries
+ *                    rows of ceil(in_f/256) chunks of 384 bytes
+ *                    ([256 B sign|mant bytes][128 B pair-aligned 4-bit deltas]),
+ *                    12 bits per weight, plus one record per (16-row tile,
+ *                    256-column chunk): the emax of each 32-column group of
+ *                    its rows (128 B), two header words of per-quarter entry
+ *                    counts, then u32 entries for the weights whose exact
+ *                    exponent delta exceeds 15,
  *                    mma-fragment slot (11 b) | column half << 11 | exact bf16 << 16,
  *                    sorted by (64-column quarter, row, column).
  *   GGUF blocks    : 46-byte blocks of 32 weights (bf16x_gguf_block.py:6-17).
@@ -51,7 +52,7 @@ extern "C" {
 #define BF16X_DTYPE_F32_TRUNC 2
 
 #define BF16X_CHUNK_ELEMS 256
-#define BF16X_CHUNK_BYTES 368
+#define BF16X_CHUNK_BYTES 384
 
 /* ---- library ----------------------------------------------------------- */
 int bf16x_version(void);
@@ -98,8 +99,9 @@ int bf16x_quantize(const uint16_t *w, int64_t n, int sub, const void *scratch,
  * (bf16x_fused.py:154-192: _pad1 + CSR build) and Bf16xGemmLinear.__init__
  * (bf16x_gemm_fused.py:163-184).  Rows [row0, row1) of the flat dict are
  * decoded exactly (overflow applied) and re-encoded into the resident layout:
- * row-major chunks of 368 bytes, and one patch record per (16-row tile,
- * 256-column chunk) holding the weights whose exact exponent delta exceeds 7.
+ * row-major chunks of 384 bytes, and one record per (16-row tile, 256-column
+ * chunk) holding the groups' emax and the weights whose exact exponent delta
+ * exceeds 15.
  *   bf16x_resident_row_bytes: bytes per row of the layout.
  *   bf16x_repack_count: record sizes -> ptile_off[0..n_tiles*n_chunks]
  *                       (device int32, exclusive scan in words; the last

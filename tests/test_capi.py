@@ -45,10 +45,10 @@ def test_stream_words_matches_reference_rule(L, n, b):
 
 
 def test_resident_row_bytes(L):
-    assert L.bf16x_resident_row_bytes(256) == 368
-    assert L.bf16x_resident_row_bytes(4096) == 16 * 368
-    assert L.bf16x_resident_row_bytes(257) == 2 * 368
-    assert L.bf16x_resident_row_bytes(14336) == 56 * 368
+    assert L.bf16x_resident_row_bytes(256) == 384
+    assert L.bf16x_resident_row_bytes(4096) == 16 * 384
+    assert L.bf16x_resident_row_bytes(257) == 2 * 384
+    assert L.bf16x_resident_row_bytes(14336) == 56 * 384
 
 
 def _err(L):

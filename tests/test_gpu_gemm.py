@@ -71,8 +71,8 @@ def test_gemm_large_m_deterministic():
 
 
 def _dense_patch_weight(rows, in_f, seed):
-    # magnitudes spread over 2^-40..2^0: most weights sit more than 7 binades
-    # below their 16-column maximum, so records overflow every staging limit
+    # magnitudes spread over 2^-40..2^0: most weights sit more than 15 binades
+    # below their 32-column maximum, so records overflow every staging limit
     g = torch.Generator().manual_seed(seed)
     e = torch.randint(-40, 1, (rows, in_f), generator=g).float()
     m = 1.0 + torch.rand(rows, in_f, generator=g)

@@ -30,10 +30,20 @@ def test_repack_roundtrip_and_patch_count(shape):
     p = oracle_dict(w)
     rw = ResidentWeight.from_packed(p, device="cuda")
     assert np.array_equal(bits_of(rw.decode()), w)
-    if shape[1] % 16 == 0:
-        # row-local sub-blocks equal the flat ones: patches == table entries with delta > 7
-        assert rw.n_patches == int((p["delta_ovf_val"] > 7).sum())
-    assert rw.layout.shape[1] == (shape[1] + 255) // 256 * 368
+    assert rw.n_patches == expected_patches(w)
+    assert rw.layout.shape[1] == (shape[1] + 255) // 256 * 384
+
+
+def expected_patches(w_bits):
+    """Weights whose exponent is more than 15 below the largest of their
+    row-local 32-column group (columns padded to a multiple of 256)."""
+    rows, in_f = w_bits.shape
+    pad = (in_f + 255) // 256 * 256
+    e = np.zeros((rows, pad), dtype=np.int16)
+    e[:, :in_f] = (w_bits >> 7) & 0xFF
+    g = e.reshape(rows, pad // 32, 32)
+    d = g.max(axis=2, keepdims=True) - g
+    return int((d.reshape(rows, pad)[:, :in_f] > 15).sum())
 
 
 def test_repack_row_range():
