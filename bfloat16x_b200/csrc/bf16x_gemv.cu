@@ -139,33 +139,41 @@ struct ItemPatches {
     }
 };
 
-// Correction of one patched weight (row rr, column cc of the item) in the
-// accumulators of the lane (g = rr % 8, t): its products went in with the
-// saturated value; add (exact - saturated) * x[b][cc] for the lane's batch
-// columns b = 2t, 2t+1 (and 8+2t, 8+2t+1 when BMAX > 8).
-template <int BMAX>
-__device__ __forceinline__ void correct_patch(uint32_t ent, uint32_t rr, uint32_t cc, const uint32_t *rec,
-                                              const uint16_t *xs, int t, float (&ce)[4], float (&de)[4]) {
+// (exact - saturated) value of a patched weight: its products go in with the
+// saturated decode (exponent emax - 15, same sign and mantissa).
+__device__ __forceinline__ float patch_delta(uint32_t ent, uint32_t emax) {
     const uint32_t ex = ent >> 16;
-    const uint32_t em = rec_emax(rec, (int)rr, (int)(cc >> 5));
-    const uint32_t sat = (ex & 0x807Fu) | (((em - kDeltaSat) & 0xFFu) << 7);
-    const float dv = bf16_bits_to_f32(ex) - bf16_bits_to_f32(sat);
+    const uint32_t sat = (ex & 0x807Fu) | (((emax - kDeltaSat) & 0xFFu) << 7);
+    return bf16_bits_to_f32(ex) - bf16_bits_to_f32(sat);
+}
+
+// Correction of one patched weight (row rr, column cc of the item; dv = 0
+// when there is none), taken by the four lanes with g = rr % 8: dv * x[b][cc]
+// for the lane's batch columns b = 2t, 2t+1 (and 8+2t, 8+2t+1 when BMAX > 8)
+// into the correction sums pc / pd, laid out like the mma accumulators
+// (registers 0/1 row g, 2/3 row g + 8).  No branches: the other lanes add 0.
+template <int BMAX>
+__device__ __forceinline__ void add_patch(uint32_t key, float dv, bool on, int g, int t, const uint16_t *xs,
+                                          float (&pc)[4], float (&pd)[4]) {
+    const uint32_t rr = key >> 8, cc = key & 0xFFu;
+    const bool mine = on && (int)(rr & 7u) == g;
+    const float w = mine ? dv : 0.f;
+    const bool top = rr < 8;
     const int b0 = 2 * t;
-    const bool top = rr < 8;                        // accumulator registers 0/1 (row g) or 2/3 (row g + 8)
     const float x0 = b0 < BMAX ? bf16_bits_to_f32(xs[b0 * kChunkElems + cc]) : 0.f;
     const float x1 = b0 + 1 < BMAX ? bf16_bits_to_f32(xs[(b0 + 1) * kChunkElems + cc]) : 0.f;
-    const float v0 = dv * x0, v1 = dv * x1;
-    ce[0] += top ? v0 : 0.f;
-    ce[1] += top ? v1 : 0.f;
-    ce[2] += top ? 0.f : v0;
-    ce[3] += top ? 0.f : v1;
+    const float v0 = mine ? w * x0 : 0.f, v1 = mine ? w * x1 : 0.f;
+    pc[0] += top ? v0 : 0.f;
+    pc[1] += top ? v1 : 0.f;
+    pc[2] += top ? 0.f : v0;
+    pc[3] += top ? 0.f : v1;
     if constexpr (BMAX > 8) {
-        const float v2 = dv * bf16_bits_to_f32(xs[(8 + b0) * kChunkElems + cc]);
-        const float v3 = dv * bf16_bits_to_f32(xs[(9 + b0) * kChunkElems + cc]);
-        de[0] += top ? v2 : 0.f;
-        de[1] += top ? v3 : 0.f;
-        de[2] += top ? 0.f : v2;
-        de[3] += top ? 0.f : v3;
+        const float v2 = mine ? w * bf16_bits_to_f32(xs[(8 + b0) * kChunkElems + cc]) : 0.f;
+        const float v3 = mine ? w * bf16_bits_to_f32(xs[(9 + b0) * kChunkElems + cc]) : 0.f;
+        pd[0] += top ? v2 : 0.f;
+        pd[1] += top ? v3 : 0.f;
+        pd[2] += top ? 0.f : v2;
+        pd[3] += top ? 0.f : v3;
     }
 }
 
@@ -311,6 +319,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
     constexpr int PW = 16 * BW;                     // floats per partial
     float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};
     float de[4] = {0.f, 0.f, 0.f, 0.f}, dd[4] = {0.f, 0.f, 0.f, 0.f};   // rows 8..15 (BMAX > 8)
+    float pc[4] = {0.f, 0.f, 0.f, 0.f}, pd[4] = {0.f, 0.f, 0.f, 0.f};   // patch corrections
     int64_t tile = first_tile;
     int c = (int)(lo - first_tile * p.nch);
     int tile_c0 = c;                                // first chunk of the current tile in this range
@@ -389,7 +398,34 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
             }
             const ItemPatches ip{rec, p.precs, rec_of + s};
             const int n_all = (int)(hdr >> 16);
-            const uint32_t pe0 = lane < n_all ? ip.entry(lane) : 0u;
+            // entry `lane` of the item, decoded by its lane: row << 8 | column, delta
+            uint32_t pkey = 0u;
+            float pdv = 0.f;
+            if (lane < n_all) {
+                const uint32_t ent = ip.entry(lane);
+                uint32_t rr, cc;
+                frag_position(ent, rr, cc);
+                pkey = rr << 8 | cc;
+                pdv = patch_delta(ent, rec_emax(rec, (int)rr, (int)(cc >> 5)));
+            }
+            // The patched weights enter the products with their saturated
+            // value; add (exact - saturated) * x to the correction sums of
+            // their rows, in entry order (deterministic).  Done while the
+            // compressed groups are still on their way from shared memory.
+            const int n_reg = n_all < 32 ? n_all : 32;
+            for (int e = 0; e < n_reg; e += 2) {      // two entries per pass: independent chains
+                const uint32_t k0 = __shfl_sync(0xffffffffu, pkey, e), k1 = __shfl_sync(0xffffffffu, pkey, e + 1);
+                const float v0 = __shfl_sync(0xffffffffu, pdv, e), v1 = __shfl_sync(0xffffffffu, pdv, e + 1);
+                add_patch<BMAX>(k0, v0, true, g, t, xs, pc, pd);
+                add_patch<BMAX>(k1, v1, e + 1 < n_reg, g, t, xs, pc, pd);
+            }
+            for (int e = 32; e < n_all; ++e) {        // past 32 entries: from the record
+                const uint32_t ent = ip.entry(e);
+                uint32_t rr, cc;
+                frag_position(ent, rr, cc);
+                add_patch<BMAX>(rr << 8 | cc, patch_delta(ent, rec_emax(rec, (int)rr, (int)(cc >> 5))), true, g, t,
+                                xs, pc, pd);
+            }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const uint32_t eA = emax_x2(((h ? ewA.y : ewA.x) >> (8 * t)) & 0xFFu);
@@ -402,16 +438,6 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                 } else {
                     half_mma<0>(f, xg + 32 * q, g < BMAX, ce, co);
                 }
-            }
-            // The patched weights entered the products with their saturated
-            // value (exponent emax - 15); add (exact - saturated) * x to the
-            // accumulators of their rows, in entry order (deterministic).
-            for (int e = 0; e < n_all; ++e) {
-                const uint32_t ent = e < 32 ? __shfl_sync(0xffffffffu, pe0, e) : ip.entry(e);
-                uint32_t rr, cc;
-                frag_position(ent, rr, cc);
-                if ((int)(rr & 7u) == g)
-                    correct_patch<BMAX>(ent, rr, cc, rec, xs, t, ce, de);
             }
         }
 
@@ -427,8 +453,10 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
 
         // ---- tile finished (or range ends inside it)
         if (c == p.nch - 1 || it == hi - 1) {
-            const float c0 = ce[0] + co[0], c1 = ce[1] + co[1], c2 = ce[2] + co[2], c3 = ce[3] + co[3];
-            const float d0 = de[0] + dd[0], d1 = de[1] + dd[1], d2 = de[2] + dd[2], d3 = de[3] + dd[3];
+            const float c0 = ce[0] + co[0] + pc[0], c1 = ce[1] + co[1] + pc[1];
+            const float c2 = ce[2] + co[2] + pc[2], c3 = ce[3] + co[3] + pc[3];
+            const float d0 = de[0] + dd[0] + pd[0], d1 = de[1] + dd[1] + pd[1];
+            const float d2 = de[2] + dd[2] + pd[2], d3 = de[3] + dd[3] + pd[3];
             const int64_t row0 = tile * kTileRows;
             const bool whole = tile_c0 == 0 && c == p.nch - 1;
             if (whole) {
@@ -465,7 +493,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                 if (__shfl_sync(0xffffffffu, old, 0) == pieces_before(tile)) reduce_split(tile);
             }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) ce[k] = co[k] = de[k] = dd[k] = 0.f;
+            for (int k = 0; k < 4; ++k) ce[k] = co[k] = de[k] = dd[k] = pc[k] = pd[k] = 0.f;
             tile_c0 = 0;
         }
         if (++s == S) { s = 0; parity ^= 1u; }
