@@ -340,26 +340,26 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         // tile; every later warp's range begins in this tile: slot 0
         const int sl_first = item_lo(w_first, p.T, p.W) < tl * p.nch ? 1 : 0;
         constexpr int KN = PW / 32;                 // values per lane
+        constexpr int KB = KN > 4 ? 4 : 8;          // pieces loaded per round
+        const int np = (int)(w_last - w_first) + 1;
         float o4[KN];
-        {
-            const float *src = p.partials + (w_first * 2 + sl_first) * PW + lane;
 #pragma unroll
-            for (int k = 0; k < KN; ++k) o4[k] = __ldcg(src + 32 * k);
-        }
-        int64_t w2 = w_first + 1;
-        for (; w2 + 1 <= w_last; w2 += 2) {
-            const float *a = p.partials + (w2 * 2) * PW + lane;
-            const float *b2 = a + 2 * PW;
-            float va[KN], vb[KN];
+        for (int k = 0; k < KN; ++k) o4[k] = 0.f;
+        // all pieces of a round are requested before any is added (one L2
+        // round trip per round), then summed in warp order (deterministic)
+        for (int b0 = 0; b0 < np; b0 += KB) {
+            float v[KB][KN];
 #pragma unroll
-            for (int k = 0; k < KN; ++k) { va[k] = __ldcg(a + 32 * k); vb[k] = __ldcg(b2 + 32 * k); }
+            for (int u = 0; u < KB; ++u) {
+                const int i = b0 + u;
+                const float *src = p.partials + ((w_first + i) * 2 + (i == 0 ? sl_first : 0)) * PW + lane;
 #pragma unroll
-            for (int k = 0; k < KN; ++k) { o4[k] += va[k]; o4[k] += vb[k]; }
-        }
-        if (w2 <= w_last) {
-            const float *a = p.partials + (w2 * 2) * PW + lane;
+                for (int k = 0; k < KN; ++k) v[u][k] = i < np ? __ldcg(src + 32 * k) : 0.f;
+            }
 #pragma unroll
-            for (int k = 0; k < KN; ++k) o4[k] += __ldcg(a + 32 * k);
+            for (int u = 0; u < KB; ++u)
+#pragma unroll
+                for (int k = 0; k < KN; ++k) o4[k] += v[u][k];
         }
         const int64_t row0 = tl * kTileRows;
 #pragma unroll
