@@ -573,14 +573,17 @@ static GemvLaunch plan_gemv(int64_t rows, int64_t in_f, int nw) {
     return L;
 }
 
-// Warps per CTA for a launch: 12 when every warp gets many items (long
-// weights), else 8.
+// Warps per CTA for a launch: 12 (more items in flight per SM) unless that
+// splits a tile (16 rows x all chunks) into more than about 8 warps' pieces,
+// whose split-tile reduction then costs more than the extra warps gain;
+// batches above 4 have 8 (their activation slots fill shared memory).
 static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
-    const int64_t T = (rows + kTileRows - 1) / kTileRows * ((in_f + kChunkElems - 1) / kChunkElems);
-    const bool wide = T >= (int64_t)device_sms() * 12 * 48;
+    const int64_t nch = (in_f + kChunkElems - 1) / kChunkElems;
+    const int64_t T = (rows + kTileRows - 1) / kTileRows * nch;
+    const bool wide = T * 8 >= nch * (int64_t)device_sms() * 12;
     if (batch == 1) return wide ? GemvCfg<1, 12>::kWarps : GemvCfg<1, 8>::kWarps;
     if (batch == 2) return wide ? GemvCfg<2, 12>::kWarps : GemvCfg<2, 8>::kWarps;
-    if (batch <= 4) return GemvCfg<4, 8>::kWarps;
+    if (batch <= 4) return wide ? GemvCfg<4, 12>::kWarps : GemvCfg<4, 8>::kWarps;
     if (batch <= 8) return GemvCfg<8, 8>::kWarps;
     return GemvCfg<16, 8>::kWarps;
 }
@@ -672,7 +675,7 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
     cudaStream_t st = (cudaStream_t)stream;
     if (batch == 1) return nw > 8 ? launch_gemv<1, 12>(p, L, st) : launch_gemv<1, 8>(p, L, st);
     if (batch == 2) return nw > 8 ? launch_gemv<2, 12>(p, L, st) : launch_gemv<2, 8>(p, L, st);
-    if (batch <= 4) return launch_gemv<4, 8>(p, L, st);
+    if (batch <= 4) return nw > 8 ? launch_gemv<4, 12>(p, L, st) : launch_gemv<4, 8>(p, L, st);
     if (batch <= 8) return launch_gemv<8, 8>(p, L, st);
     return launch_gemv<16, 8>(p, L, st);
 }
