@@ -144,14 +144,13 @@ __device__ __forceinline__ uint32_t rec_emax(const uint32_t *rec, int r, int q) 
     return reinterpret_cast<const uint8_t *>(rec)[8 * r + q];
 }
 
-// Position of element (row, col) of a 16-row x 256-column chunk inside the
-// mma.m16n8k16 A-fragment buffer of its half (128 columns): 8 steps x 32
-// lanes x 4 registers x 2 halves of 16 bits.  Lane (g, t) holds rows g and
-// g+8 of the 32-column group t; step J carries group columns 4J..4J+3 as
-// pairs 2J (registers 0/1: rows g/g+8) and 2J+1 (registers 2/3).  The lane's
-// 16 bytes of step J sit at slot J * 32 + (lane ^ J): a permutation within
-// the step, so the fragment stores and loads stay conflict-free, that spreads
-// the patch entries of a 64-column quarter over all 32 shared-memory banks.
+// Position of element (row, col) of a 16-row x 256-column chunk among the
+// mma.m16n8k16 A fragments of its half (128 columns): 8 steps x 32 lanes x 4
+// registers x 2 halves of 16 bits, as an 11-bit index.  Lane (g, t) holds
+// rows g and g+8 of the 32-column group t; step J carries group columns
+// 4J..4J+3 as pairs 2J (registers 0/1: rows g/g+8) and 2J+1 (registers 2/3).
+// The index is (J * 32 + (lane ^ J)) * 8 + register * 2 + halfword; the
+// patch entries carry it, and frag_position recovers (row, col) from it.
 __host__ __device__ inline uint32_t frag_index(uint32_t row, uint32_t col) {
     const uint32_t kk = col & 127u;
     const uint32_t owner = 4u * (row & 7u) + (kk >> 5);
