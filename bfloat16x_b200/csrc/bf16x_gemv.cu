@@ -32,6 +32,7 @@
 //   * every mbarrier wait is bounded (bf16x_common.cuh) and reports a timeout
 //     through the device status word instead of hanging.
 #include <algorithm>
+#include <type_traits>
 #include <mutex>
 
 #include <cuda_runtime.h>
@@ -43,7 +44,8 @@
 
 namespace bf16x {
 
-constexpr int kPcapWords = 64;       // record words staged per slot: emax, header, 30 entries (more: from L2)
+constexpr int kPcapWords = 256;      // record words staged per slot: emax, header, 222 entries (more: from L2)
+constexpr int kSparseEntries = 8;    // items with more patch entries take the fragment round trip
 constexpr int kXRowBytes = kChunkElems * 2;
 
 // Configuration per (batch bound, warps per CTA).  Shared memory holds the
@@ -174,6 +176,30 @@ __device__ __forceinline__ void add_patch(uint32_t key, float dv, bool on, int g
         pd[1] += top ? v3 : 0.f;
         pd[2] += top ? 0.f : v2;
         pd[3] += top ? 0.f : v3;
+    }
+}
+
+// Patches of one half chunk for items with many entries (weights holding
+// exact zeros, say): each lane stores its 8 decoded fragments at its slots
+// (frag_index order) of `fb`, the lanes store the exact bf16 values of the
+// half's entries [jlo, jhi) over their slots, 32 at a time, and each lane
+// reads its fragments back.  Called by the whole warp.
+__device__ __forceinline__ void patch_half_dense(StepFrag (&f)[8], uint4 *fb, const ItemPatches &ip, int jlo,
+                                                 int jhi, int lane) {
+    __syncwarp();   // earlier reads of fb's memory by any lane are done
+#pragma unroll
+    for (int J = 0; J < 8; ++J) fb[J * 32 + (lane ^ J)] = make_uint4(f[J].a0, f[J].a1, f[J].a2, f[J].a3);
+    __syncwarp();
+    uint16_t *fb16 = reinterpret_cast<uint16_t *>(fb);
+    for (int j = jlo + lane; j < jhi; j += 32) {
+        const uint32_t ent = ip.entry(j);
+        fb16[ent & 0x7FFu] = (uint16_t)(ent >> 16);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int J = 0; J < 8; ++J) {
+        const uint4 v = fb[J * 32 + (lane ^ J)];
+        f[J] = StepFrag{v.x, v.y, v.z, v.w};
     }
 }
 
@@ -397,48 +423,60 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                 load_group_sw(wsl + kRowB, go[h], smB[h], dB[h]);
             }
             const ItemPatches ip{rec, p.precs, rec_of + s};
-            const int n_all = (int)(hdr >> 16);
-            // entry `lane` of the item, decoded by its lane: row << 8 | column, delta
-            uint32_t pkey = 0u;
-            float pdv = 0.f;
-            if (lane < n_all) {
-                const uint32_t ent = ip.entry(lane);
-                uint32_t rr, cc;
-                frag_position(ent, rr, cc);
-                pkey = rr << 8 | cc;
-                pdv = patch_delta(ent, rec_emax(rec, (int)rr, (int)(cc >> 5)));
-            }
-            // The patched weights enter the products with their saturated
-            // value; add (exact - saturated) * x to the correction sums of
-            // their rows, in entry order (deterministic).  Done while the
-            // compressed groups are still on their way from shared memory.
-            const int n_reg = n_all < 32 ? n_all : 32;
-            for (int e = 0; e < n_reg; e += 2) {      // two entries per pass: independent chains
-                const uint32_t k0 = __shfl_sync(0xffffffffu, pkey, e), k1 = __shfl_sync(0xffffffffu, pkey, e + 1);
-                const float v0 = __shfl_sync(0xffffffffu, pdv, e), v1 = __shfl_sync(0xffffffffu, pdv, e + 1);
-                add_patch<BMAX>(k0, v0, true, g, t, xs, pc, pd);
-                add_patch<BMAX>(k1, v1, e + 1 < n_reg, g, t, xs, pc, pd);
-            }
-            for (int e = 32; e < n_all; ++e) {        // past 32 entries: from the record
-                const uint32_t ent = ip.entry(e);
-                uint32_t rr, cc;
-                frag_position(ent, rr, cc);
-                add_patch<BMAX>(rr << 8 | cc, patch_delta(ent, rec_emax(rec, (int)rr, (int)(cc >> 5))), true, g, t,
-                                xs, pc, pd);
-            }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t eA = emax_x2(((h ? ewA.y : ewA.x) >> (8 * t)) & 0xFFu);
-                const uint32_t eB = emax_x2(((h ? ewB.y : ewB.x) >> (8 * t)) & 0xFFu);
-                StepFrag f[8];
-                decode_half<0>(f, smA[h], dA[h], eA, smB[h], dB[h], eB);
-                const int q = 4 * h + t;
-                if constexpr (BMAX > 8) {
-                    half_mma2<0>(f, xg + 32 * q, xs + (8 + g) * kChunkElems + 32 * q, ce, co, de, dd);
-                } else {
-                    half_mma<0>(f, xg + 32 * q, g < BMAX, ce, co);
+            const int n_low = (int)(hdr & 0xFFFFu), n_all = (int)(hdr >> 16);
+            // Few entries (the usual case): the patched weights enter the
+            // products with their saturated value, and (exact - saturated) * x
+            // is added to the correction sums of their rows, in entry order
+            // (deterministic), while the compressed groups are still on their
+            // way from shared memory.  Many entries: the fragments go through
+            // shared memory, where the exact values are stored over them.
+            const bool dense = n_all > kSparseEntries;
+            if (!dense) {
+                // entry `lane`, decoded by its lane: row << 8 | column, delta
+                uint32_t pkey = 0u;
+                float pdv = 0.f;
+                if (lane < n_all) {
+                    const uint32_t ent = ip.entry(lane);
+                    uint32_t rr, cc;
+                    frag_position(ent, rr, cc);
+                    pkey = rr << 8 | cc;
+                    pdv = patch_delta(ent, rec_emax(rec, (int)rr, (int)(cc >> 5)));
+                }
+                for (int e = 0; e < n_all; e += 2) {      // two entries per pass: independent chains
+                    const uint32_t k0 = __shfl_sync(0xffffffffu, pkey, e), k1 = __shfl_sync(0xffffffffu, pkey, e + 1);
+                    const float v0 = __shfl_sync(0xffffffffu, pdv, e), v1 = __shfl_sync(0xffffffffu, pdv, e + 1);
+                    add_patch<BMAX>(k0, v0, true, g, t, xs, pc, pd);
+                    add_patch<BMAX>(k1, v1, e + 1 < n_all, g, t, xs, pc, pd);
                 }
             }
+            // the two halves: decode, patch (dense items), multiply; the
+            // dense path is a separate copy so the usual one stays straight
+            auto halves = [&](auto dense_tag) {
+                constexpr bool kDense = decltype(dense_tag)::value;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t eA = emax_x2(((h ? ewA.y : ewA.x) >> (8 * t)) & 0xFFu);
+                    const uint32_t eB = emax_x2(((h ? ewB.y : ewB.x) >> (8 * t)) & 0xFFu);
+                    StepFrag f[8];
+                    decode_half<0>(f, smA[h], dA[h], eA, smB[h], dB[h], eB);
+                    // the item's compressed rows are in registers by now, so
+                    // their slot serves as the 4 KB fragment buffer
+                    if constexpr (kDense)
+                        patch_half_dense(f, reinterpret_cast<uint4 *>(const_cast<uint8_t *>(wsl)), ip, h ? n_low : 0,
+                                         h ? n_all : n_low, lane);
+                    const int q = 4 * h + t;
+                    if constexpr (BMAX > 8) {
+                        half_mma2<0>(f, xg + 32 * q, xs + (8 + g) * kChunkElems + 32 * q, ce, co, de, dd);
+                    } else {
+                        half_mma<0>(f, xg + 32 * q, g < BMAX, ce, co);
+                    }
+                }
+            };
+            if (dense) halves(std::true_type{});
+            else halves(std::false_type{});
+            // shared-memory writes of the generic proxy before the slot's
+            // refill by the TMA engine (async proxy)
+            if (dense) fence_proxy_async_smem();
         }
 
         // ---- refill this slot S items ahead
