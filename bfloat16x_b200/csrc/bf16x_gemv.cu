@@ -58,9 +58,10 @@ template <int BMAX, int NW>
 struct GemvCfg {
     static constexpr int kWBytes = kTileRows * kChunkBytes;                 // 6144
     static constexpr int kPOff = BMAX * kXRowBytes;                         // record after the activations
-    static constexpr int kXRSlot = kPOff + kPcapWords * 4;
+    static constexpr int kPcap = kPcapWords;
+    static constexpr int kXRSlot = kPOff + kPcap * 4;
     static constexpr int kPerSlot = kWBytes + kXRSlot;
-    static constexpr int kBudget = 220 * 1024 - 2048;
+    static constexpr int kBudget = 224 * 1024;                              // slots; the rest below 227 KB
     static constexpr int kWarpsFit = kBudget / (2 * kPerSlot);
     static constexpr int kWarps = NW < kWarpsFit ? NW : kWarpsFit;
     static constexpr int kStagesFit = kBudget / kWarps / kPerSlot;
@@ -129,15 +130,16 @@ __device__ __forceinline__ uint4 lds128_if(const void *ptr, bool pred) {
     return v;
 }
 
-// The patch entries of the item: the first kPcapWords - kRecHdrWords are
+// The patch entries of the item: the first cap - kRecHdrWords are
 // staged in shared memory with the record, later ones are read from the
 // record in global memory (precs + *rof).
 struct ItemPatches {
     const uint32_t *rec;
     const uint32_t *precs;
     const int64_t *rof;
+    int cap;                                  // record words staged in shared memory
     __device__ __forceinline__ uint32_t entry(int j) const {
-        return kRecHdrWords + j < kPcapWords ? rec[kRecHdrWords + j] : __ldg(precs + *rof + kRecHdrWords + j);
+        return kRecHdrWords + j < cap ? rec[kRecHdrWords + j] : __ldg(precs + *rof + kRecHdrWords + j);
     }
 };
 
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
     // three TMA operations (16 weight rows, the activation slice, the record)
     auto issue = [&](int64_t tile, int c, int s, int32_t r_off, int32_t r_end) {
         if (lane == 0) {
-            const int staged = min(r_end - r_off, kPcapWords);
+            const int staged = min(r_end - r_off, C::kPcap);
             uint8_t *xr = xrs + s * C::kXRSlot;
             rec_of[s] = r_off;
             mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + BMAX * kXRowBytes + staged * 4));
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         for (int s = 0; s < S && lo + s < hi; ++s) {
             const int32_t r_off = __shfl_sync(0xffffffffu, v, s), r_end = __shfl_sync(0xffffffffu, v, s + 1);
             if (lane == 0) {
-                const int staged = min(r_end - r_off, kPcapWords);
+                const int staged = min(r_end - r_off, C::kPcap);
                 rec_of[s] = r_off;
                 mbar_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
                 tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, cc, (int)(tl * kTileRows), &bars[s]);
@@ -422,7 +424,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
                 load_group_sw(wsl, go[h], smA[h], dA[h]);
                 load_group_sw(wsl + kRowB, go[h], smB[h], dB[h]);
             }
-            const ItemPatches ip{rec, p.precs, rec_of + s};
+            const ItemPatches ip{rec, p.precs, rec_of + s, C::kPcap};
             const int n_low = (int)(hdr & 0xFFFFu), n_all = (int)(hdr >> 16);
             // Few entries (the usual case): the patched weights enter the
             // products with their saturated value, and (exact - saturated) * x
@@ -614,7 +616,8 @@ static GemvLaunch plan_gemv(int64_t rows, int64_t in_f, int nw) {
 // Warps per CTA for a launch: 12 (more items in flight per SM) unless that
 // splits a tile (16 rows x all chunks) into more than about 8 warps' pieces,
 // whose split-tile reduction then costs more than the extra warps gain;
-// batches above 4 have 8 (their activation slots fill shared memory).
+// batches of 5..8 have 10 or 8, above 8 always 8 (their activation slots
+// fill shared memory).
 static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
     const int64_t nch = (in_f + kChunkElems - 1) / kChunkElems;
     const int64_t T = (rows + kTileRows - 1) / kTileRows * nch;
@@ -622,7 +625,7 @@ static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
     if (batch == 1) return wide ? GemvCfg<1, 12>::kWarps : GemvCfg<1, 8>::kWarps;
     if (batch == 2) return wide ? GemvCfg<2, 12>::kWarps : GemvCfg<2, 8>::kWarps;
     if (batch <= 4) return wide ? GemvCfg<4, 12>::kWarps : GemvCfg<4, 8>::kWarps;
-    if (batch <= 8) return GemvCfg<8, 8>::kWarps;
+    if (batch <= 8) return wide ? GemvCfg<8, 10>::kWarps : GemvCfg<8, 8>::kWarps;
     return GemvCfg<16, 8>::kWarps;
 }
 
@@ -714,7 +717,7 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
     if (batch == 1) return nw > 8 ? launch_gemv<1, 12>(p, L, st) : launch_gemv<1, 8>(p, L, st);
     if (batch == 2) return nw > 8 ? launch_gemv<2, 12>(p, L, st) : launch_gemv<2, 8>(p, L, st);
     if (batch <= 4) return nw > 8 ? launch_gemv<4, 12>(p, L, st) : launch_gemv<4, 8>(p, L, st);
-    if (batch <= 8) return launch_gemv<8, 8>(p, L, st);
+    if (batch <= 8) return nw > 8 ? launch_gemv<8, 10>(p, L, st) : launch_gemv<8, 8>(p, L, st);
     return launch_gemv<16, 8>(p, L, st);
 }
 
