@@ -6,9 +6,9 @@
 //
 // Design (HBM-bound: the only large stream is the compressed weight):
 //   * work items are (16-row tile, 256-column chunk) pairs in tile-major
-//     order; persistent CTAs of 8 warps split them stream-K style, every warp
-//     a contiguous, equal range, so every SM streams the same number of bytes
-//     whatever the shape;
+//     order; persistent CTAs of 8 to 12 warps split them stream-K style,
+//     every warp a contiguous, equal range, so every SM streams the same
+//     number of bytes whatever the shape;
 //   * each warp feeds itself: a ring of shared-memory slots filled by the
 //     TMA engine -- 16 weight rows x 384 bytes (128-byte swizzled), the
 //     activation slice, and the (tile, chunk) patch record with the groups'
@@ -21,8 +21,10 @@
 //     (k x batch): the tensor core does the multiply-accumulate.  The rare
 //     weights whose exponent is more than 15 below their group's largest
 //     enter the products saturated (exponent emax - 15); their record
-//     entries then add (exact - saturated) * x to the accumulators of their
-//     rows, so the sum is that of the exact weights;
+//     entries then add (exact - saturated) * x to correction sums of their
+//     rows, so the sum is that of the exact weights.  Items with many
+//     entries (exact zeros, say) instead pass their fragments through the
+//     consumed weight slot, where the exact values are stored over them;
 //   * a tile split between warps is finished by whichever warp arrives last
 //     (an atomic counter per tile in the workspace), summing the pieces in a
 //     fixed order, so results are deterministic and no warp ever waits;
@@ -51,9 +53,8 @@ constexpr int kXRowBytes = kChunkElems * 2;
 // Configuration per (batch bound, warps per CTA).  Shared memory holds the
 // weight slots of all warps first (16 rows x 384 bytes each, 1024-byte
 // aligned for the 128-byte swizzle), then every warp's activation + record
-// slots, zeros, record offsets and mbarriers.  Long weights run 12 warps per
-// SM with 2-slot rings; short ones 8 warps with 3-slot rings (more bytes in
-// flight per warp).
+// slots, zeros, record offsets and mbarriers.  12-warp configurations get
+// 2-slot rings, 8-warp ones 3-slot rings (see warps_for).
 template <int BMAX, int NW>
 struct GemvCfg {
     static constexpr int kWBytes = kTileRows * kChunkBytes;                 // 6144
