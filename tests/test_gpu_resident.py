@@ -34,6 +34,17 @@ def test_repack_roundtrip_and_patch_count(shape):
     assert rw.layout.shape[1] == (shape[1] + 255) // 256 * 384
 
 
+@pytest.mark.parametrize("shape", [(4096, 4096), (300, 1000)])
+def test_host_byte_model_matches_layout(shape):
+    # bench.py counts the stored bytes of the reference arm's workload with a
+    # host model of the resident layout; it must equal what the repack builds
+    import bench
+    w = bits_of(synthetic_weight(*shape, seed=21))
+    p = oracle_dict(w)
+    rw = ResidentWeight.from_packed(p, device="cuda")
+    assert bench.stored_weight_bytes(p, *shape) == rw.nbytes()
+
+
 def expected_patches(w_bits):
     """Weights whose exponent is more than 15 below the largest of their
     row-local 32-column group (columns padded to a multiple of 256)."""
