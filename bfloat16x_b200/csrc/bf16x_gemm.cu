@@ -454,12 +454,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
 
 // ------------------------------------------------ CTA-pair (cluster of 2) glue
+// BN = tokens per pair tile: 256 (each CTA stages 128; two accumulators, so
+// the epilogue of one tile overlaps the next) or 512 (each CTA stages 256;
+// two N=256 MMAs per decoded k-block fill the whole of tensor memory, one
+// accumulator) -- the latter decodes every weight once per 512 tokens.
+template <int BN>
 struct Gemm2Cfg {
     static constexpr int kWStages = 2;
-    static constexpr int kAStages = 4;
-    static constexpr int kBStages = 3;
+    static constexpr int kAStages = BN > 256 ? 3 : 4;
+    static constexpr int kBStages = BN > 256 ? 2 : 3;
+    static constexpr int kAccBufs = BN > 256 ? 1 : 2;
     static constexpr int kAStage = kGemmBM * 128;     // 16 KB: 128 rows x 64 columns
-    static constexpr int kBStage = 128 * 128;         // 16 KB: this CTA's 128 tokens x 64 columns
+    static constexpr int kBStage = (BN / 2) * 128;    // this CTA's BN/2 tokens x 64 columns
     static constexpr int kRecStage = kSubsPerStage * kGemmRecCap * 4;
     static constexpr int kAOff = 0;
     static constexpr int kBOff = kAOff + kAStages * kAStage;
@@ -469,7 +475,7 @@ struct Gemm2Cfg {
     static constexpr int kNumBars = 2 * kWStages + 3 * kAStages + 2 * kBStages + 4;
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
     static constexpr int kSmem = kMiscOff + 16 + 1024;
-    static constexpr int kTmemCols = 512;             // two 256-column accumulators
+    static constexpr int kTmemCols = 512;             // two 256-column accumulators, or one of 512
     static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
@@ -546,7 +552,7 @@ __device__ __forceinline__ void cluster_sync_all() {
 // release the leader's accumulator.
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_constant__ GemmParams p) {
-    using C = Gemm2Cfg;
+    using C = Gemm2Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled operand slots
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -656,8 +662,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
                     // this CTA's half of the token tile, counted on the leader's barrier
                     const uint32_t lb = leader(&b_full[bs]);
                     if (rank == 0) mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(2 * C::kBStage));
-                    tma_load_2d_pair(smem + C::kBOff + bs * C::kBStage, &p.xmap, kb * kGemmBK,
-                                     nt * BN + (int)rank * (BN / 2), lb);
+                    if constexpr (BN > 256) {
+                        // tokens [r*128, +128) and [256 + r*128, +128) of the tile: the
+                        // first and second N=256 MMA each read 128 tokens per CTA
+                        tma_load_2d_pair(smem + C::kBOff + bs * C::kBStage, &p.xmap, kb * kGemmBK,
+                                         nt * BN + (int)rank * 128, lb);
+                        tma_load_2d_pair(smem + C::kBOff + bs * C::kBStage + 128 * 128, &p.xmap, kb * kGemmBK,
+                                         nt * BN + 256 + (int)rank * 128, lb);
+                    } else {
+                        tma_load_2d_pair(smem + C::kBOff + bs * C::kBStage, &p.xmap, kb * kGemmBK,
+                                         nt * BN + (int)rank * (BN / 2), lb);
+                    }
                     if (++bs == C::kBStages) { bs = 0; bph ^= 1u; }
                 }
             }
@@ -665,7 +680,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
     } else if (warp == 2) {
         // ------------------------------------------------------- MMA issuer
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = umma_idesc_bf16_m<2 * kGemmBM, BN>();
+            constexpr uint32_t idesc = umma_idesc_bf16_m<2 * kGemmBM, (BN > 256 ? 256 : BN)>();
             const uint32_t peer = 1u;
             int as = 0, bs = 0, ac = 0;
             uint32_t aph = 0, bph = 0, acph = 0;
@@ -683,8 +698,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
                     const uint64_t ad = umma_desc_sw128(smem_u32(smem + C::kAOff + as * C::kAStage));
                     const uint64_t bd = umma_desc_sw128(smem_u32(smem + C::kBOff + bs * C::kBStage));
 #pragma unroll
-                    for (int k16 = 0; k16 < kGemmBK / 16; ++k16)   // 32 bytes along K per step
+                    for (int k16 = 0; k16 < kGemmBK / 16; ++k16) {   // 32 bytes along K per step
                         umma_bf16_pair(d_tmem, ad + 2u * k16, bd + 2u * k16, idesc, (kb | k16) != 0);
+                        if constexpr (BN > 256)   // tokens 256..511: the stage's rows 128..255 (16 KB on)
+                            umma_bf16_pair(d_tmem + 256u, ad + 2u * k16, bd + (uint64_t)((128 * 128) >> 4) + 2u * k16,
+                                           idesc, (kb | k16) != 0);
+                    }
                     umma_commit_pair(smem_u32(&a_empty[as]));
                     umma_commit_pair(mapa_shared(smem_u32(&a_empty[as]), peer));
                     umma_commit_pair(smem_u32(&b_empty[bs]));
@@ -695,7 +714,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
                 if (!ok) break;
                 umma_commit_pair(smem_u32(&acc_full[ac]));
                 umma_commit_pair(mapa_shared(smem_u32(&acc_full[ac]), peer));
-                if (++ac == 2) { ac = 0; acph ^= 1u; }
+                if (++ac == C::kAccBufs) { ac = 0; acph ^= 1u; }
             }
         }
         if (lane == 0 && rank == 1) {
@@ -853,7 +872,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
                 if (rank == 0) mbar_arrive(&acc_empty[ac]);
                 else mbar_arrive_cluster(leader(&acc_empty[ac]));
             }
-            if (++ac == 2) { ac = 0; acph ^= 1u; }
+            if (++ac == C::kAccBufs) { ac = 0; acph ^= 1u; }
         }
     }
 
@@ -1351,16 +1370,17 @@ static int launch_gemm(GemmParams &p, const uint8_t *layout, int64_t in_f, const
 }
 
 // CTA-pair launch: tiles of 256 rows x 256 tokens, clusters of 2 CTAs.
+template <int BN>
 static int launch_gemm2sm(GemmParams &p, const uint8_t *layout, int64_t in_f, const uint16_t *x, int64_t ldx,
                           cudaStream_t st) {
-    using C = Gemm2Cfg;
+    using C = Gemm2Cfg<BN>;
     if (!encode_resident_map(&p.wmap, layout, p.rows, p.nch, resident_row_bytes(in_f), kGemmWRows))
         return set_error(BF16X_ERR_CUDA, "bf16x_gemm: weight tensor map");
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: cuTensorMapEncodeTiled unavailable");
     const cuuint64_t xdims[2] = {(cuuint64_t)in_f, (cuuint64_t)p.M};
     const cuuint64_t xstr[1] = {(cuuint64_t)ldx * 2};
-    const cuuint32_t xbox[2] = {(cuuint32_t)kGemmBK, 128u};      // each CTA stages half the 256-token tile
+    const cuuint32_t xbox[2] = {(cuuint32_t)kGemmBK, 128u};      // 128 tokens per copy (one or two per stage)
     const cuuint32_t estr[2] = {1, 1};
     if (fn(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), xdims, xstr, xbox, estr,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1371,7 +1391,7 @@ static int launch_gemm2sm(GemmParams &p, const uint8_t *layout, int64_t in_f, co
     static bool attr_set[64] = {false};
     if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: device index");
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm2sm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemm2sm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
         if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: smem attribute: %s", cudaGetErrorString(e));
         attr_set[dev] = true;
     }
@@ -1388,7 +1408,7 @@ static int launch_gemm2sm(GemmParams &p, const uint8_t *layout, int64_t in_f, co
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm2sm_kernel<256>, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm2sm_kernel<BN>, p);
     if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: pair launch: %s", cudaGetErrorString(e));
     return check_launch("bf16x_gemm");
 }
@@ -1597,12 +1617,19 @@ extern "C" int bf16x_gemm_ws(const uint8_t *layout, const int32_t *ptile_off, co
     if (bn == 256 && tiles_m * ((M + 255) / 256) < sms) bn = 128;
 #ifndef BF16X_GEMM_NO_PAIR
     if (bn == 256) {
-        // CTA pairs: tiles of 256 rows x 256 tokens
-        p.tiles_n = (int)((M + 255) / 256);
+        // CTA pairs: tiles of 256 rows x 256 tokens, or x 512 tokens when
+        // that is one tile per 256-row slab and the slabs fit in one round of
+        // pairs: each weight is then decoded once.  With more rounds the
+        // shallower rings and the single accumulator (no epilogue overlap)
+        // of 512-token tiles cost more than the halved decode saves.
+        const int64_t slabs = (rows + 2 * kGemmBM - 1) / (2 * kGemmBM);
+        const int pbn = (M > 256 && M <= 512 && slabs <= sms / 2) ? 512 : 256;
+        p.tiles_n = (int)((M + pbn - 1) / pbn);
         const int64_t total2 = (rows + 2 * kGemmBM - 1) / (2 * kGemmBM) * p.tiles_n;
         if (total2 > 0x7fffffffLL) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemm: too many tiles");
         p.tiles_total = (int)total2;
-        return launch_gemm2sm(p, layout, in_f, x, ldx, st);
+        return pbn == 512 ? launch_gemm2sm<512>(p, layout, in_f, x, ldx, st)
+                          : launch_gemm2sm<256>(p, layout, in_f, x, ldx, st);
     }
 #endif
     p.tiles_n = (int)((M + bn - 1) / bn);

@@ -127,6 +127,34 @@ def test_gemm_pair_ragged_vs_oracle(rows, M, dense):
     _lib.check_device_status()
 
 
+# 257..512 tokens on shapes that fill the GPU with pair tiles run 512-token
+# pair tiles (each CTA stages two 128-token blocks; two N=256 MMAs per
+# k-block): the identity probe checks every token's column in all four
+# blocks, the ragged case a tile with 300 of 512 tokens and partial rows.
+@pytest.mark.parametrize("rows,in_f,M", [(9600, 1024, 512), (9728, 512, 384)])
+def test_gemm_pair512_identity_probe(rows, in_f, M):
+    wb = bits_of(synthetic_weight(rows, in_f, seed=31))
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    x = torch.eye(M, in_f, dtype=torch.bfloat16)
+    y = rw.gemm(x.cuda(), out_dtype=torch.float32).cpu().numpy()
+    expect = oracle.bf16_bits_to_f32(wb)[:, :M].T
+    assert np.array_equal(y.view(np.uint32), np.ascontiguousarray(expect).view(np.uint32))
+    _lib.check_device_status()
+
+
+@pytest.mark.parametrize("dense", [False, True])
+def test_gemm_pair512_ragged_vs_oracle(dense):
+    rows, in_f, M = 9700, 1024, 300
+    wb = _dense_patch_weight(rows, in_f, seed=7) if dense else bits_of(synthetic_weight(rows, in_f, seed=37))
+    rw = ResidentWeight.from_packed(oracle_dict(wb), device="cuda")
+    bias = (torch.randn(rows, generator=torch.Generator().manual_seed(2)) * 0.1).to(torch.bfloat16)
+    x = synthetic_activation(M, in_f, seed=41)
+    ref = oracle.matmul_bf16w(x.float().numpy(), wb, bias.float().numpy())
+    y = rw.gemm(x.cuda(), bias=bias.cuda(), out_dtype=torch.float32).cpu().numpy()
+    assert rel_l2(y, ref) < GATE
+    _lib.check_device_status()
+
+
 # Slab path (bf16x_gemm_ws with a workspace, at least 4 token tiles per
 # 256-row slab): 16 slabs through a ring of 12 slots, and K = 14336 (56
 # chunks) through a 42-chunk window, so slots are reused and windows wrap.
