@@ -55,26 +55,35 @@ constexpr int kXRowBytes = kChunkElems * 2;
 // aligned for the 128-byte swizzle), then every warp's activation + record
 // slots, zeros, record offsets and mbarriers.  12-warp configurations get
 // 2-slot rings, 8-warp ones 3-slot rings (see warps_for).
-template <int BMAX, int NW>
+//
+// XRES (5..8 activation rows, in_f <= 4096): the whole activation block is
+// copied once per CTA into shared memory and every item reads its chunk
+// there, instead of copying a 4 KB slice into its slot; with records staged
+// to 160 words (126 entries) the slots then shrink enough for 12 warps per SM.
+constexpr int kXResChunks = 16;      // in_f <= 4096
+template <int BMAX, int NW, bool XRES = false>
 struct GemvCfg {
     static constexpr int kWBytes = kTileRows * kChunkBytes;                 // 6144
-    static constexpr int kPOff = BMAX * kXRowBytes;                         // record after the activations
-    static constexpr int kPcap = kPcapWords;
+    static constexpr int kPOff = XRES ? 0 : BMAX * kXRowBytes;              // record after the activations
+    static constexpr int kPcap = XRES ? 160 : kPcapWords;      // XRES: 126 entries staged
     static constexpr int kXRSlot = kPOff + kPcap * 4;
     static constexpr int kPerSlot = kWBytes + kXRSlot;
-    static constexpr int kBudget = 224 * 1024;                              // slots; the rest below 227 KB
+    static constexpr int kXCache = XRES ? kXResChunks * BMAX * kXRowBytes : 0;
+    static constexpr int kBudget = 224 * 1024 - kXCache;                    // slots; the rest below 227 KB
     static constexpr int kWarpsFit = kBudget / (2 * kPerSlot);
     static constexpr int kWarps = NW < kWarpsFit ? NW : kWarpsFit;
     static constexpr int kStagesFit = kBudget / kWarps / kPerSlot;
     static constexpr int kStages = kStagesFit < 3 ? kStagesFit : 3;
     static constexpr int kWOff = 0;                                          // [warp][stage] weight rows
     static constexpr int kXROff = kWarps * kStages * kWBytes;                // [warp][stage] x + record
-    static constexpr int kZeroOff = kXROff + kWarps * kStages * kXRSlot;     // 512 zero bytes
+    static constexpr int kXCOff = kXROff + kWarps * kStages * kXRSlot;       // [chunk][BMAX][256] (XRES)
+    static constexpr int kZeroOff = kXCOff + kXCache;                        // 512 zero bytes
     static constexpr int kRecOff = kZeroOff + 512;                           // per slot record offset
     static constexpr int kBarOff = kRecOff + kWarps * kStages * 8;
-    static constexpr int kSmem = kBarOff + kWarps * kStages * 8 + 1024;      // + base alignment
+    static constexpr int kSmem = kBarOff + kWarps * kStages * 8 + 8 + 1024;  // + the x barrier, base alignment
     static_assert(kStages >= 2, "ring too shallow for this configuration");
-    static_assert(kWBytes % 1024 == 0 && kXRSlot % 16 == 0 && kPOff % 16 == 0, "slot alignment");
+    static_assert(kWBytes % 1024 == 0 && kXRSlot % 128 == 0 && kPOff % 16 == 0 && kXCOff % 128 == 0,
+                  "slot alignment");
     static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
@@ -194,9 +203,18 @@ __device__ __forceinline__ void patch_half_dense(StepFrag (&f)[8], uint4 *fb, co
     for (int J = 0; J < 8; ++J) fb[J * 32 + (lane ^ J)] = make_uint4(f[J].a0, f[J].a1, f[J].a2, f[J].a3);
     __syncwarp();
     uint16_t *fb16 = reinterpret_cast<uint16_t *>(fb);
-    for (int j = jlo + lane; j < jhi; j += 32) {
-        const uint32_t ent = ip.entry(j);
-        fb16[ent & 0x7FFu] = (uint16_t)(ent >> 16);
+    // all of the half's entries are requested before any is stored (one
+    // round trip whether staged in shared memory or read from L2)
+    for (int j0 = jlo; j0 < jhi; j0 += 8 * 32) {
+        uint32_t ent[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int j = j0 + 32 * k + lane;
+            ent[k] = j < jhi ? ip.entry(j) : 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (j0 + 32 * k + lane < jhi) fb16[ent[k] & 0x7FFu] = (uint16_t)(ent[k] >> 16);
     }
     __syncwarp();
 #pragma unroll
@@ -247,9 +265,10 @@ __device__ __forceinline__ void half_mma2(const StepFrag (&f)[8], const uint16_t
 __device__ __forceinline__ int64_t item_lo(int64_t w, int64_t T, int64_t W) { return T * w / W; }
 __device__ __forceinline__ int64_t item_owner(int64_t i, int64_t T, int64_t W) { return ((i + 1) * W - 1) / T; }
 
-template <int BMAX, int NW>
-__global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
-    using C = GemvCfg<BMAX, NW>;
+template <int BMAX, int NW, bool XRES>
+__global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
+    gemv_kernel(const __grid_constant__ GemvParams p) {
+    using C = GemvCfg<BMAX, NW, XRES>;
     constexpr int S = C::kStages;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the weight slots want a 1024-byte-aligned base (128-byte swizzle)
@@ -258,9 +277,11 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff) + warp * S;
     int64_t *rec_of = reinterpret_cast<int64_t *>(smem + C::kRecOff) + warp * S;
+    uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + C::kBarOff) + C::kWarps * S;
     for (int i = threadIdx.x; i < 128; i += blockDim.x) reinterpret_cast<uint32_t *>(smem + C::kZeroOff)[i] = 0u;
     if (lane == 0)
         for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    if (XRES && threadIdx.x == 0) mbar_init(xbar, 1);
     fence_mbar_init();
     __syncthreads();
     griddep_launch_dependents();
@@ -284,9 +305,9 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
             const int staged = min(r_end - r_off, C::kPcap);
             uint8_t *xr = xrs + s * C::kXRSlot;
             rec_of[s] = r_off;
-            mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + BMAX * kXRowBytes + staged * 4));
+            mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + (XRES ? 0 : BMAX * kXRowBytes) + staged * 4));
             tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, c, (int)(tile * kTileRows), &bars[s]);
-            tma_load_2d(xr, &p.xmap, c * kChunkElems, 0, &bars[s]);
+            if constexpr (!XRES) tma_load_2d(xr, &p.xmap, c * kChunkElems, 0, &bars[s]);
             bulk_g2s(xr + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
         }
     };
@@ -321,19 +342,30 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
             if (lane == 0) {
                 const int staged = min(r_end - r_off, C::kPcap);
                 rec_of[s] = r_off;
-                mbar_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
+                if constexpr (XRES) mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
+                else mbar_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
                 tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, cc, (int)(tl * kTileRows), &bars[s]);
                 bulk_g2s(xrs + s * C::kXRSlot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
             }
             if (++cc == p.nch) { cc = 0; ++tl; }
         }
         griddep_wait();
-        for (int s = 0; s < S && i_it < hi; ++s) {
-            if (lane == 0) {
-                mbar_arrive_expect_tx(&bars[s], (uint32_t)(BMAX * kXRowBytes));
-                tma_load_2d(xrs + s * C::kXRSlot, &p.xmap, i_c * kChunkElems, 0, &bars[s]);
+        if constexpr (XRES) {
+            if (warp == 0 && lane == 0) {
+                mbar_arrive_expect_tx(xbar, (uint32_t)(p.nch * BMAX * kXRowBytes));
+                for (int c2 = 0; c2 < p.nch; ++c2)
+                    tma_load_2d(smem + C::kXCOff + c2 * BMAX * kXRowBytes, &p.xmap, c2 * kChunkElems, 0, xbar);
             }
-            advance_issue();
+            for (int s = 0; s < S && i_it < hi; ++s) advance_issue();
+            if (!mbar_wait(xbar, 0u, &g_status)) return;
+        } else {
+            for (int s = 0; s < S && i_it < hi; ++s) {
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&bars[s], (uint32_t)(BMAX * kXRowBytes));
+                    tma_load_2d(xrs + s * C::kXRSlot, &p.xmap, i_c * kChunkElems, 0, &bars[s]);
+                }
+                advance_issue();
+            }
         }
         nxt_off = __shfl_sync(0xffffffffu, v, S);
         nxt_end = __shfl_sync(0xffffffffu, v, S + 1);
@@ -410,7 +442,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW>::kWarps * 32, 1) gemv_kernel
         if (!mbar_wait(&bars[s], parity, &g_status)) return;
         const uint8_t *wsl = wsm + s * C::kWBytes;
         const uint8_t *xr = xrs + s * C::kXRSlot;
-        const uint16_t *xs = reinterpret_cast<const uint16_t *>(xr);
+        const uint16_t *xs = reinterpret_cast<const uint16_t *>(XRES ? smem + C::kXCOff + c * BMAX * kXRowBytes : xr);
         {
             const uint32_t *rec = reinterpret_cast<const uint32_t *>(xr + C::kPOff);
             const uint32_t hdr = rec[kRecHdr];
@@ -616,9 +648,12 @@ static GemvLaunch plan_gemv(int64_t rows, int64_t in_f, int nw) {
 
 // Warps per CTA for a launch: 12 (more items in flight per SM) unless that
 // splits a tile (16 rows x all chunks) into more than about 8 warps' pieces,
-// whose split-tile reduction then costs more than the extra warps gain;
-// batches of 5..8 have 10 or 8, above 8 always 8 (their activation slots
-// fill shared memory).
+// whose split-tile reduction then costs more than the extra warps gain.
+// 5..8 rows: 12 with the CTA's activation block (in_f <= 4096 and enough
+// items to repay its copy), else 10, else 8; above 8 rows always 8 (their
+// activation slots fill shared memory).
+static bool xres_for(int64_t T, int64_t nch) { return nch <= kXResChunks && T >= 8192; }
+
 static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
     const int64_t nch = (in_f + kChunkElems - 1) / kChunkElems;
     const int64_t T = (rows + kTileRows - 1) / kTileRows * nch;
@@ -626,22 +661,23 @@ static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
     if (batch == 1) return wide ? GemvCfg<1, 12>::kWarps : GemvCfg<1, 8>::kWarps;
     if (batch == 2) return wide ? GemvCfg<2, 12>::kWarps : GemvCfg<2, 8>::kWarps;
     if (batch <= 4) return wide ? GemvCfg<4, 12>::kWarps : GemvCfg<4, 8>::kWarps;
-    if (batch <= 8) return wide ? GemvCfg<8, 10>::kWarps : GemvCfg<8, 8>::kWarps;
+    if (batch <= 8)
+        return wide ? (xres_for(T, nch) ? GemvCfg<8, 12, true>::kWarps : GemvCfg<8, 10>::kWarps) : GemvCfg<8, 8>::kWarps;
     return GemvCfg<16, 8>::kWarps;
 }
 
 // partial sums: per unit two [16][8] (batch <= 8) or [16][16] fp32 slots
 static int64_t scratch_need(const GemvLaunch &L, int64_t batch) { return L.W * 2 * 16 * (batch > 8 ? 16 : 8) * 4; }
 
-template <int BMAX, int NW>
+template <int BMAX, int NW, bool XRES = false>
 static int launch_gemv(const GemvParams &p, const GemvLaunch &L, cudaStream_t st) {
-    using C = GemvCfg<BMAX, NW>;
+    using C = GemvCfg<BMAX, NW, XRES>;
     int dev = 0;
     cudaGetDevice(&dev);
     static bool attr_set[64] = {false};
     if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv: device index %d", dev);
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BMAX, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BMAX, NW, XRES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
         if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: smem attribute: %s", cudaGetErrorString(e));
         attr_set[dev] = true;
     }
@@ -657,7 +693,7 @@ static int launch_gemv(const GemvParams &p, const GemvLaunch &L, cudaStream_t st
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<BMAX, NW>, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<BMAX, NW, XRES>, p);
     if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: launch: %s", cudaGetErrorString(e));
     return check_launch("bf16x_gemv");
 }
@@ -718,7 +754,10 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
     if (batch == 1) return nw > 8 ? launch_gemv<1, 12>(p, L, st) : launch_gemv<1, 8>(p, L, st);
     if (batch == 2) return nw > 8 ? launch_gemv<2, 12>(p, L, st) : launch_gemv<2, 8>(p, L, st);
     if (batch <= 4) return nw > 8 ? launch_gemv<4, 12>(p, L, st) : launch_gemv<4, 8>(p, L, st);
-    if (batch <= 8) return nw > 8 ? launch_gemv<8, 10>(p, L, st) : launch_gemv<8, 8>(p, L, st);
+    if (batch <= 8) {
+        if (nw <= 8) return launch_gemv<8, 8>(p, L, st);
+        return xres_for(L.T, L.nch) ? launch_gemv<8, 12, true>(p, L, st) : launch_gemv<8, 10>(p, L, st);
+    }
     return launch_gemv<16, 8>(p, L, st);
 }
 

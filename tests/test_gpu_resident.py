@@ -156,9 +156,11 @@ def test_repack_filtered_table():
     _lib.check_device_status()
 
 
-# (4096, 1024) at 6 rows: the configuration that keeps the whole activation
-# block in shared memory (5..8 rows, in_f <= 4096, enough tiles for 10 warps)
-@pytest.mark.parametrize("shape,b", [((300, 1536), 1), ((300, 1536), 8), ((300, 1536), 13), ((4096, 1024), 6)])
+# 6 rows: (4096, 1024) runs a 10-warp configuration, (8192, 4096) the one
+# that keeps the CTA's whole activation block in shared memory and stages
+# fewer record words (5..8 rows, in_f <= 4096, at least 8192 items)
+@pytest.mark.parametrize("shape,b", [((300, 1536), 1), ((300, 1536), 8), ((300, 1536), 13), ((4096, 1024), 6),
+                                     ((8192, 4096), 6)])
 def test_gemv_dense_patches(shape, b):
     from tests.test_gpu_gemm import _dense_patch_weight
     wb = _dense_patch_weight(*shape, seed=9)
