@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the BF16X fused decode+GEMV hot path.
+"""Benchmark of the BF16X fused decode+GEMV hot path (the four-shape decode sweep).
 
 One step = one pass of the fused decode+GEMV over the four benchmark weight
 shapes ([out x in] = 4096x4096, 14336x4096, 4096x14336, 128256x4096) at the
@@ -488,7 +488,7 @@ def run_ours(args):
 
 def run_gemm(args):
     """Prefill: one step = the fused decode+GEMM over the four weight shapes at
-    M tokens (BASELINE config 3); value = TFLOPS (2*M*out*in per launch)."""
+    M tokens; value = TFLOPS (2*M*out*in per launch)."""
     import torch
     import torch.distributed as dist
 
@@ -599,7 +599,7 @@ def run_gemm(args):
 
 
 def run_e2e(args):
-    """BASELINE configs 4/5: greedy decode after a prompt prefill, ms per
+    """Llama-style decoders (1B, 8B): greedy decode after a prompt prefill, ms per
     generated token with BF16X weights (every projection and lm_head through
     the fused kernels) and with the same weights in plain bf16.  Under
     torchrun the model is tensor-parallel over the ranks (one GPU each)."""

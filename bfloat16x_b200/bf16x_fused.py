@@ -5,8 +5,8 @@
   per-row CSR of overflow corrections (``olk`` column, ``old`` true delta,
   ``oloff`` row offsets).  It runs the sm_100a decode+GEMV kernel on the
   resident layout, which it builds from those tensors on the first call and
-  caches by their addresses (the reference modules build their CSR once at
-  ``__init__`` the same way).  ``r``, ``bk``, ``group`` and ``num_warps`` are
+  caches for as long as the same tensor objects live unmodified (the
+  reference modules build their CSR once at ``__init__`` the same way).  ``r``, ``bk``, ``group`` and ``num_warps`` are
   Triton tuning knobs of the reference kernel; they are accepted and ignored.
 * ``Bf16xFused`` -- the three-mode Linear (bf16x_fused.py:149-229):
   ``'fused'`` runs the fused kernels (decode+GEMV for up to 16 rows of
@@ -22,6 +22,7 @@ Everything computes on the GPU through the C ABI; there is no CPU path.
 """
 from __future__ import annotations
 
+import weakref
 from collections import OrderedDict
 
 import torch
@@ -33,7 +34,49 @@ from .bf16x_decode import bf16x_decode_triton
 from .resident import ResidentWeight
 
 _CACHE_SLOTS = 256
-_RESIDENT_CACHE: "OrderedDict[tuple, ResidentWeight]" = OrderedDict()
+# address key -> _CacheEntry.  An entry is used only while every stream tensor
+# it was built from is the same live object at the same version: torch's
+# caching allocator hands freed addresses to new tensors, so an address alone
+# could return another weight's layout.
+_RESIDENT_CACHE: "OrderedDict[tuple, _CacheEntry]" = OrderedDict()
+
+
+class _CacheEntry:
+    __slots__ = ("refs", "versions", "rw", "__weakref__")
+
+    def __init__(self, tensors, rw):
+        self.refs = tuple(weakref.ref(t) for t in tensors)
+        self.versions = tuple(t._version for t in tensors)
+        self.rw = rw
+
+    def valid_for(self, tensors) -> bool:
+        return all(r() is t and t._version == v for r, t, v in zip(self.refs, tensors, self.versions))
+
+
+def _evict(key, ent_ref) -> None:
+    if _RESIDENT_CACHE.get(key) is ent_ref():
+        _RESIDENT_CACHE.pop(key, None)
+
+
+def cached_resident(key_tag, streams, build) -> ResidentWeight:
+    """The resident layout built by ``build()`` from the tensors ``streams``,
+    reused while those very tensor objects live unmodified.  The lookup key
+    holds their addresses; the entry is checked against the objects and their
+    in-place version counters, so a new tensor at a freed address, or a stream
+    edited in place, gets a fresh layout."""
+    key = (key_tag,) + tuple(t.data_ptr() if t is not None else 0 for t in streams)
+    live = tuple(t for t in streams if t is not None)
+    ent = _RESIDENT_CACHE.get(key)
+    if ent is not None and ent.valid_for(live):
+        _RESIDENT_CACHE.move_to_end(key)
+        return ent.rw
+    ent = _CacheEntry(live, build())
+    _RESIDENT_CACHE[key] = ent
+    # the layout is released as soon as the first stream it came from dies
+    weakref.finalize(live[0], _evict, key, weakref.ref(ent))
+    while len(_RESIDENT_CACHE) > _CACHE_SLOTS:
+        _RESIDENT_CACHE.popitem(last=False)
+    return ent.rw
 
 
 def _pad1(t: torch.Tensor) -> torch.Tensor:
@@ -56,23 +99,17 @@ def csr_to_table(olk: torch.Tensor, old: torch.Tensor, oloff: torch.Tensor, in_f
     return idx.to(torch.int32), val.to(torch.uint8)
 
 
-def _resident_from_streams(sign, mant, delta, emax, ovf_idx, ovf_val, out_f, in_f, key=None) -> ResidentWeight:
-    if key is not None and key in _RESIDENT_CACHE:
-        _RESIDENT_CACHE.move_to_end(key)
-        return _RESIDENT_CACHE[key]
+def _resident_from_streams(sign, mant, delta, emax, ovf_idx, ovf_val, out_f, in_f) -> ResidentWeight:
     p = {"sign_packed": sign, "mant_packed": mant, "delta_packed": delta, "emax": emax,
          "delta_ovf_idx": ovf_idx, "delta_ovf_val": ovf_val, "out_f": int(out_f), "in_f": int(in_f), "sub": 16}
-    rw = ResidentWeight.from_packed(p, device=sign.device)
-    if key is not None:
-        _RESIDENT_CACHE[key] = rw
-        while len(_RESIDENT_CACHE) > _CACHE_SLOTS:
-            _RESIDENT_CACHE.popitem(last=False)
-    return rw
+    return ResidentWeight.from_packed(p, device=sign.device)
 
 
 def clear_cache() -> None:
-    """Drop the resident layouts built by ``bf16x_fused_gemv`` (call after
-    changing the contents of stream tensors in place)."""
+    """Drop the resident layouts built by ``bf16x_fused_gemv``.  Not needed
+    for correctness: an entry is rebuilt whenever a stream tensor it was built
+    from has died or been modified in place (torch's version counter); this
+    only releases the device memory early."""
     _RESIDENT_CACHE.clear()
 
 
@@ -86,15 +123,15 @@ def bf16x_fused_gemv(x, sign, mant, delta, emax, olk, old, oloff,
         raise ValueError("only 16-element sub-blocks are supported")
     if x.numel() != in_f:
         raise ValueError(f"bf16x_fused_gemv takes one vector of {in_f} elements, got {x.numel()}")
-    key = (x.device.index, sign.data_ptr(), mant.data_ptr(), delta.data_ptr(), emax.data_ptr(),
-           olk.data_ptr(), old.data_ptr(), oloff.data_ptr(), int(out_f), int(in_f))
-    rw = _RESIDENT_CACHE.get(key)
-    if rw is None:
-        oi, ov = csr_to_table(olk.to(x.device), old.to(x.device), oloff.to(x.device), in_f)
-        rw = _resident_from_streams(sign.to(x.device), mant.to(x.device), delta.to(x.device),
-                                    emax.to(x.device), oi, ov, out_f, in_f, key=key)
-    else:
-        _RESIDENT_CACHE.move_to_end(key)
+    dev = x.device
+
+    def build():
+        oi, ov = csr_to_table(olk.to(dev), old.to(dev), oloff.to(dev), in_f)
+        return _resident_from_streams(sign.to(dev), mant.to(dev), delta.to(dev), emax.to(dev), oi, ov,
+                                      out_f, in_f)
+
+    rw = cached_resident(("gemv", dev.index, int(out_f), int(in_f)), (sign, mant, delta, emax, olk, old, oloff),
+                         build)
     return rw.gemv(x.reshape(1, in_f), out_dtype=torch.bfloat16).reshape(out_f)
 
 

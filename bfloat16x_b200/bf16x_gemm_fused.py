@@ -24,7 +24,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib
-from .bf16x_fused import _RESIDENT_CACHE, _linear_targets, _resident_from_streams, _set_module
+from .bf16x_fused import _linear_targets, _resident_from_streams, _set_module, cached_resident
 from .resident import ResidentWeight
 
 _CHUNK_MB = 1024
@@ -68,20 +68,18 @@ def bf16x_fused_gemm(x, sign, mant, delta, emax, out_f, in_f, group=16,
     M = x.numel() // int(in_f)
     dev = x.device
     has_ovf = ovf_idx is not None and ovf_idx.numel() > 0
-    key = ("gemm", dev.index, sign.data_ptr(), mant.data_ptr(), delta.data_ptr(), emax.data_ptr(),
-           ovf_idx.data_ptr() if has_ovf else 0, int(out_f), int(in_f))
-    rw = _RESIDENT_CACHE.get(key)
-    if rw is None:
+
+    def build():
         if has_ovf:
             oi = ovf_idx.to(dev, torch.int32)
             ov = ovf_val.to(dev, torch.uint8)
         else:
             oi = torch.empty(0, dtype=torch.int32, device=dev)
             ov = torch.empty(0, dtype=torch.uint8, device=dev)
-        rw = _resident_from_streams(sign.to(dev), mant.to(dev), delta.to(dev), emax.to(dev), oi, ov,
-                                    out_f, in_f, key=key)
-    else:
-        _RESIDENT_CACHE.move_to_end(key)
+        return _resident_from_streams(sign.to(dev), mant.to(dev), delta.to(dev), emax.to(dev), oi, ov, out_f, in_f)
+
+    streams = (sign, mant, delta, emax) + ((ovf_idx, ovf_val) if has_ovf else ())
+    rw = cached_resident(("gemm", dev.index, int(out_f), int(in_f), has_ovf), streams, build)
     od = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
     y = rw.gemm(x.reshape(M, int(in_f)), out_dtype=od)
     return y.to(x.dtype)

@@ -86,15 +86,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs, sets kErrWaitTimeout in *status and returns false, so a
-// broken pipeline ends the kernel with an error instead of hanging the GPU.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *status) {
+// limit_ns (kWaitLimitNs in the kernels), sets kErrWaitTimeout in *status and
+// returns false, so a broken pipeline ends the kernel with an error instead of
+// hanging the GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *status,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(a, parity)) return true;
-        if ((i & 7u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+        if ((i & 7u) == 0 && globaltimer_ns() - t0 > limit_ns) {
             atomicOr(status, kErrWaitTimeout);
             return false;
         }

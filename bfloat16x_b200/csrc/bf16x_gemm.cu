@@ -39,6 +39,7 @@
 #include "bf16x_resident.cuh"
 #include "bf16x_status.cuh"
 #include "bf16x_tmap.h"
+#include "bf16x_wait.cuh"
 
 namespace bf16x {
 
@@ -144,28 +145,6 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 // 128-byte-swizzled tile (16-byte chunk index XOR row % 8).
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
     return row * 128u + ((((col >> 3) ^ row) & 7u) << 4) + ((col & 7u) << 1);
-}
-
-// Bounded wait used by every role; on timeout the abort flag is raised and
-// false is returned, and a role that finds the flag raised while waiting
-// gives up too.
-// The fast path (phase already complete) reads nothing else: the abort flag
-// is a shared-memory load, and on the MMA issuer's path one such load per
-// wait measurably slows the issue of the k-blocks.  It is checked while
-// waiting instead.
-__device__ __forceinline__ bool role_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    const uint32_t a = smem_u32(bar);
-    if (mbar_try_wait(a, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (*abort_flag) return false;
-        if (mbar_try_wait(a, parity)) return true;
-        if ((i & 7u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(&g_status, kErrWaitTimeout);
-            *abort_flag = 1;
-            return false;
-        }
-    }
 }
 
 template <int BN>
@@ -965,30 +944,6 @@ struct SlabParams {
     int y_f32;
     int64_t ldy;
 };
-
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
-
-// Wait until *ctr >= target (another CTA's progress); bounded like role_wait.
-__device__ __forceinline__ bool counter_wait(const uint32_t *ctr, uint32_t target, volatile int *abort_flag) {
-    if (ld_acquire_gpu(ctr) >= target) return true;
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (*abort_flag) return false;
-        __nanosleep(64);
-        if (ld_acquire_gpu(ctr) >= target) return true;
-        if ((i & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(&g_status, kErrWaitTimeout);
-            *abort_flag = 1;
-            return false;
-        }
-    }
-}
 
 // load_group for the compressed weight in global memory, read once per
 // launch: evict-first loads, so the stream of compressed weights does not

@@ -42,9 +42,9 @@ class LlamaConfig:
 
 
 CONFIGS = {
-    # 1B-class Llama-style decoder
+    # 1B-class Llama-style decoder (hidden 2048, 24 layers, GQA 16/8, vocab 73448)
     "1b": LlamaConfig(hidden=2048, layers=24, heads=16, kv_heads=8, head_dim=128, ffn=6144, vocab=73448),
-    # 8B Llama-3-style decoder
+    # 8B Llama-3-style decoder (hidden 4096, 32 layers, GQA 32/8, vocab 128256)
     "8b": LlamaConfig(hidden=4096, layers=32, heads=32, kv_heads=8, head_dim=128, ffn=14336, vocab=128256),
     # a small one for tests
     "tiny": LlamaConfig(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000),

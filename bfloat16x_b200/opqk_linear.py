@@ -118,6 +118,11 @@ class BF16XLinear(nn.Module):
     def weight(self):
         return torch.zeros(1, 1, dtype=torch.bfloat16, device=self.resident.device)
 
+    def _decode_tile(self, s, e):
+        """Exact bf16 rows [s, e) of the weight, [e - s, in_f] on the device
+        (opqk_linear.py:360-377 decodes the same rows from the flat streams)."""
+        return self.resident.decode_rows(s, e)
+
     def decode_to_bf16(self):
         self._w_bf16 = self.resident.decode()
         return self._w_bf16

@@ -185,6 +185,23 @@ class ResidentWeight:
                  self.rows, self.in_f, ptr(out), out.stride(0), self._stream())
         return out
 
+    def decode_rows(self, r0: int, r1: int) -> torch.Tensor:
+        """Exact bf16 rows [r0, r1) of this weight (relative to its first row).
+        Decoding starts at the 16-row tile holding r0: a tile's record covers
+        its 16 rows, so the layout and record offsets are entered there."""
+        r0, r1 = int(r0), int(r1)
+        if not (0 <= r0 <= r1 <= self.rows):
+            raise ValueError(f"row range [{r0}, {r1}) outside 0..{self.rows}")
+        a = r0 // TILE_ROWS * TILE_ROWS
+        out = torch.empty((r1 - a, self.in_f), dtype=torch.bfloat16, device=self.device)
+        if r1 > a:
+            nch = (self.in_f + CHUNK_ELEMS - 1) // CHUNK_ELEMS
+            with torch.cuda.device(self.device):
+                call("bf16x_resident_decode", self.layout.data_ptr() + a * self.row_bytes,
+                     self.ptile_off.data_ptr() + 4 * (a // TILE_ROWS) * nch, ptr(self.precs),
+                     r1 - a, self.in_f, ptr(out), out.stride(0), self._stream())
+        return out[r0 - a:]
+
     def _prep_x(self, x2: torch.Tensor) -> torch.Tensor:
         """bf16 activations with a row pitch covering the padded columns (zeros)."""
         x2 = x2.to(torch.bfloat16)

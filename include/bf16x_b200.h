@@ -154,11 +154,12 @@ int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *
  * device memory, for callers that cannot allocate: a plain C host or FFI
  * binding with no device allocator of its own, or a serving loop that must
  * not call cudaMalloc/cudaFree (which synchronise the device) once running.
- * Same arguments, results and limits as bf16x_gemv otherwise; nothing is
- * allocated.  The tile counters and partial sums live in one fixed device
- * array of this library (2 MiB of partial sums + 128 KiB of counters per
- * device), so rows <= bf16x_gemv_noalloc_max_rows() (524288); larger requests
- * fail with BF16X_ERR_UNSUPPORTED.  Each call clears its counters on
+ * Same arguments and results as bf16x_gemv otherwise, but batch 1..8 only
+ * (9..16 rows fail with BF16X_ERR_INVALID: their partial sums are twice as
+ * large); nothing is allocated.  The tile counters and partial sums live in
+ * one fixed device array of this library (2 MiB of partial sums + 128 KiB of
+ * counters per device), so rows <= bf16x_gemv_noalloc_max_rows() (524288);
+ * larger requests fail with BF16X_ERR_UNSUPPORTED.  Each call clears its counters on
  * `stream` before the launch.  The first call on a device looks up that
  * array's address (cudaGetSymbolAddress), so make it before any stream
  * capture.  All calls on a device share the one array: calls that can
@@ -222,6 +223,17 @@ int bf16x_gguf_ovf_pack(const void *x, int x_dtype, int64_t rows, int64_t cols, 
  * exact value into y [rows][cols] (bf16 bits or float32). */
 int bf16x_gguf_apply_ovf(void *y, int y_dtype, int64_t rows, int64_t cols, const uint32_t *row_off,
                          const uint16_t *ecols, const uint16_t *ebits, int64_t n_entries, void *stream);
+
+/* ---- self-test of the bounded waits ------------------------------------- */
+/* No counterpart in the reference.  Runs one of the library's bounded device
+ * waits -- which: 0 the GEMV's mbarrier wait, 1 the tcgen05 GEMM roles' wait,
+ * 2 the slab GEMM's cross-CTA counter wait, 3 the collective GEMV's peer-flag
+ * wait -- against a fresh mbarrier that nothing completes (0, 1) or until
+ * *flag (device u32) reaches 1, with a limit of limit_ns (1 us .. 100 ms).
+ * result (device int32[3]): gave up (1/0), abort flag raised (1/0),
+ * microseconds waited.  A wait that gives up sets the wait-timeout bit read by
+ * bf16x_device_status; the kernel returns and the context stays usable. */
+int bf16x_selftest_wait(int which, int64_t limit_ns, const uint32_t *flag, int32_t *result, void *stream);
 
 #ifdef __cplusplus
 }

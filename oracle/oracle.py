@@ -52,6 +52,7 @@ def lib() -> ctypes.CDLL:
         _lib.oracle_linear.argtypes = [p, i64, p, i64, p, i64, p, p, p, i64,
                                        i64, i64, i64, p, i64, p, p]
         _lib.oracle_num_threads.restype = ctypes.c_int
+        _lib.oracle_set_num_threads.argtypes = [ctypes.c_int]
         _lib.oracle_f32_to_bf16_bits.argtypes = [p, i64, p]
         _lib.oracle_gguf_quantize_blocks.argtypes = [p, i64, p]
         _lib.oracle_gguf_dequantize_blocks.argtypes = [p, i64, p]
@@ -71,6 +72,10 @@ def stream_words(n: int, b: int) -> int:
 
 def num_threads() -> int:
     return int(lib().oracle_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    lib().oracle_set_num_threads(int(n))
 
 
 # --------------------------------------------------------------------------- #

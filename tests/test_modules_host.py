@@ -55,3 +55,38 @@ def test_empty_csr():
     ti, tv = csr_to_table(torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
                           torch.zeros(5, dtype=torch.int32), 64)
     assert ti.numel() == 0 and tv.numel() == 0
+
+
+def test_resident_cache_keys_on_live_objects():
+    """The functional entry points' layout cache (cached_resident) reuses a
+    layout only for the very stream objects it was built from, unmodified:
+    another tensor at the same address (a view here; a new allocation at a
+    freed address on the GPU), an in-place edit, or a dead stream rebuild."""
+    import gc
+
+    from bfloat16x_b200 import bf16x_fused as bf
+    built = []
+
+    def build():
+        built.append(object())
+        return built[-1]
+
+    bf.clear_cache()
+    a = torch.arange(64, dtype=torch.int32)
+    b = torch.arange(16, dtype=torch.int32)
+    r1 = bf.cached_resident(("t",), (a, b), build)
+    assert bf.cached_resident(("t",), (a, b), build) is r1 and len(built) == 1
+    view = a[:]                                   # same address, another object
+    assert view.data_ptr() == a.data_ptr()
+    r2 = bf.cached_resident(("t",), (view, b), build)
+    assert r2 is not r1 and len(built) == 2
+    b.add_(1)                                     # in-place edit: version counter moves
+    r3 = bf.cached_resident(("t",), (view, b), build)
+    assert r3 is not r2 and len(built) == 3
+    assert bf.cached_resident(("t",), (view, b), build) is r3
+    key = (("t",), view.data_ptr(), b.data_ptr())
+    assert key in bf._RESIDENT_CACHE
+    del view
+    gc.collect()
+    assert key not in bf._RESIDENT_CACHE          # evicted when its first stream died
+    bf.clear_cache()

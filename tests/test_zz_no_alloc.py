@@ -57,6 +57,9 @@ def _gemv_noalloc(rw, xp, bias, y):
     ((64, 14336), 8, torch.bfloat16),
     ((14336, 4096), 2, torch.float32),
     ((33, 96), 5, torch.bfloat16),
+    # 6 rows on 8192 x 4096: the 12-warp configuration that keeps the CTA's
+    # whole activation block in shared memory (most warps, most partial sums)
+    ((8192, 4096), 6, torch.float32),
 ])
 def test_noalloc_matches_gemv_twice(shape, batch, dtype):
     rw = _weight(*shape, seed=41)
@@ -90,3 +93,17 @@ def test_noalloc_rejects_oversize():
         # the size check comes before any pointer is used
         call("bf16x_gemv_noalloc", ptr(rw.layout), ptr(rw.ptile_off), ptr(rw.precs), limit + 16, rw.in_f,
              ptr(xp), 1, xp.stride(0), None, ptr(y), BF16X_DTYPE_F32, y.stride(0), _stream())
+
+
+def test_noalloc_rejects_batch_above_8():
+    # 9..16 activation rows need twice the partial sums of the fixed scratch;
+    # bf16x_gemv takes them, the no-alloc entry point refuses them up front
+    rw = _weight(64, 512, seed=61)
+    xp = _x(rw, 9, seed=67)
+    y = torch.empty((9, rw.rows), dtype=torch.float32, device="cuda")
+    with pytest.raises(_lib.Bf16xError, match="batch must be 1..8"):
+        _gemv_noalloc(rw, xp, None, y)
+    y_ref = torch.empty_like(y)
+    _gemv_owned(rw, xp, None, y_ref)
+    torch.cuda.synchronize()
+    assert np.isfinite(y_ref.cpu().numpy()).all()
