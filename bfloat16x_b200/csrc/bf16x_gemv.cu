@@ -43,9 +43,11 @@
 #include "bf16x_resident.cuh"
 #include "bf16x_status.cuh"
 #include "bf16x_tmap.h"
+#include "bf16x_wait.cuh"
 
 namespace bf16x {
 
+constexpr int kMaxRanks = 8;          // GPUs of one NVSwitch domain reached by the collective epilogue
 constexpr int kPcapWords = 256;      // record words staged per slot: emax, header, 222 entries (more: from L2)
 constexpr int kSparseEntries = 8;    // items with more patch entries take the fragment round trip
 constexpr int kXRowBytes = kChunkElems * 2;
@@ -106,6 +108,15 @@ struct GemvParams {
     int64_t ldy;
     int32_t *tile_cnt;  // n_tiles counters, zero between launches
     float *partials;    // scratch: W x 2 x [16][8]
+    // Collective epilogue (nranks > 1): every output is stored to ydst[q] for
+    // each rank q (peer memory over NVLink, ydst[rank] is this GPU's), then the
+    // last warp to finish posts this launch's epoch to flags[q][rank] of every
+    // rank and waits until its own flags[rank][*] all carry it.  state: this
+    // GPU's [finished warps, epoch] words.
+    int nranks, rank;
+    void *ydst[kMaxRanks];
+    uint32_t *flags[kMaxRanks];
+    uint32_t *state;
 };
 
 __device__ __forceinline__ void mma_bf16_16816(float &c0, float &c1, float &c2, float &c3, uint32_t a0, uint32_t a1,
@@ -258,6 +269,47 @@ __device__ __forceinline__ void half_mma2(const StepFrag (&f)[8], const uint16_t
     mma_bf16_16816(c[0], c[1], c[2], c[3], f[J].a0, f[J].a1, f[J].a2, f[J].a3, b.x, b.y);
     mma_bf16_16816(d[0], d[1], d[2], d[3], f[J].a0, f[J].a1, f[J].a2, f[J].a3, b2.x, b2.y);
     if constexpr (J + 1 < 8) half_mma2<J + 1>(f, xq, xq2, ce, co, de, dd);
+}
+
+// One output value to every destination: this GPU's y, and with the
+// collective epilogue the same position of every other rank's y.
+__device__ __forceinline__ void store_y(const GemvParams &p, int64_t idx, float o) {
+    if (p.y_f32) {
+        for (int q = 0; q < p.nranks; ++q) reinterpret_cast<float *>(p.ydst[q])[idx] = o;
+    } else {
+        const uint16_t v = f32_to_bf16_bits_rn(o);
+        for (int q = 0; q < p.nranks; ++q) reinterpret_cast<uint16_t *>(p.ydst[q])[idx] = v;
+    }
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+// End of the collective epilogue, run by every warp that took part in the
+// partition once its outputs are stored (their peer stores included).  The
+// warp makes its stores visible system-wide and counts itself; the last one
+// of the grid resets the count, advances the epoch, posts it to every rank's
+// flag word for this rank (a release at system scope, after a full fence that
+// covers every warp's stores it observed through the count) and waits,
+// bounded, until every rank has posted the same epoch here.  Only then does
+// the kernel complete, so the next kernel of the stream sees all ranks' rows.
+__device__ __forceinline__ void collective_finish(const GemvParams &p, int64_t n_warps, int lane) {
+    __threadfence_system();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(p.state, 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + 1 != (uint32_t)n_warps) return;
+    __threadfence_system();
+    const uint32_t epoch = p.state[1] + 1u;
+    if (lane == 0) {
+        p.state[0] = 0u;
+        p.state[1] = epoch;
+    }
+    if (lane < p.nranks) st_release_sys(p.flags[lane] + p.rank, epoch);
+    if (lane < p.nranks) peer_flag_wait(p.flags[p.rank] + lane, epoch);
+    __syncwarp();
 }
 
 // Warp w of the partition owns items [T*w/W, T*(w+1)/W); item i belongs to
@@ -431,8 +483,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
             const int64_t row = row0 + rr;
             if (b < p.batch && row < p.rows) {
                 if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
-                if (p.y_f32) reinterpret_cast<float *>(p.y)[b * p.ldy + row] = o;
-                else reinterpret_cast<uint16_t *>(p.y)[b * p.ldy + row] = f32_to_bf16_bits_rn(o);
+                store_y(p, b * p.ldy + row, o);
             }
         }
         if (lane == 0) p.tile_cnt[tl] = 0;
@@ -541,8 +592,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
                     if (b < p.batch && row < p.rows) {
                         float o = v[k];
                         if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
-                        if (p.y_f32) reinterpret_cast<float *>(p.y)[b * p.ldy + row] = o;
-                        else reinterpret_cast<uint16_t *>(p.y)[b * p.ldy + row] = f32_to_bf16_bits_rn(o);
+                        store_y(p, b * p.ldy + row, o);
                     }
                 }
             } else {
@@ -572,6 +622,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
         if (++s == S) { s = 0; parity ^= 1u; }
         if (++c == p.nch) { c = 0; ++tile; }
     }
+    if (p.nranks > 1) collective_finish(p, p.W, lane);
 }
 
 struct GemvLaunch {
@@ -709,10 +760,56 @@ extern "C" int64_t bf16x_gemv_scratch_bytes(int64_t rows, int64_t in_f) {
     return need;
 }
 
+namespace bf16x {
+
+// Destinations of the collective epilogue (bf16x_gemv_peers); none for the
+// plain GEMV.
+struct PeerArgs {
+    int nranks, rank;
+    void *const *ydst;
+    uint32_t *const *flags;
+    uint32_t *state;
+};
+
+static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                     int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
+                     const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
+                     int32_t *tile_counters, void *scratch, int64_t scratch_bytes, void *stream,
+                     const PeerArgs *peers);
+
+}  // namespace bf16x
+
 extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
                           int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
                           const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
                           int32_t *tile_counters, void *scratch, int64_t scratch_bytes, void *stream) {
+    return gemv_impl(layout, ptile_off, precs, rows, in_f, x, batch, ldx, bias, y, y_dtype, ldy, tile_counters,
+                     scratch, scratch_bytes, stream, nullptr);
+}
+
+extern "C" int bf16x_gemv_peers(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                                int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
+                                const uint16_t *bias, void *const *ydst, int nranks, int rank, int y_dtype,
+                                int64_t ldy, uint32_t *const *flags, uint32_t *state, int32_t *tile_counters,
+                                void *scratch, int64_t scratch_bytes, void *stream) {
+    if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: need 1 <= nranks <= %d and 0 <= rank < nranks", kMaxRanks);
+    if (!ydst || !flags || !state) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: null destination table");
+    for (int q = 0; q < nranks; ++q)
+        if (!ydst[q] || !flags[q]) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: null pointer for rank %d", q);
+    if (rows <= 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: every rank needs rows (its peers wait for it)");
+    const PeerArgs pa{nranks, rank, ydst, flags, state};
+    return gemv_impl(layout, ptile_off, precs, rows, in_f, x, batch, ldx, bias, ydst[rank], y_dtype, ldy,
+                     tile_counters, scratch, scratch_bytes, stream, &pa);
+}
+
+namespace bf16x {
+
+static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                     int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
+                     const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
+                     int32_t *tile_counters, void *scratch, int64_t scratch_bytes, void *stream,
+                     const PeerArgs *peers) {
     if (rows < 0 || in_f <= 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: bad shape");
     if (in_f > 65536) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv: in_f > 65536");
     if (batch < 1 || batch > 16) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: batch must be 1..16 (got %lld)", (long long)batch);
@@ -733,7 +830,7 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: scratch of %lld bytes needed", (long long)scratch_need(L, batch));
     if (reinterpret_cast<uintptr_t>(scratch) & 15u)
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: scratch must be 16-byte aligned");
-    GemvParams p;
+    GemvParams p = {};
     {
         int dev = 0;
         cudaGetDevice(&dev);
@@ -750,6 +847,19 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
     p.bias = bias; p.y = y; p.y_f32 = y_dtype == BF16X_DTYPE_F32; p.ldy = ldy;
     p.tile_cnt = tile_counters;
     p.partials = static_cast<float *>(scratch);
+    p.nranks = 1;
+    p.rank = 0;
+    p.ydst[0] = y;
+    p.state = nullptr;
+    if (peers) {
+        p.nranks = peers->nranks;
+        p.rank = peers->rank;
+        for (int q = 0; q < peers->nranks; ++q) {
+            p.ydst[q] = peers->ydst[q];
+            p.flags[q] = peers->flags[q];
+        }
+        p.state = peers->state;
+    }
     cudaStream_t st = (cudaStream_t)stream;
     if (batch == 1) return nw > 8 ? launch_gemv<1, 12>(p, L, st) : launch_gemv<1, 8>(p, L, st);
     if (batch == 2) return nw > 8 ? launch_gemv<2, 12>(p, L, st) : launch_gemv<2, 8>(p, L, st);
@@ -760,6 +870,8 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
     }
     return launch_gemv<16, 8>(p, L, st);
 }
+
+}  // namespace bf16x
 
 // ------------------------------------------------ no-allocation GEMV entry
 // bf16x_gemv_noalloc serves callers that cannot hand this library device

@@ -236,6 +236,36 @@ class ResidentWeight:
                  self._stream())
         return out
 
+    def gemv_peers(self, x: torch.Tensor, peers, offset: int, ldy: int, col0: int,
+                   bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16) -> None:
+        """The fused decode+GEMV of this rank's rows whose epilogue stores
+        every output straight into every rank's copy of the PeerGroup heap
+        buffer at ``offset`` ([batch][ldy] of out_dtype, this shard's rows at
+        columns col0..col0+rows): the row-sharded layer's all-gather happens
+        inside the kernel, over NVLink.  The kernel completes once every
+        rank's rows have arrived here."""
+        _lib.require_cuda(x, "x")
+        x2 = x.reshape(-1, self.in_f)
+        B = x2.shape[0]
+        if B < 1 or B > GEMV_MAX_BATCH:
+            raise ValueError(f"gemv takes 1..{GEMV_MAX_BATCH} rows of activations, got {B}")
+        xp = self._prep_x(x2)
+        ydt = {torch.bfloat16: BF16X_DTYPE_BF16, torch.float32: BF16X_DTYPE_F32}[out_dtype]
+        esize = 2 if out_dtype == torch.bfloat16 else 4
+        b = None if bias is None else bias.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        key = (offset, col0, esize)
+        tables = getattr(self, "_peer_tables", None)
+        if tables is None or tables[0] != (id(peers), key):
+            tables = ((id(peers), key), peers.table(offset + col0 * esize))
+            self._peer_tables = tables
+        with torch.cuda.device(self.device):
+            if self._scratch_need is None:
+                self._scratch_need = int(_lib.lib().bf16x_gemv_scratch_bytes(self.rows, self.in_f))
+            ws = gemv_scratch(self.device, self._scratch_need)
+            call("bf16x_gemv_peers", ptr(self.layout), ptr(self.ptile_off), ptr(self.precs), self.rows, self.in_f,
+                 ptr(xp), B, xp.stride(0), ptr(b), tables[1], peers.world, peers.rank, ydt, int(ldy),
+                 peers.flag_table, peers.state_ptr, ptr(self.tile_counters), ptr(ws), ws.numel(), self._stream())
+
     def gemm(self, x: torch.Tensor, bias: torch.Tensor | None = None,
              out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
         """y[m, n] = sum_k W[n, k] x[m, k] (+ bias) on the tensor cores, any number of rows m."""

@@ -171,6 +171,39 @@ int bf16x_gemv_noalloc(const uint8_t *layout, const int32_t *ptile_off, const ui
                        const uint16_t *x, int64_t batch, int64_t ldx,
                        const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream);
 
+/* ---- tensor parallel over NVLink: GEMV with the all-gather inside -------- */
+/* The row-sharded layer of tensor parallelism (each of nranks GPUs of one
+ * node holds rows of the weight) needs every rank's output rows on
+ * every rank.  The reference has no multi-GPU path; this replaces
+ * bf16x_fused_gemv (bf16x_fused.py:114-127) + a separate all-gather.
+ * bf16x_gemv_peers is bf16x_gemv whose epilogue stores each output to
+ * ydst[q] + b*ldy + row for every rank q (ydst: host array of nranks device
+ * pointers, ydst[rank] on this GPU, the others peer memory mapped with
+ * bf16x_peer_import), then the last warp posts the launch's epoch to
+ * flags[q][rank] for every q and waits (bounded) until flags[rank][0..nranks)
+ * all carry it: the kernel completes only once every rank's rows are here.
+ * state: this GPU's two zeroed u32 words (finished warps, epoch), shared by
+ * the collective GEMVs of one group, which must run in the same order on
+ * every rank, on one stream each.  flags: host array of nranks device
+ * pointers to each rank's nranks zeroed u32 flag words.  nranks <= 8,
+ * rows >= 1 on every rank. */
+int bf16x_gemv_peers(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
+                     int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
+                     const uint16_t *bias, void *const *ydst, int nranks, int rank, int y_dtype,
+                     int64_t ldy, uint32_t *const *flags, uint32_t *state, int32_t *tile_counters,
+                     void *scratch, int64_t scratch_bytes, void *stream);
+
+/* CUDA IPC plumbing for the peer pointers above (no counterpart in the
+ * reference).  bf16x_peer_export: the IPC handle (bf16x_peer_handle_bytes()
+ * bytes, host) of the device allocation holding ptr and ptr's offset in it.
+ * bf16x_peer_import: maps another process's handle on the current device
+ * (lazy peer access) and returns the allocation's base; a handle imported
+ * twice shares one mapping.  bf16x_peer_close: releases one import. */
+int64_t bf16x_peer_handle_bytes(void);
+int bf16x_peer_export(const void *ptr, void *handle, int64_t *offset);
+int bf16x_peer_import(const void *handle, void **base);
+int bf16x_peer_close(void *base);
+
 /* ---- fused decode + GEMM (tcgen05, prefill) ----------------------------- */
 /* Replaces bf16x_fused_gemm / _bf16x_gemm_fused_kernel
  * (bf16x_gemm_fused.py:31-114): y[m][n] = sum_k x[m][k] * W[n][k] (+ bias[n])
