@@ -47,7 +47,13 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong",
+                    help="N>1: strong = the four weights row-sharded over the GPUs (tensor parallel, y "
+                         "all-gathered); weak = every GPU an independent replica of the whole workload")
+    ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
+                    help="tensor parallel all-gather: inside the GEMV (peer stores over NVLink) or NCCL")
+    ap.add_argument("--no-nccl-compare", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill and decode sub-records")
     ap.add_argument("--shapes", default="", help="e.g. 4096x4096,128256x4096 (default: all four)")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -164,23 +170,34 @@ def stored_weight_bytes(p, rows, in_f):
     exact decode: 384 B per 256-column chunk of each row; one record per
     (16-row tile, chunk) of 32 emax words, 2 header words and one word per
     weight whose exponent is more than 15 below the largest of its row-local
-    32-column group, padded to 4 words; tiles x chunks + 1 record offsets."""
+    32-column group, padded to 4 words; tiles x chunks + 1 record offsets.
+    Decoded 4096 rows at a time, so large weights stay within host memory."""
     import numpy as np
     from oracle import oracle
     nch = (in_f + 255) // 256
     n_tiles = (rows + 15) // 16
-    e = np.zeros((n_tiles * 16, nch * 256), dtype=np.int16)
-    e[:rows, :in_f] = ((oracle.decode(p).reshape(rows, in_f) >> 7) & 0xFF).astype(np.int16)
-    valid = np.zeros_like(e, dtype=bool)
-    valid[:rows, :in_f] = True
-    g = e.reshape(n_tiles * 16, nch * 8, 32)
-    patch = ((g.max(axis=2, keepdims=True) - g) > 15) & valid.reshape(g.shape)
-    counts = patch.reshape(n_tiles, 16, nch, 256).sum(axis=(1, 3))
-    rec_words = int(((34 + counts + 3) // 4 * 4).sum())
+    rec_words = 0
+    step = 4096
+    for r0 in range(0, rows, step):
+        r1 = min(rows, r0 + step)
+        nt = (r1 - r0 + 15) // 16
+        e = np.zeros((nt * 16, nch * 256), dtype=np.int16)
+        e[:r1 - r0, :in_f] = ((oracle.decode(p, r0, r1).reshape(r1 - r0, in_f) >> 7) & 0xFF).astype(np.int16)
+        valid = np.zeros_like(e, dtype=bool)
+        valid[:r1 - r0, :in_f] = True
+        g = e.reshape(nt * 16, nch * 8, 32)
+        patch = ((g.max(axis=2, keepdims=True) - g) > 15) & valid.reshape(g.shape)
+        counts = patch.reshape(nt, 16, nch, 256).sum(axis=(1, 3))
+        rec_words += int(((34 + counts + 3) // 4 * 4).sum())
     return rows * nch * 384 + 4 * rec_words + 4 * (n_tiles * nch + 1)
 
 
 def run_reference(args):
+    """The reference's CPU decode+matmul path (BF16XLinear.forward,
+    opqk_linear.py:390-404, restated in the C oracle: per-1024-row-tile decode
+    with the overflow searchsorted, fp32 matmul) on this arm's workload: the
+    same four weights (drawn with the same seeds, packed by the reference's
+    quantize restated), the same activations, all host threads."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -191,28 +208,46 @@ def run_reference(args):
     from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
     from oracle import oracle
 
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    oracle.set_num_threads(cores)          # a launcher's OMP_NUM_THREADS=1 must not apply here
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    gen_dev = "cuda" if torch.cuda.is_available() else "cpu"
     shapes = shapes_of(args)
-    w = synthetic_weight(4096, 4096, seed=0)
-    bits = w.view(torch.int16).numpy().view(np.uint16)
-    p = oracle.quantize(bits, 4096, 4096)
-    x = synthetic_activation(args.batch, 4096, seed=1).float().numpy()
-    nbytes = workload_bytes(stored_weight_bytes(p, 4096, 4096), 4096, 4096, args.batch)
+    B = args.batch
+    layers = []
+    nbytes = 0
+    for si, (out_f, in_f) in enumerate(shapes):
+        # the same inputs as the device arm at one GPU (seeds 1000*si and si+1)
+        w = synthetic_weight(out_f, in_f, seed=1000 * si, device=gen_dev).cpu()
+        bits = w.view(torch.int16).numpy().view(np.uint16)
+        del w
+        p = oracle.quantize(bits, out_f, in_f)
+        nbytes += workload_bytes(stored_weight_bytes(p, out_f, in_f), out_f, in_f, B)
+        del bits
+        x = synthetic_activation(B, in_f, seed=si + 1, device=gen_dev).float().cpu().numpy()
+        layers.append((p, x))
+
+    def step():
+        for p, x in layers:
+            oracle.linear(p, x)
     for _ in range(warmup):
-        oracle.linear(p, x)
+        step()
     t0 = time.perf_counter()
     for _ in range(steps):
-        oracle.linear(p, x)
+        step()
     el = time.perf_counter() - t0
     v = nbytes * steps / el / 1e9
-    sample = ("one 4096x4096 BF16X weight (same synthetic distribution) per step: CPU oracle port of "
-              "BF16XLinear.forward (opqk_linear.py:390-404), tile decode + fp32 matmul, batch %d" % args.batch)
+    sample = (f"the whole workload every step ({', '.join(f'{o}x{i}' for o, i in shapes)}, batch {B}): "
+              f"CPU restatement of BF16XLinear.forward (opqk_linear.py:390-404) in C, OpenMP over {cores} "
+              f"threads; GB/s counts the same bytes as the device arm (stored weight + x + y)")
     line = {
         "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "impl": "reference",
-        "n_gpus": args.gpus, "steps": steps, "warmup": warmup, "ms_per_step": round(el / steps * 1e3, 3),
-        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": round(el / steps * 1e3, 3),
+        "higher_is_better": True, "scaling": args.scaling if world > 1 else "strong", "vs_baseline": None,
+        "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.02) weights with 0.5% x 2^U{4..8} outliers, bf16 N(0,1) activations)",
-        "config": {"workload": workload_name(args, shapes), "batch": args.batch},
-        "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": oracle.num_threads(), "kind": "port",
+        "config": bench_config(args, shapes, world),
+        "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -273,6 +308,125 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _l2_flusher(dev):
+    """A kernel that writes 256 MB (twice the 126 MB L2) on the current stream."""
+    import torch
+    buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def flush():
+        buf.fill_(1)
+    return flush
+
+
+def prefill_record(layers, dev, steps, warmup, with_cublas):
+    """Fused decode+GEMM over the same resident weights at M = 512 and 2048
+    tokens: TFLOP/s per step, the dominant launch's fraction of the measured
+    bf16 burst peak, cuBLAS bf16 on the uncompressed weights beside it."""
+    import torch
+    import torch.nn.functional as F
+
+    from bfloat16x_b200.synthetic import synthetic_activation
+    peak_tf, peak_kind = peak_tf_burst()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    out = {}
+    for M in (512, 2048):
+        xs = [synthetic_activation(M, L["in_f"], seed=31 + i, device=dev) for i, L in enumerate(layers)]
+        ys = [torch.empty((M, L["rows"]), dtype=torch.bfloat16, device=dev) for L in layers]
+
+        def step():
+            for L, x, y in zip(layers, xs, ys):
+                L["rw"].gemm(x, out=y)
+        for _ in range(max(warmup, 3)):
+            step()
+        torch.cuda.synchronize(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in layers]
+        per = [0.0] * len(layers)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            for i, (L, x, y) in enumerate(zip(layers, xs, ys)):
+                ev[i][0].record()
+                L["rw"].gemm(x, out=y)
+                ev[i][1].record()
+        b.record()
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / steps
+        for i in range(len(layers)):
+            per[i] = ev[i][0].elapsed_time(ev[i][1])
+        flops = sum(2.0 * M * L["rows"] * L["in_f"] for L in layers)
+        dom = max(range(len(layers)), key=lambda i: per[i])
+        Ld = layers[dom]
+        ach = 2.0 * M * Ld["rows"] * Ld["in_f"] / (per[dom] / 1e3) / 1e12
+        rec = {"tokens": M, "TFLOPS": round(flops / (ms / 1e3) / 1e12, 1), "ms_per_step": round(ms, 4),
+               "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per[i], 4) for i, L in enumerate(layers)},
+               "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                            "frac": round(ach / peak_tf, 4), "peak_source": peak_kind + " (burst)",
+                            "kernel": f"{gemm_kernel_name(Ld['rows'], Ld['in_f'], M, sms)} {Ld['rows']}x{Ld['in_f']}"}}
+        if with_cublas:
+            for L, x in zip(layers, xs):
+                F.linear(x, L["w"])
+            torch.cuda.synchronize(dev)
+            a.record()
+            for _ in range(steps):
+                for L, x in zip(layers, xs):
+                    F.linear(x, L["w"])
+            b.record()
+            torch.cuda.synchronize(dev)
+            c_ms = a.elapsed_time(b) / steps
+            rec["cublas_bf16"] = {"ms_per_step": round(c_ms, 4), "TFLOPS": round(flops / (c_ms / 1e3) / 1e12, 1),
+                                  "ratio_vs_cublas": round(c_ms / ms, 3)}
+        out[f"M{M}"] = rec
+        del xs, ys
+    return out
+
+
+def decode_record(dev, reps=20):
+    """Stand-alone flat decode + overflow fix (bf16x_decode_triton) on 2048x1536
+    and 4096x4096: bytes = 1.4375 B/weight of streams + 5 B per overflow entry
+    in + 2 B/weight out, each launch timed alone after an L2 flush."""
+    import torch
+
+    from bfloat16x_b200.bf16x_decode import bf16x_decode_triton
+    from bfloat16x_b200.opqk_linear import bf16x_quantize
+    from bfloat16x_b200.synthetic import synthetic_weight
+    peak, kind = peak_hbm()
+    flush = _l2_flusher(dev)
+    out = {}
+    for (o, i) in ((2048, 1536), (4096, 4096)):
+        w = synthetic_weight(o, i, seed=0, device=dev)
+        p = bf16x_quantize(w, device=dev)
+        args = (p["sign_packed"], p["mant_packed"], p["delta_packed"], p["emax"], o, i,
+                p["delta_ovf_idx"], p["delta_ovf_val"])
+        y = bf16x_decode_triton(*args)
+        assert torch.equal(y.view(torch.int16), w.view(torch.int16)), "decode not bit-exact"
+        nbytes = (4 * (p["sign_packed"].numel() + p["mant_packed"].numel() + p["delta_packed"].numel())
+                  + p["emax"].numel() + 5 * p["delta_ovf_idx"].numel() + 2 * o * i)
+        times = []
+        for _ in range(reps):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            bf16x_decode_triton(*args, out=y)
+            b.record()
+            torch.cuda.synchronize(dev)
+            times.append(a.elapsed_time(b))
+        t = statistics.median(times)
+        out[f"{o}x{i}"] = {"us": round(t * 1e3, 2), "GB/s": round(nbytes / (t / 1e3) / 1e9, 1),
+                           "frac": round(nbytes / (t / 1e3) / 1e9 / peak, 4), "bytes": int(nbytes),
+                           "overflow_entries": int(p["delta_ovf_idx"].numel())}
+    out["note"] = ("median of %d launches, each after a 256 MB L2 flush; fraction of the %s HBM copy "
+                   "bandwidth (%.1f GB/s)" % (reps, kind, peak))
+    return out
+
+
+def peak_tf_burst():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -287,31 +441,59 @@ def run_ours(args):
 
     from bfloat16x_b200 import _lib
     from bfloat16x_b200.opqk_linear import bf16x_quantize
-    from bfloat16x_b200.resident import ResidentWeight
     from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
+    from bfloat16x_b200.tp import shard_bounds
 
     B = args.batch
     shapes = shapes_of(args)
+    tp = world > 1 and args.scaling == "strong"
+    peers = None
+    if tp and args.collective == "peer":
+        from bfloat16x_b200.peer import PeerGroup
+        heap = sum(2 * (B * o * 4 + 256) for o, _ in shapes) + (1 << 20)
+        peers = PeerGroup(None, dev, heap_bytes=heap)
     layers = []
     for si, (out_f, in_f) in enumerate(shapes):
-        if args.scaling == "weak":
-            rows = out_f
+        if args.scaling == "weak" or world == 1:
+            r0, r1 = 0, out_f
+            w = synthetic_weight(out_f, in_f, seed=1000 * si + rank, device=dev)
         else:
-            base = out_f // world
-            rows = base + (out_f % world if rank == world - 1 else 0)
-        w = synthetic_weight(rows, in_f, seed=1000 * si + rank, device=dev)
+            # every rank draws the whole weight and packs its row shard, so the
+            # N-GPU job computes exactly the 1-GPU job's outputs
+            r0, r1 = shard_bounds(out_f, world, rank, 16)
+            w = synthetic_weight(out_f, in_f, seed=1000 * si, device=dev)[r0:r1].contiguous()
+        rows = r1 - r0
         rw = make_resident(w, args.format, dev)
         wb = None if args.no_cublas else w
         del w
         x = synthetic_activation(B, in_f, seed=si + 1, device=dev)
-        y = torch.empty((B, rows), dtype=torch.bfloat16, device=dev)
-        layers.append(dict(rw=rw, x=x, y=y, w=wb, rows=rows, in_f=in_f,
-                           nbytes=workload_bytes(rw.nbytes(), rows, in_f, B)))
+        L = dict(rw=rw, x=x, w=wb, rows=rows, r0=r0, out_f=out_f, in_f=in_f,
+                 nbytes=workload_bytes(rw.nbytes(), rows, in_f, B))
+        if peers is not None:
+            L["yoff"] = peers.alloc(B * out_f * 2)
+            L["y"] = peers.local(L["yoff"], (B, out_f), torch.bfloat16)
+        elif tp:
+            rmax = max(h - l for l, h in (shard_bounds(out_f, world, q, 16) for q in range(world)))
+            L["y"] = torch.empty((B, rmax), dtype=torch.bfloat16, device=dev)
+            L["yall"] = torch.empty((world * B, rmax), dtype=torch.bfloat16, device=dev)
+        else:
+            L["y"] = torch.empty((B, rows), dtype=torch.bfloat16, device=dev)
+        layers.append(L)
     torch.cuda.synchronize()
+
+    def run_layer(L, x=None):
+        x = L["x"] if x is None else x
+        if peers is not None:
+            L["rw"].gemv_peers(x, peers, L["yoff"], L["out_f"], L["r0"])
+        elif tp:
+            L["rw"].gemv(x, out=L["y"][:, :L["rows"]])
+            dist.all_gather_into_tensor(L["yall"], L["y"])
+        else:
+            L["rw"].gemv(x, out=L["y"])
 
     def step():
         for L in layers:
-            L["rw"].gemv(L["x"], out=L["y"])
+            run_layer(L)
 
     def barrier():
         if world > 1:
@@ -333,8 +515,9 @@ def run_ours(args):
         return float(t.item())
 
     # ---------------- device-resident timing (value) --------------------------
-    # One step (the four launches) is captured once in a CUDA graph and
-    # replayed: what is timed is device work, not Python launch overhead.
+    # One step (the four launches, with their all-gathers under tensor
+    # parallelism) is captured once in a CUDA graph and replayed: what is
+    # timed is device work, not Python launch overhead.
     for _ in range(max(args.warmup, 3)):
         step()
     barrier()
@@ -343,6 +526,7 @@ def run_ours(args):
     with torch.cuda.stream(gstream):
         step()                                   # per-stream scratch for the capture stream
         torch.cuda.synchronize(dev)
+        barrier()
         g_step = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_step, stream=gstream):
             step()
@@ -350,7 +534,7 @@ def run_ours(args):
         for L in layers:
             gl = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gl, stream=gstream):
-                L["rw"].gemv(L["x"], out=L["y"])
+                run_layer(L)
             g_layer.append(gl)
     torch.cuda.synchronize(dev)
     for _ in range(max(args.warmup, 3)):
@@ -371,18 +555,55 @@ def run_ours(args):
     per_layer_ms = []
     for gl in g_layer:
         gl.replay()
+        barrier()
         a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a_ev.record()
         for _ in range(args.steps):
             gl.replay()
         b_ev.record()
         torch.cuda.synchronize(dev)
-        per_layer_ms.append(a_ev.elapsed_time(b_ev) / args.steps)
+        per_layer_ms.append(max_over_ranks(a_ev.elapsed_time(b_ev) / args.steps))
     el_max = max_over_ranks(el_ms)
     step_bytes = sum(L["nbytes"] for L in layers)
     total_bytes = sum_over_ranks(step_bytes * args.steps)
     value = total_bytes / (el_max / 1e3) / 1e9
     _lib.check_device_status(local)
+
+    # the in-kernel all-gather against GEMV + NCCL all-gather on the same shards
+    nccl_cmp = None
+    if peers is not None and not args.no_nccl_compare:
+        ys, yall = [], []
+        for L in layers:
+            rmax = max(h - l for l, h in (shard_bounds(L["out_f"], world, q, 16) for q in range(world)))
+            ys.append(torch.empty((B, rmax), dtype=torch.bfloat16, device=dev))
+            yall.append(torch.empty((world * B, rmax), dtype=torch.bfloat16, device=dev))
+
+        def nccl_step():
+            for L, y, ya in zip(layers, ys, yall):
+                L["rw"].gemv(L["x"], out=y[:, :L["rows"]])
+                dist.all_gather_into_tensor(ya, y)
+        with torch.cuda.stream(gstream):
+            nccl_step()
+            torch.cuda.synchronize(dev)
+            barrier()
+            g_n = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_n, stream=gstream):
+                nccl_step()
+        for _ in range(3):
+            g_n.replay()
+        barrier()
+        a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_ev.record()
+        for _ in range(args.steps):
+            g_n.replay()
+        b_ev.record()
+        barrier()
+        n_ms = max_over_ranks(a_ev.elapsed_time(b_ev)) / args.steps
+        nccl_cmp = {"ms_per_step": round(n_ms, 4), "GB/s": round(total_bytes / args.steps / (n_ms / 1e3) / 1e9, 1),
+                    "speedup_of_fused": round(n_ms / (el_max / args.steps), 3),
+                    "note": "the same row-shard GEMVs writing local rows, each followed by NCCL "
+                            "all_gather_into_tensor, CUDA graph"}
+        del g_n
 
     # dominant kernel: the launch with the largest share of device time
     dom = max(range(len(layers)), key=lambda i: per_layer_ms[i])
@@ -395,14 +616,15 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         hx = [L["x"].cpu().pin_memory() for L in layers]
-        hy = [torch.empty((B, L["rows"]), dtype=torch.bfloat16).pin_memory() for L in layers]
+        yout = [L["yall"] if "yall" in L else L["y"] for L in layers]     # the full y of each layer
+        hy = [torch.empty(tuple(y.shape), dtype=torch.bfloat16).pin_memory() for y in yout]
         dx = [torch.empty_like(L["x"]) for L in layers]
 
         def e2e_step():
             for i, L in enumerate(layers):
                 dx[i].copy_(hx[i], non_blocking=True)
-                L["rw"].gemv(dx[i], out=L["y"])
-                hy[i].copy_(L["y"], non_blocking=True)
+                run_layer(L, dx[i])
+                hy[i].copy_(yout[i], non_blocking=True)
 
         for _ in range(max(args.warmup, 3)):
             e2e_step()
@@ -417,7 +639,9 @@ def run_ours(args):
         e2e = {"value": round(total_bytes / (e_max / 1e3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": sum(t.numel() * 2 for t in hx) * world,
                "d2h_bytes_per_step": sum(t.numel() * 2 for t in hy) * world,
-               "path": "ResidentWeight.gemv (module forward path): pinned x -> H2D, fused kernel, D2H y",
+               "path": ("ResidentWeight.gemv_peers (row shards, in-kernel all-gather)" if peers is not None else
+                        "ResidentWeight.gemv (module forward path)") +
+                       ": pinned x -> H2D, fused kernel, D2H y, every rank",
                "ms_per_step": round(e_max / args.steps, 4)}
 
     # ---------------- cuBLAS bf16 GEMV on the same shapes ----------------------
@@ -444,7 +668,13 @@ def run_ours(args):
         c_ms = max_over_ranks(a.elapsed_time(b)) / args.steps
         cublas = {"ms_per_step": round(c_ms, 4), "speedup_vs_cublas_bf16": round(c_ms / (el_max / args.steps), 3),
                   "bf16_bytes_per_step": sum(L["rows"] * L["in_f"] * 2 for L in layers),
-                  "note": "torch F.linear (cuBLAS) on the uncompressed bf16 weights, same shapes, CUDA graph"}
+                  "note": "torch F.linear (cuBLAS) on the uncompressed bf16 weights (this rank's rows, no "
+                          "all-gather), same shapes, CUDA graph"}
+
+    prefill = decode = None
+    if world == 1 and not args.no_prefill:
+        prefill = prefill_record(layers, dev, min(args.steps, 10), args.warmup, not args.no_cublas)
+        decode = decode_record(dev)
 
     # ---------------- CPU baseline (rank 0, N=1) ---------------------------------
     cpu = None
@@ -459,31 +689,46 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
+            "scaling": args.scaling if world > 1 else "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights with 0.5% x 2^U{4..8} outliers, bf16 N(0,1) activations)",
-            "config": {"workload": workload_name(args, shapes), "batch": B, "format": args.format,
-                       "parallelism": f"row-shard x{world} ({args.scaling})",
-                       "l2": "inputs larger than L2 (%.0f MB of weights per step per GPU)" % (step_bytes / 1e6),
-                       "resident_bpw": round(8 * sum(L['rw'].nbytes() for L in layers) /
-                                             sum(L['rows'] * L['in_f'] for L in layers), 3)},
+            "config": bench_config(args, shapes, world),
+            "resident_bpw": round(8 * sum(L['rw'].nbytes() for L in layers) /
+                                  sum(L['rows'] * L['in_f'] for L in layers), 3),
             "frac_of_8TBs": round(value / world / 8000.0, 4),
             "tok_s": round(B / (ms_step / 1e3), 1),
             "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per_layer_ms[i], 4) for i, L in enumerate(layers)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "kernel": f"gemv_kernel (fused decode+GEMV) {Ld['rows']}x{Ld['in_f']} batch {B}",
-                         "traffic": traffic_from_profile(kernel_key)},
+                         "traffic": traffic_from_profile(kernel_key) if world == 1 else None},
             "gpu_launches": args.steps * len(layers),
             "timing": "CUDA-graph replay of the step; per_shape_ms from the same launch replayed back to back",
             "clocks": clocks,
             "e2e": e2e,
             "cublas_bf16": cublas,
+            "allgather_nccl": nccl_cmp,
+            "prefill": prefill,
+            "decode": decode,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        del g_step, g_layer
+        barrier()
+        if peers is not None:
+            peers.close()
         dist.barrier()
         dist.destroy_process_group()
+
+
+def bench_config(args, shapes, world):
+    """The workload description, identical in both arms."""
+    tp = world > 1 and args.scaling == "strong"
+    par = (f"row-sharded tensor parallel x{world}, all-gather of y "
+           + ("inside the GEMV kernel (NVLink peer stores)" if args.collective == "peer" else "by NCCL")
+           if tp else f"row-shard x{world} (weak: independent replicas)" if world > 1 else "1 GPU")
+    return {"workload": workload_name(args, shapes), "batch": args.batch, "format": args.format,
+            "parallelism": par, "l2": "inputs larger than L2 (~1 GB of compressed weights per step)"}
 
 
 def run_gemm(args):

@@ -92,13 +92,33 @@ def _linear_from(w: torch.Tensor) -> nn.Linear:
 
 class ColumnShard(nn.Module):
     """The input-column slice of a linear: this rank's partial outputs,
-    summed over the group (fp32 all-reduce)."""
+    summed over the group.  By default an fp32 NCCL all-reduce; once packed
+    and given a PeerGroup (``use_peer_collectives``), up to 16 tokens take the
+    fused decode+GEMV that stores the fp32 partials into this rank's slot of
+    every rank's slot array over NVLink, and the slots are summed in rank
+    order (the same sum on every rank)."""
 
     def __init__(self, lin: nn.Module, group=None, tp: int = 1):
         super().__init__()
         self.lin, self.group, self.tp = lin, group, tp
+        self.peers = None
+
+    def attach_peers(self, peers, max_batch: int) -> None:
+        self.peers = peers
+        self.max_batch = max_batch
+        self.out_f = self.lin.out_features
+        self._slot = max_batch * self.out_f * 4
+        self._soff = peers.alloc(peers.world * self._slot)
 
     def forward(self, x):
+        if self.peers is not None and x.numel() // x.shape[-1] <= self.max_batch:
+            x2 = x.reshape(-1, x.shape[-1])
+            B = x2.shape[0]
+            pg = self.peers
+            self.lin.rw.gemv_peers(x2, pg, self._soff + pg.rank * self._slot, self.out_f, 0,
+                                   out_dtype=torch.float32)
+            slots = pg.local(self._soff, (pg.world, self.max_batch, self.out_f), torch.float32)[:, :B]
+            return slots.sum(0).to(x.dtype).reshape(*x.shape[:-1], self.out_f)
         y = self.lin(x)
         if self.tp == 1:
             return y
@@ -114,8 +134,22 @@ class VocabShard(nn.Module):
     def __init__(self, lin: nn.Module, vocab: int, piece: int, group=None, tp: int = 1):
         super().__init__()
         self.lin, self.vocab, self.piece, self.group, self.tp = lin, vocab, piece, group, tp
+        self.peers = None
+
+    def attach_peers(self, peers, max_batch: int) -> None:
+        """Logits gathered inside the fused GEMV (every rank's vocab rows
+        stored into every rank's logits buffer over NVLink)."""
+        self.peers = peers
+        self.max_batch = max_batch
+        self._off = peers.alloc(max_batch * self.vocab * 2)
 
     def forward(self, x):
+        if self.peers is not None and x.numel() // x.shape[-1] <= self.max_batch:
+            x2 = x.reshape(-1, x.shape[-1])
+            pg = self.peers
+            self.lin.rw.gemv_peers(x2, pg, self._off, self.vocab, pg.rank * self.piece)
+            y = pg.local(self._off, (self.max_batch, self.vocab), torch.bfloat16)[:x2.shape[0]]
+            return y.reshape(*x.shape[:-1], self.vocab)
         y = self.lin(x)
         if self.tp == 1:
             return y
@@ -283,6 +317,27 @@ def pack_model(model: LlamaModel) -> tuple[int, int]:
     return total, n
 
 
+def use_peer_collectives(model: LlamaModel, peers) -> None:
+    """After ``pack_model``: the o_proj / down_proj all-reduces and the
+    lm_head all-gather of decode steps (up to 16 tokens per step) run inside
+    the fused GEMVs over NVLink peer memory (``peers``: a PeerGroup over the
+    model's tensor-parallel group, heap of ``peer_heap_bytes(model)``)."""
+    if model.tp == 1:
+        return
+    for m in model.modules():
+        if isinstance(m, (ColumnShard, VocabShard)):
+            if not isinstance(m.lin, ResidentLinear):
+                raise ValueError("use_peer_collectives needs a packed model (pack_model first)")
+            m.attach_peers(peers, max(model.batch, 1))
+
+
+def peer_heap_bytes(model: LlamaModel) -> int:
+    """PeerGroup heap that use_peer_collectives carves for ``model``."""
+    cfg, B, tp = model.cfg, max(model.batch, 1), model.tp
+    per_layer = 2 * (tp * B * cfg.hidden * 4 + 256)
+    return cfg.layers * per_layer + B * cfg.vocab * 2 + (1 << 20)
+
+
 class GraphDecoder:
     """One decode step (a token in, the greedy next token out) captured as a
     CUDA graph and replayed; the position lives in a device tensor."""
@@ -353,4 +408,4 @@ def generate(model: LlamaModel, prompt: torch.Tensor, new_tokens: int, use_graph
 
 
 __all__ = ["LlamaConfig", "CONFIGS", "LlamaModel", "ColumnShard", "VocabShard", "ResidentLinear", "pack_model",
-           "GraphDecoder", "generate"]
+           "GraphDecoder", "generate", "use_peer_collectives", "peer_heap_bytes"]

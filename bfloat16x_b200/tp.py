@@ -100,10 +100,17 @@ class ColumnParallel(nn.Module):
 
 
 class RowParallelBf16x(RowParallel):
-    """Rows [r0, r1) of a BF16X dict resident on this rank's GPU."""
+    """Rows [r0, r1) of a BF16X dict resident on this rank's GPU.
+
+    With ``peers`` (a PeerGroup over the same ranks), up to 16 rows of
+    activations take the fused decode+GEMV whose epilogue stores each rank's
+    output rows into every rank's output buffer over NVLink
+    (``ResidentWeight.gemv_peers``): no separate all-gather.  The result is
+    then a view of this rank's copy of that buffer, valid until the layer's
+    next call; more rows take the GEMM and NCCL."""
 
     def __init__(self, packed: dict, bias: torch.Tensor | None = None, group=None, gather: bool = True,
-                 device=None):
+                 device=None, peers=None, max_batch: int = 16):
         from .resident import ResidentWeight
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
@@ -122,14 +129,43 @@ class RowParallelBf16x(RowParallel):
         super().__init__(local, out_f, group, gather, 16)
         self.resident = self_rw
         self.rows = (r0, r1)
+        self.peers = peers if (gather and world > 1) else None
+        self._bias = b
+        if self.peers is not None:
+            if any(h <= l for l, h in self.bounds):
+                raise ValueError("the in-kernel all-gather needs rows on every rank (out_f >= 16 * world)")
+            self.max_batch = int(max_batch)
+            # two buffers used alternately: a call never rewrites the rows the
+            # previous call of this layer returned while a peer may read them
+            self._yoff = [peers.alloc(self.max_batch * out_f * 4) for _ in range(2)]
+            self._turn = 0
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.peers is None:
+            return super().forward(x)
+        x2 = x.reshape(-1, x.shape[-1])
+        B = x2.shape[0]
+        if B > self.max_batch:
+            return super().forward(x)
+        od = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.bfloat16
+        off = self._yoff[self._turn]
+        self._turn ^= 1
+        self.resident.gemv_peers(x2, self.peers, off, self.out_f, self.rows[0], bias=self._bias, out_dtype=od)
+        return self.peers.local(off, (B, self.out_f), od).reshape(*x.shape[:-1], self.out_f)
 
 
 class ColumnParallelBf16x(ColumnParallel):
     """Columns [c0, c1) of a bf16 weight, BF16X-packed on this rank's GPU.
-    The bias, if any, is added once after the reduction."""
+    The bias, if any, is added once after the reduction.
+
+    With ``peers``, up to 16 rows of activations take the fused decode+GEMV
+    whose epilogue stores this rank's fp32 partial outputs into its slot of
+    every rank's slot array over NVLink; the kernel completes once all
+    partials are in, and the sum over the slots (rank order, the same on
+    every rank) replaces the NCCL all-reduce."""
 
     def __init__(self, weight: torch.Tensor, bias: torch.Tensor | None = None, group=None,
-                 input_is_sharded: bool = False, device=None):
+                 input_is_sharded: bool = False, device=None, peers=None, max_batch: int = 16):
         from .opqk_linear import bf16x_quantize
         from .resident import ResidentWeight
         world = dist.get_world_size(group)
@@ -146,9 +182,30 @@ class ColumnParallelBf16x(ColumnParallel):
         super().__init__(local, in_f, group, input_is_sharded, 256)
         self.resident = rw
         self.bias = None if bias is None else bias.detach().to(dev, torch.bfloat16)
+        self.peers = peers if world > 1 else None
+        if self.peers is not None:
+            self.max_batch = int(max_batch)
+            self.out_f = int(weight.shape[0])
+            self._slot = self.max_batch * self.out_f * 4
+            self._soff = [peers.alloc(world * self._slot) for _ in range(2)]
+            self._turn = 0
+
+    def _peer_sum(self, x: torch.Tensor) -> torch.Tensor:
+        xs = x if self.input_is_sharded else x[..., self.c0:self.c1]
+        x2 = xs.reshape(-1, xs.shape[-1]).contiguous()
+        B = x2.shape[0]
+        off = self._soff[self._turn]
+        self._turn ^= 1
+        self.resident.gemv_peers(x2, self.peers, off + self.rank * self._slot, self.out_f, 0,
+                                 out_dtype=torch.float32)
+        slots = self.peers.local(off, (self.world, self.max_batch, self.out_f), torch.float32)[:, :B]
+        return slots.sum(0).reshape(*x.shape[:-1], self.out_f)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        y = super().forward(x)
+        if self.peers is not None and x.numel() // x.shape[-1] <= self.max_batch:
+            y = self._peer_sum(x)
+        else:
+            y = super().forward(x)
         if self.bias is not None:
             y = y + self.bias.float()
         return y.to(x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.bfloat16)

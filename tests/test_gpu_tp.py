@@ -108,3 +108,105 @@ def test_tp_decoder_packed_nccl():
         p.join(timeout=60)
     for r in res:
         assert r[1], r
+
+
+def _peer_worker(rank, world, port, q):
+    try:
+        import torch.distributed as dist
+
+        from bfloat16x_b200 import _lib
+        from bfloat16x_b200.peer import PeerGroup
+        from bfloat16x_b200.resident import ResidentWeight
+        from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
+        from bfloat16x_b200.tp import shard_bounds
+        from tests.gpu_util import bits_of, oracle_dict, rel_l2
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        pg = PeerGroup(None, dev, heap_bytes=8 << 20)
+        res = []
+        for (out_f, in_f), B, dt in [((1000, 2048), 1, torch.float32), ((4096, 4096), 8, torch.bfloat16),
+                                     ((300, 1536), 3, torch.float32)]:
+            w = synthetic_weight(out_f, in_f, seed=out_f)
+            wb = bits_of(w)
+            r0, r1 = shard_bounds(out_f, world, rank, 16)
+            rw = ResidentWeight.from_packed(oracle_dict(wb), device=dev, row_range=(r0, r1))
+            off = [pg.alloc(B * out_f * 4), pg.alloc(B * out_f * 4)]      # two buffers, used alternately
+            ref = (x_ := synthetic_activation(B, in_f, seed=B)).float() @ w.float().T
+            for it in range(4):
+                buf = off[it % 2]
+                yv = pg.local(buf, (B, out_f), dt)
+                yv.fill_(float("nan"))
+                dist.barrier()
+                rw.gemv_peers(x_.to(dev), pg, buf, out_f, r0, out_dtype=dt)
+                torch.cuda.synchronize()
+                ref_c = ref if dt == torch.float32 else ref.to(torch.bfloat16).float()
+                got = yv.float().cpu()
+                res.append(bool(torch.isfinite(got).all()) and rel_l2(got.numpy(), ref_c.numpy()) < 1e-3)
+                dist.barrier()
+            _lib.check_device_status(rank)
+        # the same launches captured in a CUDA graph and replayed: the epoch
+        # lives in device memory, so replays keep the ranks in step
+        out_f, in_f, B = 2048, 1024, 2
+        w = synthetic_weight(out_f, in_f, seed=77)
+        r0, r1 = shard_bounds(out_f, world, rank, 16)
+        rw = ResidentWeight.from_packed(oracle_dict(bits_of(w)), device=dev, row_range=(r0, r1))
+        x = synthetic_activation(B, in_f, seed=5).to(dev)
+        bufs = [pg.alloc(B * out_f * 2) for _ in range(2)]
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for bo in bufs:
+                rw.gemv_peers(x, pg, bo, out_f, r0)
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for bo in bufs:
+                    rw.gemv_peers(x, pg, bo, out_f, r0)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        ref = (x.float().cpu() @ w.float().T).to(torch.bfloat16).float()
+        for _ in range(5):
+            for bo in bufs:
+                pg.local(bo, (B, out_f), torch.bfloat16).zero_()
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            g.replay()
+            torch.cuda.synchronize(dev)
+            for bo in bufs:
+                got = pg.local(bo, (B, out_f), torch.bfloat16).float().cpu()
+                res.append(rel_l2(got.numpy(), ref.numpy()) < 1e-3)
+            dist.barrier()
+        _lib.check_device_status(rank)
+        del g
+        pg.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, all(res), res))
+    except Exception as e:
+        import traceback
+        q.put((rank, False, traceback.format_exc()))
+
+
+# The row-sharded GEMV whose epilogue writes every rank's output rows into
+# every rank's buffer over NVLink (bf16x_gemv_peers): the full output on each
+# rank against the unsharded product, eager and replayed from a CUDA graph.
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_gemv_peers_allgather_2gpu():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29400 + os.getpid() % 1000
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert r[1], r
