@@ -852,7 +852,8 @@ def run_e2e(args):
     import torch.distributed as dist
 
     from bfloat16x_b200 import _lib
-    from bfloat16x_b200.llama_e2e import CONFIGS, LlamaModel, generate, pack_model
+    from bfloat16x_b200.llama_e2e import (CONFIGS, LlamaModel, generate, logits_rel_l2, pack_model,
+                                          teacher_forced_logits)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
@@ -867,7 +868,19 @@ def run_e2e(args):
     n_w = sum(m.weight.numel() for m in model.modules() if isinstance(m, torch.nn.Linear))
     generate(model, prompt, 4)                                   # warm-up
     ref_tok, ref_pre, ref_ms = generate(model, prompt, args.new)
+    # logits of the bf16 weights on the prompt and on 16 teacher-forced steps
+    n_tf = min(16, args.new)
+    ref_logits = teacher_forced_logits(model, prompt, ref_tok[:n_tf])
     nbytes, _ = pack_model(model)
+    got_logits = teacher_forced_logits(model, prompt, ref_tok[:n_tf])
+    tf_max, tf_mean = logits_rel_l2(got_logits, ref_logits)
+    del ref_logits, got_logits
+    peers = None
+    if world > 1 and args.collective == "peer":
+        from bfloat16x_b200.llama_e2e import peer_heap_bytes, use_peer_collectives
+        from bfloat16x_b200.peer import PeerGroup
+        peers = PeerGroup(None, dev, heap_bytes=peer_heap_bytes(model))
+        use_peer_collectives(model, peers)
     generate(model, prompt, 4)
     clock = ClockSampler(dev.index)
     clock.start()
@@ -897,12 +910,19 @@ def run_e2e(args):
             "prefill_ms": round(pre, 3), "bf16_prefill_ms": round(ref_pre, 3),
             "linear_weight_bytes": {"bf16x_resident": int(nbytes), "bf16": int(2 * n_w)},
             "tokens_equal_to_bf16_run": same,
+            "logits_rel_l2_vs_bf16": {"max": round(tf_max, 6), "mean": round(tf_mean, 6),
+                                      "steps": 1 + n_tf, "how": "prompt's last position + teacher-forced decode "
+                                                                "steps on the bf16 run's tokens"},
             "timing": "decode step as one CUDA graph replayed per token; max over ranks",
+            "collectives": ("decode: o/down_proj partial sums and lm_head logits exchanged inside the fused GEMVs "
+                            "(NVLink peer stores); prefill: NCCL") if peers is not None else "NCCL",
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if peers is not None:
+            peers.close()
         dist.destroy_process_group()
 
 

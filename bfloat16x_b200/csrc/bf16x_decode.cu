@@ -2,16 +2,37 @@
 //
 // Replaces the reference's two-kernel decode (_bf16x_decode_kernel +
 // _bf16x_fix_ovf_kernel, bf16x_triton_test.py:11-108) and its host-side
-// filter/.item() sync with one pass:
-//   * a CTA owns a tile of 8192 consecutive flat elements, one 32-element
-//     group per thread: 1 sign word, 7 mantissa words, 3 delta words and two
-//     emax bytes, all whole words because the group is 32-aligned;
-//   * two warps locate the tile's slice of the sorted overflow table with a
-//     32-ary search while the others decode;
-//   * the tile is assembled in shared memory, the slice is applied there
-//     (only at positions whose stream delta is the saturated 7, which is the
-//     reference decode's rule, opqk_linear.py:367-372), and the tile leaves
-//     with coalesced 16-byte stores.
+// filter/.item() sync with one pass.  HBM-bound: 1.4375 bytes of streams +
+// 5 bytes per overflow entry in, 2 bytes out per weight.
+//
+//   * Tiles of 8192 consecutive flat elements; each CTA (persistent, up to
+//     four per SM) owns a contiguous range of tiles, so its reads and writes
+//     walk memory in order and the overflow slice of one tile ends where the
+//     next one's begins.
+//   * A tile's streams -- 256 sign words, 1792 mantissa words, 768 delta
+//     words and 512 emax bytes, every piece 16-byte aligned because the tile
+//     is 8192-aligned -- arrive by four bulk copies (TMA engine) into one of
+//     two shared-memory stages, the next tile's copies issued while this one
+//     is decoded; a tile that is not whole (the last) or streams that are not
+//     16-byte aligned take plain loads instead.
+//   * Thread t decodes group t (32 elements: one sign word, seven mantissa
+//     words, three delta words, two emax bytes -- shared-memory strides 7 and
+//     3 words touch 32 distinct banks) with funnel shifts and writes four
+//     16-byte chunks into the shared tile, XOR-swizzled so neither these
+//     writes nor the linear read-back for the global stores conflict.
+//   * The overflow table is sorted, so a tile's entries are the run that
+//     starts where the previous tile's ended (one 32-way search per CTA finds
+//     the first): the next 512 entries are requested before the tile's
+//     streams are waited for, counted below the tile's end with the barrier
+//     that publishes the decoded tile, and patch it in shared memory, only
+//     where the stream delta is the saturated 7 (the reference decode's rule,
+//     opqk_linear.py:367-372).
+//   * The tile leaves with coalesced 16-byte stores.
+#include <algorithm>
+#include <climits>
+
+#include <cuda_runtime.h>
+
 #include "bf16x_common.cuh"
 #include "bf16x_flat.cuh"
 #include "bf16x_status.cuh"
@@ -19,100 +40,222 @@
 namespace bf16x {
 
 constexpr int kDecThreads = 256;
-constexpr int kDecTile = kDecThreads * 32;   // elements per CTA
+constexpr int kDecTile = kDecThreads * 32;               // elements per tile
+constexpr int kDecSignW = kDecTile / 32;                 // 256 words
+constexpr int kDecMantW = kDecTile * 7 / 32;             // 1792 words
+constexpr int kDecDeltaW = kDecTile * 3 / 32;            // 768 words
+constexpr int kDecEmaxB = kDecTile / 16;                 // 512 bytes
+constexpr int kDecStageB = 4 * (kDecSignW + kDecMantW + kDecDeltaW) + kDecEmaxB;   // 11776
+constexpr int kDecPrefetch = 2;                          // overflow entries per thread held ahead
+constexpr int kDecCtasPerSm = 4;
 
-__global__ void __launch_bounds__(kDecThreads)
-flat_decode_kernel(FlatStreams f, uint16_t *__restrict__ out) {
-    __shared__ __align__(16) uint32_t tile[kDecTile / 2];    // bf16 pairs
-    __shared__ int64_t slice[2];
+struct DecStage {
+    uint32_t sign[kDecSignW];
+    uint32_t mant[kDecMantW];
+    uint32_t delta[kDecDeltaW];
+    uint8_t emax[kDecEmaxB];
+};
+static_assert(sizeof(DecStage) == kDecStageB && kDecStageB % 16 == 0, "stage layout");
 
-    const int tid = threadIdx.x;
-    const int64_t t0 = (int64_t)blockIdx.x * kDecTile;
-    const int64_t t1 = min(t0 + (int64_t)kDecTile, f.n);
-    const int warp = tid >> 5;
+struct DecSmem {
+    DecStage stage[2];
+    uint4 tile[kDecTile / 8];                            // 16 KB of bf16, swizzled 16-byte chunks
+    uint64_t bar[2];
+    int64_t slice_lo;                                    // start of the first tile's overflow slice
+};
 
-    if (warp < 2 && f.n_ovf > 0) {
-        const int64_t r = warp_lower_bound(f.ovf_idx, f.n_ovf, warp == 0 ? t0 : t1);
-        if ((tid & 31) == 0) slice[warp] = r;
+// 16-byte chunk j (0..3) of group t in the swizzled tile: the eight threads of
+// a store phase (and the chunks a read phase takes) fall in eight different
+// 16-byte bank groups.
+__device__ __forceinline__ int dec_chunk(int t, int j) { return 4 * t + (j ^ ((t >> 1) & 3)); }
+
+// Element e (0..8191) of the swizzled tile, as a bf16 index.
+__device__ __forceinline__ int dec_elem(int e) {
+    const int t = e >> 5, o = e & 31;
+    return dec_chunk(t, o >> 3) * 8 + (o & 7);
+}
+
+// bf16 bits of the 32 elements of one group from its words.
+__device__ __forceinline__ void decode_group32(uint32_t sw, const uint32_t (&mw)[8], const uint32_t (&dw)[4],
+                                               uint32_t eb0, uint32_t eb1, uint32_t (&pairs)[16]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const uint32_t s = (sw >> i) & 1u;
+        const uint32_t mb = 7 * i, db = 3 * i;
+        const uint32_t m = funnel_r(mw[mb >> 5], mw[(mb >> 5) + 1], mb & 31) & 0x7Fu;
+        const uint32_t d = funnel_r(dw[db >> 5], dw[(db >> 5) + 1], db & 31) & 0x7u;
+        const uint32_t e = i < 16 ? eb0 : eb1;
+        const uint32_t b = (s << 15) | (((e - d) & 0xFFu) << 7) | m;
+        if (i & 1) pairs[i >> 1] |= b << 16; else pairs[i >> 1] = b;
     }
+}
 
-    // ---- base decode of this thread's 32-element group
-    const int64_t g = (int64_t)blockIdx.x * kDecThreads + tid;   // global group index
-    const int64_t e0 = g * 32;
-    if (e0 < f.n) {
-        uint32_t sw, mw[8], dw[4];
-        uint32_t eb0, eb1;
-        const bool full = (g + 1) * 7 <= f.n_mant && (g + 1) * 3 <= f.n_delta &&
-                          g < f.n_sign && 2 * g + 1 < f.n_emax;
-        if (full) {
-            sw = __ldg(f.sign + g);
-#pragma unroll
-            for (int i = 0; i < 7; ++i) mw[i] = __ldg(f.mant + 7 * g + i);
-#pragma unroll
-            for (int i = 0; i < 3; ++i) dw[i] = __ldg(f.delta + 3 * g + i);
-            eb0 = __ldg(f.emax + 2 * g);
-            eb1 = __ldg(f.emax + 2 * g + 1);
-        } else {
-            sw = ld_word(f.sign, f.n_sign, g);
-#pragma unroll
-            for (int i = 0; i < 7; ++i) mw[i] = ld_word(f.mant, f.n_mant, 7 * g + i);
-#pragma unroll
-            for (int i = 0; i < 3; ++i) dw[i] = ld_word(f.delta, f.n_delta, 3 * g + i);
-            eb0 = 2 * g < f.n_emax ? __ldg(f.emax + 2 * g) : 0u;
-            eb1 = 2 * g + 1 < f.n_emax ? __ldg(f.emax + 2 * g + 1) : 0u;
-        }
-        mw[7] = 0u;
-        dw[3] = 0u;
-        uint32_t pairs[16];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const uint32_t s = (sw >> i) & 1u;
-            const uint32_t mb = 7 * i, db = 3 * i;
-            const uint32_t m = funnel_r(mw[mb >> 5], mw[(mb >> 5) + 1], mb & 31) & 0x7Fu;
-            const uint32_t d = funnel_r(dw[db >> 5], dw[(db >> 5) + 1], db & 31) & 0x7u;
-            const uint32_t e = i < 16 ? eb0 : eb1;
-            const uint32_t b = (s << 15) | (((e - d) & 0xFFu) << 7) | m;
-            if (i & 1) pairs[i >> 1] |= b << 16; else pairs[i >> 1] = b;
-        }
-        uint4 *dst = reinterpret_cast<uint4 *>(tile + tid * 16);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(pairs[4 * i], pairs[4 * i + 1], pairs[4 * i + 2], pairs[4 * i + 3]);
+__global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm)
+flat_decode_kernel(FlatStreams f, uint16_t *__restrict__ out, int64_t n_tiles, int bulk_ok) {
+    extern __shared__ __align__(128) uint8_t dec_smem_raw[];
+    DecSmem &sm = *reinterpret_cast<DecSmem *>(dec_smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // this CTA's contiguous tiles [tb, te)
+    const int64_t tb = n_tiles * blockIdx.x / gridDim.x;
+    const int64_t te = n_tiles * (blockIdx.x + 1) / gridDim.x;
+    if (tb >= te) return;
+    // a tile goes through the bulk copies when it is whole and the streams are aligned
+    auto bulk_tile = [&](int64_t t) { return bulk_ok && (t + 1) * kDecTile <= f.n; };
+    auto issue = [&](int64_t t, int s) {     // one thread
+        DecStage &st = sm.stage[s];
+        mbar_arrive_expect_tx(&sm.bar[s], (uint32_t)kDecStageB);
+        bulk_g2s(st.sign, f.sign + t * kDecSignW, 4 * kDecSignW, &sm.bar[s]);
+        bulk_g2s(st.mant, f.mant + t * kDecMantW, 4 * kDecMantW, &sm.bar[s]);
+        bulk_g2s(st.delta, f.delta + t * kDecDeltaW, 4 * kDecDeltaW, &sm.bar[s]);
+        bulk_g2s(st.emax, f.emax + t * kDecEmaxB, kDecEmaxB, &sm.bar[s]);
+    };
+    if (tid == 0) {
+        mbar_init(&sm.bar[0], 1);
+        mbar_init(&sm.bar[1], 1);
     }
+    fence_mbar_init();
     __syncthreads();
+    if (tid == 0 && bulk_tile(tb)) issue(tb, 0);
 
-    // ---- overflow fix inside shared memory
+    // start of the first tile's overflow slice; every later tile's slice
+    // starts where the previous one ended
+    int64_t lo = 0;
     if (f.n_ovf > 0) {
-        const int64_t lo = slice[0], hi = slice[1];
-        uint16_t *t16 = reinterpret_cast<uint16_t *>(tile);
-        for (int64_t j = lo + tid; j < hi; j += kDecThreads) {
-            const int64_t pos = __ldg(f.ovf_idx + j);
-            if (j > 0 && (int64_t)__ldg(f.ovf_idx + j - 1) >= pos) atomicOr(&g_status, kErrOvfUnsorted);
-            if (pos < t0 || pos >= t1) { atomicOr(&g_status, kErrOvfRange); continue; }
-            const uint32_t val = __ldg(f.ovf_val + j);
+        if (warp == 0) {
+            const int64_t r = warp_lower_bound(f.ovf_idx, f.n_ovf, tb * (int64_t)kDecTile);
+            if (lane == 0) sm.slice_lo = r;
+        }
+        __syncthreads();
+        lo = sm.slice_lo;
+    }
+
+    uint32_t phases = 0u;                                 // bit s: parity of the next phase of stage s
+    uint16_t *t16 = reinterpret_cast<uint16_t *>(sm.tile);
+    for (int64_t t = tb; t < te; ++t) {
+        const int s = (int)((t - tb) & 1);
+        const int64_t t0 = t * (int64_t)kDecTile;
+        const int64_t t1 = min(t0 + (int64_t)kDecTile, f.n);
+        const bool bulk = bulk_tile(t);
+        if (t + 1 < te && tid == 0 && bulk_tile(t + 1)) issue(t + 1, s ^ 1);
+        // The next entries of the sorted overflow table, requested before the
+        // streams are awaited: those below t1 (a prefix, the table being
+        // sorted) are this tile's.
+        int32_t e_pos[kDecPrefetch], e_prev[kDecPrefetch];
+        uint32_t e_val[kDecPrefetch];
+        bool e_in[kDecPrefetch];
+#pragma unroll
+        for (int k = 0; k < kDecPrefetch; ++k) {
+            const int64_t j = lo + tid + (int64_t)k * kDecThreads;
+            const bool ok = j < f.n_ovf;
+            e_pos[k] = ok ? __ldg(f.ovf_idx + j) : INT32_MAX;
+            e_prev[k] = (ok && j > 0) ? __ldg(f.ovf_idx + j - 1) : INT32_MIN;
+            e_val[k] = ok ? __ldg(f.ovf_val + j) : 0u;
+            e_in[k] = ok && (int64_t)e_pos[k] < t1;
+        }
+
+        // ---- base decode of group tid
+        const int64_t g = t * kDecThreads + tid;
+        if (g * 32 < f.n) {
+            uint32_t sw, mw[8], dw[4], eb0, eb1;
+            if (bulk) {
+                if (!mbar_wait(&sm.bar[s], (phases >> s) & 1u, &g_status)) return;
+                const DecStage &st = sm.stage[s];
+                sw = st.sign[tid];
+#pragma unroll
+                for (int i = 0; i < 7; ++i) mw[i] = st.mant[7 * tid + i];
+#pragma unroll
+                for (int i = 0; i < 3; ++i) dw[i] = st.delta[3 * tid + i];
+                eb0 = st.emax[2 * tid];
+                eb1 = st.emax[2 * tid + 1];
+            } else {
+                sw = ld_word(f.sign, f.n_sign, g);
+#pragma unroll
+                for (int i = 0; i < 7; ++i) mw[i] = ld_word(f.mant, f.n_mant, 7 * g + i);
+#pragma unroll
+                for (int i = 0; i < 3; ++i) dw[i] = ld_word(f.delta, f.n_delta, 3 * g + i);
+                eb0 = 2 * g < f.n_emax ? __ldg(f.emax + 2 * g) : 0u;
+                eb1 = 2 * g + 1 < f.n_emax ? __ldg(f.emax + 2 * g + 1) : 0u;
+            }
+            mw[7] = 0u;
+            dw[3] = 0u;
+            uint32_t pairs[16];
+            decode_group32(sw, mw, dw, eb0, eb1, pairs);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                sm.tile[dec_chunk(tid, j)] = make_uint4(pairs[4 * j], pairs[4 * j + 1], pairs[4 * j + 2], pairs[4 * j + 3]);
+        }
+        if (bulk) phases ^= 1u << s;
+
+        // ---- overflow fix inside shared memory (the counting barriers also
+        // publish the decoded tile)
+        auto fix = [&](int64_t pos, int64_t prev, uint32_t val) {
+            if (prev >= pos) atomicOr(&g_status, kErrOvfUnsorted);
+            if (pos < t0) { atomicOr(&g_status, kErrOvfRange); return; }
             const int64_t ei = pos / 16;
-            const uint32_t e = ei < f.n_emax ? __ldg(f.emax + ei) : 0u;
-            const uint32_t cur = t16[pos - t0];
+            const uint32_t e = bulk ? (uint32_t)sm.stage[s].emax[ei - t0 / 16]
+                                    : (ei < f.n_emax ? (uint32_t)__ldg(f.emax + ei) : 0u);
+            const int idx = dec_elem((int)(pos - t0));
+            const uint32_t cur = t16[idx];
             // the reference substitutes the table delta only where the stream says 7
             if (((cur >> 7) & 0xFFu) == ((e - 7u) & 0xFFu))
-                t16[pos - t0] = (uint16_t)((cur & 0x807Fu) | (((e - val) & 0xFFu) << 7));
+                t16[idx] = (uint16_t)((cur & 0x807Fu) | (((e - val) & 0xFFu) << 7));
+        };
+        int64_t n_in = 0;
+        if (f.n_ovf > 0) {
+            int full = 1;
+#pragma unroll
+            for (int k = 0; k < kDecPrefetch; ++k) {
+                const int c = __syncthreads_count(e_in[k]);
+                n_in += c;
+                full &= c == kDecThreads;
+            }
+#pragma unroll
+            for (int k = 0; k < kDecPrefetch; ++k)
+                if (e_in[k]) fix(e_pos[k], e_prev[k], e_val[k]);
+            // a tile with more entries than were requested ahead (dense
+            // overflow): the rest, a block of entries at a time
+            for (int64_t j0 = lo + (int64_t)kDecPrefetch * kDecThreads; full; j0 += kDecThreads) {
+                const int64_t j = j0 + tid;
+                const bool ok = j < f.n_ovf;
+                const int64_t pos = ok ? (int64_t)__ldg(f.ovf_idx + j) : INT64_MAX;
+                const bool in = ok && pos < t1;
+                const int c = __syncthreads_count(in);
+                n_in += c;
+                full = c == kDecThreads;
+                if (in) fix(pos, (int64_t)__ldg(f.ovf_idx + j - 1), __ldg(f.ovf_val + j));
+            }
         }
-        // entries outside every tile (index >= N) are found by the last CTA
-        if (blockIdx.x == gridDim.x - 1 && tid == 0 && hi < f.n_ovf) atomicOr(&g_status, kErrOvfRange);
-        if (blockIdx.x == 0 && tid == 0 && f.n_ovf > 0 && __ldg(f.ovf_idx) < 0) atomicOr(&g_status, kErrOvfRange);
         __syncthreads();
-    }
 
-    // ---- coalesced store
-    const int64_t cnt = t1 - t0;
-    if (cnt == kDecTile) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(tile);
-        uint4 *dst = reinterpret_cast<uint4 *>(out + t0);
-        for (int i = tid; i < kDecTile / 8; i += kDecThreads) dst[i] = src[i];
-    } else {
-        const uint16_t *src = reinterpret_cast<const uint16_t *>(tile);
-        for (int64_t i = tid; i < cnt; i += kDecThreads) out[t0 + i] = src[i];
+        // ---- coalesced store (linear 16-byte chunks read back through the swizzle)
+        const int64_t cnt = t1 - t0;
+        if (cnt == kDecTile) {
+            uint4 *dst = reinterpret_cast<uint4 *>(out + t0);
+#pragma unroll
+            for (int i = tid; i < kDecTile / 8; i += kDecThreads) dst[i] = sm.tile[dec_chunk(i >> 2, i & 3)];
+        } else {
+            for (int64_t i = tid; i < cnt; i += kDecThreads) out[t0 + i] = t16[dec_elem((int)i)];
+        }
+        lo += n_in;
+        __syncthreads();     // the tile and this stage are free
     }
+    // entries past every tile (index >= N) or a negative first index
+    if (f.n_ovf > 0 && tid == 0) {
+        if (te == n_tiles && lo < f.n_ovf) atomicOr(&g_status, kErrOvfRange);
+        if (tb == 0 && __ldg(f.ovf_idx) < 0) atomicOr(&g_status, kErrOvfRange);
+    }
+}
+
+static int decode_grid(int64_t n_tiles) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return (int)std::min<int64_t>(n_tiles, (int64_t)sms * kDecCtasPerSm);
 }
 
 }  // namespace bf16x
@@ -141,8 +284,19 @@ extern "C" int bf16x_decode(const uint32_t *sign, int64_t n_sign_words,
         return set_error(BF16X_ERR_INVALID, "bf16x_decode: out must be 16-byte aligned");
     FlatStreams f{sign, n_sign_words, mant, n_mant_words, delta, n_delta_words,
                   emax, n_emax, ovf_idx, ovf_val, n_ovf, n};
-    const int64_t grid = (n + kDecTile - 1) / kDecTile;
-    if (grid > 0x7fffffffLL) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_decode: tensor too large");
-    flat_decode_kernel<<<(unsigned)grid, kDecThreads, 0, (cudaStream_t)stream>>>(f, out);
+    const int64_t n_tiles = (n + kDecTile - 1) / kDecTile;
+    const int bulk_ok = ((reinterpret_cast<uintptr_t>(sign) | reinterpret_cast<uintptr_t>(mant) |
+                          reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(emax)) & 15u) == 0;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(flat_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)sizeof(DecSmem));
+        if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_decode: smem attribute: %s", cudaGetErrorString(e));
+        attr_set[dev] = true;
+    }
+    flat_decode_kernel<<<(unsigned)decode_grid(n_tiles), kDecThreads, sizeof(DecSmem), (cudaStream_t)stream>>>(
+        f, out, n_tiles, bulk_ok);
     return check_launch("bf16x_decode");
 }

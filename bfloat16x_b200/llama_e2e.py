@@ -373,6 +373,27 @@ class GraphDecoder:
 
 
 @torch.no_grad()
+def teacher_forced_logits(model: LlamaModel, prompt: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
+    """Logits [1 + n, batch, vocab] (fp32) of the prompt's last position and of
+    n decode steps fed the given tokens [n, batch] (not the model's own
+    choices), so two models -- bf16 and BF16X weights -- are compared on the
+    same inputs at every step, without greedy divergence."""
+    dev = prompt.device
+    P = prompt.shape[1]
+    out = [model(prompt, torch.zeros((), dtype=torch.long, device=dev)).float()]
+    for i in range(tokens.shape[0]):
+        pos = torch.tensor(P + i, dtype=torch.long, device=dev)
+        out.append(model(tokens[i].reshape(-1, 1), pos).float())
+    return torch.stack(out)
+
+
+def logits_rel_l2(a: torch.Tensor, b: torch.Tensor) -> tuple[float, float]:
+    """(max, mean) over steps of ||a - b|| / ||b|| per step (fp64)."""
+    d = (a.double() - b.double()).flatten(1).norm(dim=1) / b.double().flatten(1).norm(dim=1)
+    return float(d.max()), float(d.mean())
+
+
+@torch.no_grad()
 def generate(model: LlamaModel, prompt: torch.Tensor, new_tokens: int, use_graph: bool = True):
     """Greedy generation: prefill ``prompt`` [batch, P], then ``new_tokens``
     decode steps.  Returns (tokens [new_tokens, batch], prefill ms, decode
@@ -408,4 +429,5 @@ def generate(model: LlamaModel, prompt: torch.Tensor, new_tokens: int, use_graph
 
 
 __all__ = ["LlamaConfig", "CONFIGS", "LlamaModel", "ColumnShard", "VocabShard", "ResidentLinear", "pack_model",
-           "GraphDecoder", "generate", "use_peer_collectives", "peer_heap_bytes"]
+           "GraphDecoder", "generate", "use_peer_collectives", "peer_heap_bytes", "teacher_forced_logits",
+           "logits_rel_l2"]

@@ -63,6 +63,41 @@ def test_decode_vs_oracle(shape):
     assert np.array_equal(got, w)
 
 
+def test_decode_dense_overflow_and_many_tiles():
+    """Tiles with far more overflow entries than the kernel requests ahead
+    (magnitudes spread over 2^-40..2^0: most weights overflow), and enough
+    tiles that every persistent CTA walks several."""
+    from tests.test_gpu_gemm import _dense_patch_weight
+    w = _dense_patch_weight(600, 1024, seed=13)
+    p = oracle_dict(w)
+    assert p["delta_ovf_idx"].numel() > 600 * 1024 // 2
+    assert np.array_equal(_decode(p), w)
+    w2 = synthetic_weight(4096, 4096, seed=17, device="cuda")
+    p2 = bf16x_quantize(w2, device="cuda")
+    out = bf16x_decode_triton(p2["sign_packed"], p2["mant_packed"], p2["delta_packed"], p2["emax"], 4096, 4096,
+                              p2["delta_ovf_idx"], p2["delta_ovf_val"])
+    assert torch.equal(out.view(torch.int16), w2.view(torch.int16))
+    _lib.check_device_status()
+
+
+def test_decode_unaligned_streams():
+    """Streams that do not start on a 16-byte boundary take plain loads
+    instead of the bulk copies; the result is the same."""
+    w = bits_of(synthetic_weight(1000, 1536, seed=19))
+    p = oracle_dict(w)
+
+    def shifted(t):
+        buf = torch.zeros(t.numel() + 4, dtype=t.dtype, device="cuda")
+        buf[1:1 + t.numel()] = t.cuda()
+        return buf[1:1 + t.numel()]
+    s, m, d = (shifted(p[k]) for k in ("sign_packed", "mant_packed", "delta_packed"))
+    e = shifted(p["emax"])
+    assert s.data_ptr() % 16 != 0 and e.data_ptr() % 16 != 0
+    out = bf16x_decode_triton(s, m, d, e, 1000, 1536, p["delta_ovf_idx"], p["delta_ovf_val"])
+    assert np.array_equal(bits_of(out), w)
+    _lib.check_device_status()
+
+
 def test_decode_reports_unsorted_table():
     w = bits_of(synthetic_weight(64, 512, seed=5))
     p = oracle_dict(w)

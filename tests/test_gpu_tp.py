@@ -210,3 +210,84 @@ def test_gemv_peers_allgather_2gpu():
         p.join(timeout=60)
     for r in res:
         assert r[1], r
+
+
+def _peer_layers_worker(rank, world, port, q):
+    try:
+        import torch.distributed as dist
+
+        from bfloat16x_b200 import _lib
+        from bfloat16x_b200.llama_e2e import (CONFIGS, LlamaModel, generate, pack_model, peer_heap_bytes,
+                                              use_peer_collectives)
+        from bfloat16x_b200.peer import PeerGroup
+        from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
+        from bfloat16x_b200.tp import ColumnParallelBf16x, RowParallelBf16x
+        from oracle import oracle
+        from tests.gpu_util import bits_of, oracle_dict, rel_l2
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        pg = PeerGroup(None, dev, heap_bytes=16 << 20)
+        res = []
+        w = synthetic_weight(1000, 2048, seed=3)
+        wb = bits_of(w)
+        p = oracle_dict(wb)
+        row = RowParallelBf16x(p, peers=pg)
+        col = ColumnParallelBf16x(w, peers=pg)
+        for M in (1, 7, 16, 40):
+            x = synthetic_activation(M, 2048, seed=M)
+            ref = oracle.matmul_bf16w(x.float().numpy(), wb)
+            ref16 = torch.from_numpy(ref).to(torch.bfloat16).float().numpy()
+            for _ in range(2):
+                y = row(x.cuda()).float().cpu().numpy()
+                res.append(rel_l2(y, ref16) < 1e-3)
+                y2 = col(x.cuda()).float().cpu().numpy()
+                res.append(rel_l2(y2, ref16) < 1e-3)
+        _lib.check_device_status(rank)
+        # the tensor-parallel decoder: collectives in the fused GEMVs against NCCL
+        cfg = CONFIGS["tiny"]
+        prompt = torch.randint(0, cfg.vocab, (2, 24), generator=torch.Generator().manual_seed(2)).to(dev)
+        model = LlamaModel(cfg, 64, dev, seed=4, tp=world, batch=2)
+        pack_model(model)
+        tok_n, _, _ = generate(model, prompt, 8, use_graph=True)
+        pos = torch.tensor(24, dtype=torch.long, device=dev)
+        lg_n = model(tok_n[:1].t().contiguous(), pos)
+        pg2 = PeerGroup(None, dev, heap_bytes=peer_heap_bytes(model))
+        use_peer_collectives(model, pg2)
+        tok_p, _, _ = generate(model, prompt, 8, use_graph=True)
+        lg_p = model(tok_n[:1].t().contiguous(), pos)
+        res.append(bool(torch.equal(tok_p, tok_n)))
+        res.append(float((lg_p - lg_n).norm() / lg_n.norm()) < 1e-2)
+        _lib.check_device_status(rank)
+        torch.cuda.synchronize()
+        pg2.close()
+        pg.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, all(res), res))
+    except Exception:
+        import traceback
+        q.put((rank, False, traceback.format_exc()))
+
+
+# Row- and column-parallel layers whose all-gather / all-reduce run inside
+# the fused GEMV (PeerGroup), and the tensor-parallel decoder with its
+# collectives moved there, against NCCL.
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_layers_and_decoder_peer_collectives_2gpu():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29200 + os.getpid() % 1000
+    procs = [ctx.Process(target=_peer_layers_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert r[1], r
