@@ -59,9 +59,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--mode", choices=["gemv", "gemm", "e2e"], default="gemv",
+    ap.add_argument("--mode", choices=["gemv", "gemm", "e2e", "kernels"], default="gemv",
                     help="gemv: decode+GEMV sweep (the headline); gemm: decode+GEMM prefill TFLOPS; "
-                         "e2e: Llama-style decoder, ms per generated token against bf16 weights")
+                         "e2e: Llama-style decoder, ms per generated token against bf16 weights; "
+                         "kernels: the stand-alone packer / repack / decode / GGUF kernels, GB/s each")
     ap.add_argument("--model", choices=["1b", "8b", "tiny"], default="1b", help="decoder for --mode e2e")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens for --mode e2e")
     ap.add_argument("--new", type=int, default=128, help="generated tokens for --mode e2e")
@@ -448,10 +449,14 @@ def run_ours(args):
     shapes = shapes_of(args)
     tp = world > 1 and args.scaling == "strong"
     peers = None
+    collective_note = None
     if tp and args.collective == "peer":
         from bfloat16x_b200.peer import PeerGroup
         heap = sum(2 * (B * o * 4 + 256) for o, _ in shapes) + (1 << 20)
-        peers = PeerGroup(None, dev, heap_bytes=heap)
+        try:
+            peers = PeerGroup(None, dev, heap_bytes=heap)
+        except _lib.Bf16xError as e:        # raised on every rank alike
+            collective_note = f"NCCL all-gather: peer mapping unavailable ({e})"
     layers = []
     for si, (out_f, in_f) in enumerate(shapes):
         if args.scaling == "weak" or world == 1:
@@ -692,6 +697,7 @@ def run_ours(args):
             "scaling": args.scaling if world > 1 else "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights with 0.5% x 2^U{4..8} outliers, bf16 N(0,1) activations)",
             "config": bench_config(args, shapes, world),
+            "collective_note": collective_note,
             "resident_bpw": round(8 * sum(L['rw'].nbytes() for L in layers) /
                                   sum(L['rows'] * L['in_f'] for L in layers), 3),
             "frac_of_8TBs": round(value / world / 8000.0, 4),
@@ -852,7 +858,7 @@ def run_e2e(args):
     import torch.distributed as dist
 
     from bfloat16x_b200 import _lib
-    from bfloat16x_b200.llama_e2e import (CONFIGS, LlamaModel, generate, logits_rel_l2, pack_model,
+    from bfloat16x_b200.llama_e2e import (CONFIGS, LlamaModel, fp32_linears, generate, logits_rel_l2, pack_model,
                                           teacher_forced_logits)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -871,6 +877,10 @@ def run_e2e(args):
     # logits of the bf16 weights on the prompt and on 16 teacher-forced steps
     n_tf = min(16, args.new)
     ref_logits = teacher_forced_logits(model, prompt, ref_tok[:n_tf])
+    with fp32_linears(model):
+        alt_logits = teacher_forced_logits(model, prompt, ref_tok[:n_tf])
+    fl_max, fl_mean = logits_rel_l2(alt_logits, ref_logits)
+    del alt_logits
     nbytes, _ = pack_model(model)
     got_logits = teacher_forced_logits(model, prompt, ref_tok[:n_tf])
     tf_max, tf_mean = logits_rel_l2(got_logits, ref_logits)
@@ -911,8 +921,11 @@ def run_e2e(args):
             "linear_weight_bytes": {"bf16x_resident": int(nbytes), "bf16": int(2 * n_w)},
             "tokens_equal_to_bf16_run": same,
             "logits_rel_l2_vs_bf16": {"max": round(tf_max, 6), "mean": round(tf_mean, 6),
+                                      "noise_floor_max": round(fl_max, 6), "noise_floor_mean": round(fl_mean, 6),
                                       "steps": 1 + n_tf, "how": "prompt's last position + teacher-forced decode "
-                                                                "steps on the bf16 run's tokens"},
+                                                                "steps on the bf16 run's tokens; the floor is the "
+                                                                "same bf16 weights with fp32-GEMM linears against "
+                                                                "cuBLAS bf16"},
             "timing": "decode step as one CUDA graph replayed per token; max over ranks",
             "collectives": ("decode: o/down_proj partial sums and lm_head logits exchanged inside the fused GEMVs "
                             "(NVLink peer stores); prefill: NCCL") if peers is not None else "NCCL",
@@ -926,6 +939,104 @@ def run_e2e(args):
         dist.destroy_process_group()
 
 
+def run_kernels(args):
+    """The non-matmul kernels on one weight (default 8192x8192, 64 M weights,
+    inputs and outputs larger than L2): the GPU packer (bf16x_quantize), the
+    resident-layout repack, the flat decode + overflow fix, and the GGUF
+    block quantize / dequantize / side-table count, pack and apply.  Each
+    launch is timed alone after a 256 MB L2 flush (median of --steps); GB/s
+    counts the bytes each kernel must read and write."""
+    import torch
+
+    from bfloat16x_b200 import _lib
+    from bfloat16x_b200 import bf16x_gguf_block as gg
+    from bfloat16x_b200._lib import BF16X_DTYPE_BF16, call, ptr
+    from bfloat16x_b200.bf16x_decode import bf16x_decode_triton
+    from bfloat16x_b200.opqk_linear import bf16x_quantize
+    from bfloat16x_b200.resident import ResidentWeight, flat_args, flat_on_device
+    from bfloat16x_b200.synthetic import synthetic_weight
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    out_f, in_f = shapes_of(args)[0] if args.shapes else (8192, 8192)
+    n = out_f * in_f
+    w = synthetic_weight(out_f, in_f, seed=0, device=dev)
+    flush = _l2_flusher(dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    peak, kind = peak_hbm()
+
+    def timed(fn):
+        ts = []
+        fn()
+        for _ in range(max(args.steps, 3)):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    rec = {}
+
+    def put(name, ms, nbytes, kernels):
+        rec[name] = {"us": round(ms * 1e3, 2), "GB/s": round(nbytes / (ms / 1e3) / 1e9, 1),
+                     "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4), "bytes": int(nbytes), "kernels": kernels}
+
+    # GPU packer: count pass + encode pass (bf16 in, streams + table out)
+    p = bf16x_quantize(w, device=dev)
+    n_ovf = p["delta_ovf_idx"].numel()
+    stream_b = 4 * (p["sign_packed"].numel() + p["mant_packed"].numel() + p["delta_packed"].numel()) + p["emax"].numel()
+    put("quantize", timed(lambda: bf16x_quantize(w, device=dev)), 2 * n + stream_b + 5 * n_ovf,
+        "quantize count + encode (bf16x_quantize_count, bf16x_quantize)")
+    # flat decode + overflow fix
+    y = torch.empty((out_f, in_f), dtype=torch.bfloat16, device=dev)
+    dargs = (p["sign_packed"], p["mant_packed"], p["delta_packed"], p["emax"], out_f, in_f,
+             p["delta_ovf_idx"], p["delta_ovf_val"])
+    bf16x_decode_triton(*dargs, out=y)
+    assert torch.equal(y.view(torch.int16), w.view(torch.int16)), "decode not bit-exact"
+    put("decode", timed(lambda: bf16x_decode_triton(*dargs, out=y)), stream_b + 5 * n_ovf + 2 * n,
+        "flat_decode_kernel (bf16x_decode)")
+    # repack: flat dict -> resident layout (count + scan + write)
+    rw = ResidentWeight.from_packed(p, device=dev)
+    f = flat_on_device(p, dev)
+    ptile = torch.empty_like(rw.ptile_off)
+
+    def repack():
+        call("bf16x_repack_count", *flat_args(f), out_f, in_f, 0, out_f, ptr(ptile), st)
+        call("bf16x_repack", *flat_args(f), out_f, in_f, 0, out_f, ptr(rw.ptile_off), ptr(rw.layout),
+             ptr(rw.precs), st)
+    put("repack", timed(repack), 2 * (stream_b + 5 * n_ovf) + rw.nbytes(),
+        "repack count + write (streams read twice, resident layout + records written)")
+    # resident decode: layout -> bf16
+    put("resident_decode", timed(lambda: rw.decode(out=y)), rw.nbytes() + 2 * n, "resident_decode_kernel")
+    # GGUF blocks
+    blocks = torch.empty(n // 32 * 46, dtype=torch.uint8, device=dev)
+    put("gguf_quantize", timed(lambda: call("bf16x_gguf_quantize", ptr(w), BF16X_DTYPE_BF16, n, ptr(blocks), st)),
+        2 * n + n // 32 * 46, "bf16x_gguf_quantize (bf16 in)")
+    put("gguf_dequantize", timed(lambda: call("bf16x_gguf_dequantize", ptr(blocks), n // 32, ptr(y),
+                                              BF16X_DTYPE_BF16, st)),
+        n // 32 * 46 + 2 * n, "bf16x_gguf_dequantize (bf16 out)")
+    row_off = torch.empty(out_f + 1, dtype=torch.int32, device=dev)
+    put("gguf_ovf_count", timed(lambda: call("bf16x_gguf_ovf_count", ptr(w), BF16X_DTYPE_BF16, out_f, in_f,
+                                             ptr(row_off), st)), 2 * n + 4 * (out_f + 1), "bf16x_gguf_ovf_count")
+    ro, ec, eb = gg._pack_ovf_dev(w, BF16X_DTYPE_BF16, out_f, in_f)
+    ne = ec.numel()
+    put("gguf_ovf_pack", timed(lambda: call("bf16x_gguf_ovf_pack", ptr(w), BF16X_DTYPE_BF16, out_f, in_f, ptr(ro),
+                                            ptr(ec), ptr(eb), st)), 2 * n + 4 * (out_f + 1) + 4 * ne,
+        "bf16x_gguf_ovf_pack")
+    put("gguf_apply_ovf", timed(lambda: call("bf16x_gguf_apply_ovf", ptr(y), BF16X_DTYPE_BF16, out_f, in_f, ptr(ro),
+                                             ptr(ec), ptr(eb), ne, st)), 4 * (out_f + 1) + 4 * ne + 4 * ne,
+        "bf16x_gguf_apply_ovf (scattered 2-byte writes)")
+    _lib.check_device_status(0)
+    line = {"metric": "stand-alone BF16X kernels, GB/s of the bytes each must move", "unit": "GB/s",
+            "config": {"workload": f"one {out_f}x{in_f} weight (synthetic, {n_ovf} overflow entries, "
+                                   f"{ne} GGUF side-table entries)", "l2": "256 MB flush before every launch"},
+            "peak": {"hbm_gbs": peak, "source": kind}, "kernels": rec}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -934,6 +1045,8 @@ def main():
         run_e2e(args)
     elif args.mode == "gemm":
         run_gemm(args)
+    elif args.mode == "kernels":
+        run_kernels(args)
     else:
         run_ours(args)
 

@@ -507,11 +507,12 @@ __device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, 
         :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
-// Arrive on the barrier at `bar_cluster` (this CTA's or the peer's) once the
-// pair's MMAs issued so far have completed.
-__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 :: "r"(bar_cluster) : "memory");
+// Arrive on the barrier at this shared-memory offset in BOTH CTAs of the
+// pair (ctaMask 0b11) once the pair's MMAs issued so far have completed: one
+// commit instead of one per CTA.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 :: "r"(smem_u32(bar)), "h"((uint16_t)3u) : "memory");
 }
 
 // All threads of both CTAs of the cluster.
@@ -660,7 +661,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
         // ------------------------------------------------------- MMA issuer
         if (lane == 0 && rank == 0) {
             constexpr uint32_t idesc = umma_idesc_bf16_m<2 * kGemmBM, (BN > 256 ? 256 : BN)>();
-            const uint32_t peer = 1u;
             int as = 0, bs = 0, ac = 0;
             uint32_t aph = 0, bph = 0, acph = 0;
             bool ok = true;
@@ -683,16 +683,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm2sm_kernel(const __grid_c
                             umma_bf16_pair(d_tmem + 256u, ad + 2u * k16, bd + (uint64_t)((128 * 128) >> 4) + 2u * k16,
                                            idesc, (kb | k16) != 0);
                     }
-                    umma_commit_pair(smem_u32(&a_empty[as]));
-                    umma_commit_pair(mapa_shared(smem_u32(&a_empty[as]), peer));
-                    umma_commit_pair(smem_u32(&b_empty[bs]));
-                    umma_commit_pair(mapa_shared(smem_u32(&b_empty[bs]), peer));
+                    umma_commit_pair_both(&a_empty[as]);
+                    umma_commit_pair_both(&b_empty[bs]);
                     if (++as == C::kAStages) { as = 0; aph ^= 1u; }
                     if (++bs == C::kBStages) { bs = 0; bph ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit_pair(smem_u32(&acc_full[ac]));
-                umma_commit_pair(mapa_shared(smem_u32(&acc_full[ac]), peer));
+                umma_commit_pair_both(&acc_full[ac]);
                 if (++ac == C::kAccBufs) { ac = 0; acph ^= 1u; }
             }
         }
@@ -1109,13 +1106,11 @@ tma_load_2d_pair(stg, &p.amap, pos * kChunkElems + (kb & 3) * kGemmBK,
                             umma_bf16_pair(d_tmem + 256u * j, ad + 2u * k16, bd + 2u * k16, idesc, (kb | k16) != 0);
                     }
                     if (!ok) break;
-                    umma_commit_pair(smem_u32(&empty[s]));
-                    umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1u));
+                    umma_commit_pair_both(&empty[s]);
                     if (++s == C::kStages) { s = 0; ph ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit_pair(smem_u32(&acc_full[ac]));
-                umma_commit_pair(mapa_shared(smem_u32(&acc_full[ac]), 1u));
+                umma_commit_pair_both(&acc_full[ac]);
                 if (NH == 1) {
                     if (++ac == 2) { ac = 0; acph ^= 1u; }
                 } else {

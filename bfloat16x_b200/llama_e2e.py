@@ -387,6 +387,29 @@ def teacher_forced_logits(model: LlamaModel, prompt: torch.Tensor, tokens: torch
     return torch.stack(out)
 
 
+class fp32_linears:
+    """Context manager: every plain nn.Linear of ``model`` computes in fp32
+    (weights and activations upcast, product rounded back to the input
+    dtype) instead of cuBLAS bf16.  Both are the exact-weight product and
+    differ only in accumulation order and rounding, so the logits' distance
+    between the two is the noise floor any exact-weight kernel is measured
+    against."""
+
+    def __init__(self, model: nn.Module):
+        self.mods = [m for m in model.modules() if type(m) is nn.Linear]
+
+    def __enter__(self):
+        for m in self.mods:
+            m.forward = (lambda x, m=m: F.linear(x.float(), m.weight.float(),
+                                                 None if m.bias is None else m.bias.float()).to(x.dtype))
+        return self
+
+    def __exit__(self, *exc):
+        for m in self.mods:
+            del m.forward
+        return False
+
+
 def logits_rel_l2(a: torch.Tensor, b: torch.Tensor) -> tuple[float, float]:
     """(max, mean) over steps of ||a - b|| / ||b|| per step (fp64)."""
     d = (a.double() - b.double()).flatten(1).norm(dim=1) / b.double().flatten(1).norm(dim=1)
@@ -430,4 +453,4 @@ def generate(model: LlamaModel, prompt: torch.Tensor, new_tokens: int, use_graph
 
 __all__ = ["LlamaConfig", "CONFIGS", "LlamaModel", "ColumnShard", "VocabShard", "ResidentLinear", "pack_model",
            "GraphDecoder", "generate", "use_peer_collectives", "peer_heap_bytes", "teacher_forced_logits",
-           "logits_rel_l2"]
+           "logits_rel_l2", "fp32_linears"]

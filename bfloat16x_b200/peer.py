@@ -49,22 +49,47 @@ class PeerGroup:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.heap_bytes = int(heap_bytes)
         self.buf = torch.zeros(HEADER_BYTES + self.heap_bytes, dtype=torch.uint8, device=self.device)
-        handle, offset = self._export(self.buf.data_ptr())
+        # Every step below is taken by every rank, and a failure on any rank
+        # (no IPC on this node, say) raises on all of them at the same point,
+        # so no rank is left waiting in a collective.
+        try:
+            mine = self._export(self.buf.data_ptr())
+        except _lib.Bf16xError as e:
+            mine = ("error", str(e))
         entries = [None] * self.world
-        dist.all_gather_object(entries, (handle, offset), group=group)
+        dist.all_gather_object(entries, mine, group=group)
+        bad = [e[1] for e in entries if e[0] == "error"]
+        if bad:
+            raise _lib.Bf16xError(f"PeerGroup: a rank could not export its buffer: {bad[0]}")
         self._imported = []
         self.ptrs = []                                   # base of every rank's buffer, in this address space
+        err = ""
         for q, (h, off) in enumerate(entries):
             if q == self.rank:
                 self.ptrs.append(self.buf.data_ptr())
-            else:
+                continue
+            try:
                 base = self._import(h)
-                self._imported.append(base)
-                self.ptrs.append(base + off)
+            except _lib.Bf16xError as e:
+                err = str(e)
+                break
+            self._imported.append(base)
+            self.ptrs.append(base + off)
+        errs = [None] * self.world
+        dist.all_gather_object(errs, err, group=group)
+        if any(errs):
+            for base in self._imported:
+                self._close(base)
+            self._imported = []
+            raise _lib.Bf16xError(f"PeerGroup: a rank could not map its peers' buffers: {next(e for e in errs if e)}")
         self._next = HEADER_BYTES
         self._flag_table = (ctypes.c_void_p * self.world)(*[p + FLAGS_OFF for p in self.ptrs])
-        torch.cuda.synchronize(self.device)
+        self._sync()
         dist.barrier(group=group)
+
+    def _sync(self) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
 
     # ---- the CUDA IPC calls (one place, so host tests can replace them) ----
     @staticmethod
@@ -120,16 +145,16 @@ class PeerGroup:
     # ---- lifetime ----------------------------------------------------------
     def reset(self) -> None:
         """Zero this rank's state and flags, collectively (after a device error)."""
-        torch.cuda.synchronize(self.device)
+        self._sync()
         dist.barrier(group=self.group)
         self.buf[:HEADER_BYTES].zero_()
-        torch.cuda.synchronize(self.device)
+        self._sync()
         dist.barrier(group=self.group)
 
     def close(self) -> None:
         """Unmap the peers' buffers, collectively (no collective GEMV may be in
         flight on any rank)."""
-        torch.cuda.synchronize(self.device)
+        self._sync()
         dist.barrier(group=self.group)
         for base in self._imported:
             self._close(base)

@@ -66,3 +66,72 @@ def test_row_and_column_parallel_gloo(world):
         p.join(timeout=60)
     for r in res:
         assert r[1:] == (True, True, True), r
+
+
+def _peer_worker(rank, world, port, q, fail_rank):
+    """PeerGroup's host logic over gloo on CPU, with the CUDA IPC calls
+    replaced by stand-ins (a handle is the rank's buffer address)."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from bfloat16x_b200 import _lib
+        from bfloat16x_b200.peer import FLAGS_OFF, HEADER_BYTES, PeerGroup
+
+        closed = []
+
+        def export(ptr):
+            if rank == fail_rank:
+                raise _lib.Bf16xError("no IPC here")
+            return (int(ptr).to_bytes(8, "little") + bytes(56), 64)
+
+        PeerGroup._export = staticmethod(export)
+        PeerGroup._import = staticmethod(lambda h: int.from_bytes(h[:8], "little") + 1000)
+        PeerGroup._close = staticmethod(lambda base: closed.append(base))
+        try:
+            pg = PeerGroup(None, torch.device("cpu"), heap_bytes=1 << 16)
+        except _lib.Bf16xError as e:
+            dist.barrier()
+            dist.destroy_process_group()
+            q.put((rank, fail_rank >= 0, "failed on every rank: " + str(e)))
+            return
+        ok = [pg.world == world, pg.rank == rank, len(pg.ptrs) == world]
+        ok.append(pg.ptrs[rank] == pg.buf.data_ptr())
+        a, b = pg.alloc(100), pg.alloc(3000)
+        ok += [a == HEADER_BYTES, b == HEADER_BYTES + 256, b % 256 == 0]
+        t = pg.table(b)
+        ok += [t[rank] == pg.buf.data_ptr() + b, list(pg.flag_table)[rank] == pg.buf.data_ptr() + FLAGS_OFF]
+        # every rank's view of every buffer: its base (+ the stand-in mapping) + the same offset
+        bases = [None] * world
+        dist.all_gather_object(bases, pg.buf.data_ptr())
+        ok += [t[q_] == (bases[q_] if q_ == rank else bases[q_] + 1000 + 64) + b for q_ in range(world)]
+        ok.append(tuple(pg.local(b, (3, 250), torch.float32).shape) == (3, 250))
+        try:
+            pg.alloc(1 << 20)
+            ok.append(False)
+        except _lib.Bf16xError:
+            ok.append(True)
+        pg.close()
+        ok.append(len(closed) == world - 1)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, fail_rank < 0 and all(ok), ok))
+    except Exception:
+        import traceback
+        q.put((rank, False, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("fail_rank", [-1, 1])
+def test_peer_group_host_logic_gloo(fail_rank):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + os.getpid() % 200 + (fail_rank + 1) * 7
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q, fail_rank)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert r[1], r
