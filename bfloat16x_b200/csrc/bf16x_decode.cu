@@ -12,9 +12,9 @@
 //   * A tile's streams -- 256 sign words, 1792 mantissa words, 768 delta
 //     words and 512 emax bytes, every piece 16-byte aligned because the tile
 //     is 8192-aligned -- arrive by four bulk copies (TMA engine) into one of
-//     two shared-memory stages, the next tile's copies issued while this one
-//     is decoded; a tile that is not whole (the last) or streams that are not
-//     16-byte aligned take plain loads instead.
+//     three shared-memory stages, the copies of the tile two ahead issued
+//     while this one is decoded; a tile that is not whole (the last) or
+//     streams that are not 16-byte aligned take plain loads instead.
 //   * Thread t decodes group t (32 elements: one sign word, seven mantissa
 //     words, three delta words, two emax bytes -- shared-memory strides 7 and
 //     3 words touch 32 distinct banks) with funnel shifts and writes four
@@ -47,6 +47,7 @@ constexpr int kDecDeltaW = kDecTile * 3 / 32;            // 768 words
 constexpr int kDecEmaxB = kDecTile / 16;                 // 512 bytes
 constexpr int kDecStageB = 4 * (kDecSignW + kDecMantW + kDecDeltaW) + kDecEmaxB;   // 11776
 constexpr int kDecPrefetch = 2;                          // overflow entries per thread held ahead
+constexpr int kDecStages = 3;                            // tiles in flight per CTA: this one + two ahead
 constexpr int kDecCtasPerSm = 4;
 
 struct DecStage {
@@ -58,9 +59,9 @@ struct DecStage {
 static_assert(sizeof(DecStage) == kDecStageB && kDecStageB % 16 == 0, "stage layout");
 
 struct DecSmem {
-    DecStage stage[2];
+    DecStage stage[kDecStages];
     uint4 tile[kDecTile / 8];                            // 16 KB of bf16, swizzled 16-byte chunks
-    uint64_t bar[2];
+    uint64_t bar[kDecStages];
     int64_t slice_lo;                                    // start of the first tile's overflow slice
 };
 
@@ -110,13 +111,13 @@ flat_decode_kernel(FlatStreams f, uint16_t *__restrict__ out, int64_t n_tiles, i
         bulk_g2s(st.delta, f.delta + t * kDecDeltaW, 4 * kDecDeltaW, &sm.bar[s]);
         bulk_g2s(st.emax, f.emax + t * kDecEmaxB, kDecEmaxB, &sm.bar[s]);
     };
-    if (tid == 0) {
-        mbar_init(&sm.bar[0], 1);
-        mbar_init(&sm.bar[1], 1);
-    }
+    if (tid == 0)
+        for (int s = 0; s < kDecStages; ++s) mbar_init(&sm.bar[s], 1);
     fence_mbar_init();
     __syncthreads();
-    if (tid == 0 && bulk_tile(tb)) issue(tb, 0);
+    if (tid == 0)
+        for (int s = 0; s < kDecStages - 1 && tb + s < te; ++s)
+            if (bulk_tile(tb + s)) issue(tb + s, s);
 
     // start of the first tile's overflow slice; every later tile's slice
     // starts where the previous one ended
@@ -133,11 +134,13 @@ flat_decode_kernel(FlatStreams f, uint16_t *__restrict__ out, int64_t n_tiles, i
     uint32_t phases = 0u;                                 // bit s: parity of the next phase of stage s
     uint16_t *t16 = reinterpret_cast<uint16_t *>(sm.tile);
     for (int64_t t = tb; t < te; ++t) {
-        const int s = (int)((t - tb) & 1);
+        const int s = (int)((t - tb) % kDecStages);
         const int64_t t0 = t * (int64_t)kDecTile;
         const int64_t t1 = min(t0 + (int64_t)kDecTile, f.n);
         const bool bulk = bulk_tile(t);
-        if (t + 1 < te && tid == 0 && bulk_tile(t + 1)) issue(t + 1, s ^ 1);
+        // the tile kDecStages - 1 ahead goes into the stage the previous tile freed
+        const int64_t ta = t + kDecStages - 1;
+        if (ta < te && tid == 0 && bulk_tile(ta)) issue(ta, (int)((ta - tb) % kDecStages));
         // The next entries of the sorted overflow table, requested before the
         // streams are awaited: those below t1 (a prefix, the table being
         // sorted) are this tile's.

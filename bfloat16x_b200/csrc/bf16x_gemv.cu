@@ -82,7 +82,8 @@ struct GemvCfg {
     static constexpr int kZeroOff = kXCOff + kXCache;                        // 512 zero bytes
     static constexpr int kRecOff = kZeroOff + 512;                           // per slot record offset
     static constexpr int kBarOff = kRecOff + kWarps * kStages * 8;
-    static constexpr int kSmem = kBarOff + kWarps * kStages * 8 + 8 + 1024;  // + the x barrier, base alignment
+    static constexpr int kCtaOff = kBarOff + kWarps * kStages * 8 + 8;       // after the x barrier: finished warps
+    static constexpr int kSmem = kCtaOff + 16 + 1024;                        // + base alignment
     static_assert(kStages >= 2, "ring too shallow for this configuration");
     static_assert(kWBytes % 1024 == 0 && kXRSlot % 128 == 0 && kPOff % 16 == 0 && kXCOff % 128 == 0,
                   "slot alignment");
@@ -273,8 +274,12 @@ __device__ __forceinline__ void half_mma2(const StepFrag (&f)[8], const uint16_t
 
 // One output value to every destination: this GPU's y, and with the
 // collective epilogue the same position of every other rank's y.
+template <bool COLL>
 __device__ __forceinline__ void store_y(const GemvParams &p, int64_t idx, float o) {
-    if (p.y_f32) {
+    if constexpr (!COLL) {
+        if (p.y_f32) reinterpret_cast<float *>(p.y)[idx] = o;
+        else reinterpret_cast<uint16_t *>(p.y)[idx] = f32_to_bf16_bits_rn(o);
+    } else if (p.y_f32) {
         for (int q = 0; q < p.nranks; ++q) reinterpret_cast<float *>(p.ydst[q])[idx] = o;
     } else {
         const uint16_t v = f32_to_bf16_bits_rn(o);
@@ -286,21 +291,33 @@ __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
 }
 
-// End of the collective epilogue, run by every warp that took part in the
-// partition once its outputs are stored (their peer stores included).  The
-// warp makes its stores visible system-wide and counts itself; the last one
-// of the grid resets the count, advances the epoch, posts it to every rank's
-// flag word for this rank (a release at system scope, after a full fence that
-// covers every warp's stores it observed through the count) and waits,
-// bounded, until every rank has posted the same epoch here.  Only then does
-// the kernel complete, so the next kernel of the stream sees all ranks' rows.
-__device__ __forceinline__ void collective_finish(const GemvParams &p, int64_t n_warps, int lane) {
-    __threadfence_system();
+// End of the collective epilogue, run by every warp of every CTA once its
+// outputs are stored (their peer stores included), the warps that had no
+// items too.  Within the CTA the warps count themselves on a shared-memory
+// word after a CTA-scope fence; the CTA's last warp then makes the CTA's
+// stores visible system-wide (fence.sc.sys, cumulative over what the count
+// ordered before it) and counts the CTA on this GPU's state word.  The grid's
+// last CTA resets the count, advances the epoch, posts it to every rank's
+// flag word for this rank (release at system scope) and waits, bounded,
+// until every rank has posted the same epoch here.  Only then does the kernel
+// complete, so the next kernel of the stream sees all ranks' rows.  A warp
+// that gave up on a wait never counts itself: its CTA never finishes, and the
+// peers' bounded waits time out and report it.
+__device__ __forceinline__ void collective_finish(const GemvParams &p, uint32_t *cta_done, int n_warps, int lane) {
     __syncwarp();
     uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(p.state, 1u);
+    if (lane == 0) {
+        __threadfence_block();
+        old = atomicAdd(cta_done, 1u);
+    }
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old + 1 != (uint32_t)n_warps) return;
+    uint32_t last = 0;
+    if (lane == 0) {
+        __threadfence_system();
+        last = atomicAdd(p.state, 1u) + 1 == gridDim.x;
+    }
+    if (!__shfl_sync(0xffffffffu, last, 0)) return;
     __threadfence_system();
     const uint32_t epoch = p.state[1] + 1u;
     if (lane == 0) {
@@ -317,7 +334,7 @@ __device__ __forceinline__ void collective_finish(const GemvParams &p, int64_t n
 __device__ __forceinline__ int64_t item_lo(int64_t w, int64_t T, int64_t W) { return T * w / W; }
 __device__ __forceinline__ int64_t item_owner(int64_t i, int64_t T, int64_t W) { return ((i + 1) * W - 1) / T; }
 
-template <int BMAX, int NW, bool XRES>
+template <int BMAX, int NW, bool XRES, bool COLL>
 __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
     gemv_kernel(const __grid_constant__ GemvParams p) {
     using C = GemvCfg<BMAX, NW, XRES>;
@@ -331,6 +348,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
     int64_t *rec_of = reinterpret_cast<int64_t *>(smem + C::kRecOff) + warp * S;
     uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + C::kBarOff) + C::kWarps * S;
     for (int i = threadIdx.x; i < 128; i += blockDim.x) reinterpret_cast<uint32_t *>(smem + C::kZeroOff)[i] = 0u;
+    if (threadIdx.x == 0) *reinterpret_cast<uint32_t *>(smem + C::kCtaOff) = 0u;
     if (lane == 0)
         for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     if (XRES && threadIdx.x == 0) mbar_init(xbar, 1);
@@ -339,7 +357,11 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
     griddep_launch_dependents();
 
     const int64_t gw = (int64_t)blockIdx.x * C::kWarps + warp;
-    if (gw >= p.W) return;
+    uint32_t *cta_done = reinterpret_cast<uint32_t *>(smem + C::kCtaOff);           // warps of the CTA finished
+    if (gw >= p.W) {
+        if constexpr (COLL) collective_finish(p, cta_done, C::kWarps, lane);
+        return;
+    }
     if (lane == 0) {
         prefetch_tensormap(&p.wmap);
         prefetch_tensormap(&p.xmap);
@@ -483,7 +505,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
             const int64_t row = row0 + rr;
             if (b < p.batch && row < p.rows) {
                 if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
-                store_y(p, b * p.ldy + row, o);
+                store_y<COLL>(p, b * p.ldy + row, o);
             }
         }
         if (lane == 0) p.tile_cnt[tl] = 0;
@@ -592,7 +614,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
                     if (b < p.batch && row < p.rows) {
                         float o = v[k];
                         if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
-                        store_y(p, b * p.ldy + row, o);
+                        store_y<COLL>(p, b * p.ldy + row, o);
                     }
                 }
             } else {
@@ -622,7 +644,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
         if (++s == S) { s = 0; parity ^= 1u; }
         if (++c == p.nch) { c = 0; ++tile; }
     }
-    if (p.nranks > 1) collective_finish(p, p.W, lane);
+    if constexpr (COLL) collective_finish(p, cta_done, C::kWarps, lane);
 }
 
 struct GemvLaunch {
@@ -720,15 +742,15 @@ static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
 // partial sums: per unit two [16][8] (batch <= 8) or [16][16] fp32 slots
 static int64_t scratch_need(const GemvLaunch &L, int64_t batch) { return L.W * 2 * 16 * (batch > 8 ? 16 : 8) * 4; }
 
-template <int BMAX, int NW, bool XRES = false>
-static int launch_gemv(const GemvParams &p, const GemvLaunch &L, cudaStream_t st) {
+template <int BMAX, int NW, bool XRES, bool COLL>
+static int launch_gemv_as(const GemvParams &p, const GemvLaunch &L, cudaStream_t st) {
     using C = GemvCfg<BMAX, NW, XRES>;
     int dev = 0;
     cudaGetDevice(&dev);
     static bool attr_set[64] = {false};
     if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv: device index %d", dev);
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BMAX, NW, XRES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BMAX, NW, XRES, COLL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
         if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: smem attribute: %s", cudaGetErrorString(e));
         attr_set[dev] = true;
     }
@@ -744,9 +766,16 @@ static int launch_gemv(const GemvParams &p, const GemvLaunch &L, cudaStream_t st
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<BMAX, NW, XRES>, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<BMAX, NW, XRES, COLL>, p);
     if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: launch: %s", cudaGetErrorString(e));
     return check_launch("bf16x_gemv");
+}
+
+// The plain GEMV and the collective-epilogue one are separate instantiations,
+// so the plain kernel carries no trace of the peer stores.
+template <int BMAX, int NW, bool XRES = false>
+static int launch_gemv(const GemvParams &p, const GemvLaunch &L, cudaStream_t st) {
+    return p.nranks > 1 ? launch_gemv_as<BMAX, NW, XRES, true>(p, L, st) : launch_gemv_as<BMAX, NW, XRES, false>(p, L, st);
 }
 
 }  // namespace bf16x

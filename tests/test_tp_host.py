@@ -135,3 +135,50 @@ def test_peer_group_host_logic_gloo(fail_rank):
         p.join(timeout=60)
     for r in res:
         assert r[1], r
+
+
+def _dead_peer_worker(rank, world, port, q):
+    """Rank 1 leaves before building the PeerGroup (between steps, nothing in
+    flight); rank 0 must get an error from its next collective, not hang."""
+    import datetime
+    import time
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+        from bfloat16x_b200 import _lib
+        from bfloat16x_b200.peer import PeerGroup
+        PeerGroup._export = staticmethod(lambda ptr: (int(ptr).to_bytes(8, "little") + bytes(56), 0))
+        PeerGroup._import = staticmethod(lambda h: int.from_bytes(h[:8], "little"))
+        PeerGroup._close = staticmethod(lambda base: None)
+        if rank == 1:
+            q.put((rank, True, "left"))
+            q.close()
+            q.join_thread()            # the message is out before the process vanishes
+            os._exit(0)
+        t0 = time.time()
+        try:
+            PeerGroup(None, torch.device("cpu"), heap_bytes=4096)
+            q.put((rank, False, "PeerGroup built without its peer"))
+        except (RuntimeError, _lib.Bf16xError) as e:
+            q.put((rank, time.time() - t0 < 60, f"raised after {time.time() - t0:.1f} s: {type(e).__name__}"))
+    except Exception:
+        import traceback
+        q.put((rank, False, traceback.format_exc()))
+
+
+def test_peer_group_dead_rank_raises():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29950 + os.getpid() % 40
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for r in res:
+        assert r[1], r
