@@ -310,12 +310,15 @@ class ClockSampler:
 
 
 def _l2_flusher(dev):
-    """A kernel that writes 256 MB (twice the 126 MB L2) on the current stream."""
+    """A kernel that reads 256 MB (twice the 126 MB L2) on the current stream.
+    Reading, not writing: a written flush buffer leaves L2 full of dirty lines
+    whose write-back to HBM would then be charged to the kernel timed next."""
     import torch
-    buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    buf = torch.ones(64 << 20, dtype=torch.int32, device=dev)
+    acc = torch.empty((), dtype=torch.int64, device=dev)
 
     def flush():
-        buf.fill_(1)
+        torch.sum(buf, dtype=torch.int64, out=acc)
     return flush
 
 
@@ -415,8 +418,8 @@ def decode_record(dev, reps=20):
         out[f"{o}x{i}"] = {"us": round(t * 1e3, 2), "GB/s": round(nbytes / (t / 1e3) / 1e9, 1),
                            "frac": round(nbytes / (t / 1e3) / 1e9 / peak, 4), "bytes": int(nbytes),
                            "overflow_entries": int(p["delta_ovf_idx"].numel())}
-    out["note"] = ("median of %d launches, each after a 256 MB L2 flush; fraction of the %s HBM copy "
-                   "bandwidth (%.1f GB/s)" % (reps, kind, peak))
+    out["note"] = ("median of %d launches, each after reading a 256 MB buffer (L2 flushed, no dirty lines); "
+                   "fraction of the %s HBM copy bandwidth (%.1f GB/s)" % (reps, kind, peak))
     return out
 
 
@@ -1032,7 +1035,7 @@ def run_kernels(args):
     _lib.check_device_status(0)
     line = {"metric": "stand-alone BF16X kernels, GB/s of the bytes each must move", "unit": "GB/s",
             "config": {"workload": f"one {out_f}x{in_f} weight (synthetic, {n_ovf} overflow entries, "
-                                   f"{ne} GGUF side-table entries)", "l2": "256 MB flush before every launch"},
+                                   f"{ne} GGUF side-table entries)", "l2": "256 MB read before every launch (L2 flushed, no dirty lines)"},
             "peak": {"hbm_gbs": peak, "source": kind}, "kernels": rec}
     print(json.dumps(line), flush=True)
 

@@ -17,8 +17,9 @@
 //     streams that are not 16-byte aligned take plain loads instead.
 //   * Thread t decodes group t (32 elements: one sign word, seven mantissa
 //     words, three delta words, two emax bytes -- shared-memory strides 7 and
-//     3 words touch 32 distinct banks) with funnel shifts and writes four
-//     16-byte chunks into the shared tile, XOR-swizzled so neither these
+//     3 words touch 32 distinct banks) two elements per step (one funnel
+//     shift for both mantissas, one for both deltas, one subtraction for both
+//     exponents) and writes four 16-byte chunks into the shared tile, XOR-swizzled so neither these
 //     writes nor the linear read-back for the global stores conflict.
 //   * The overflow table is sorted, so a tile's entries are the run that
 //     starts where the previous tile's ended (one 32-way search per CTA finds
@@ -76,19 +77,36 @@ __device__ __forceinline__ int dec_elem(int e) {
     return dec_chunk(t, o >> 3) * 8 + (o & 7);
 }
 
+// bf16x2 bits of elements 2P (low half) and 2P+1 (high half) of a group: one
+// funnel shift brings both 7-bit mantissas (stream bits 14P..14P+13), one both
+// 3-bit deltas (bits 6P..6P+5); both exponents come from one subtraction on
+// the two 16-bit halves.  e2 = emax * 0x00010001 + 0x100: the extra 256 in
+// the low half keeps (emax - delta) from borrowing out of it, and the mask
+// keeps the low 8 bits of each difference, i.e. (emax - delta) & 0xFF.
+template <int P>
+__device__ __forceinline__ uint32_t decode_flat_pair(uint32_t sw, const uint32_t (&mw)[8], const uint32_t (&dw)[4],
+                                                     uint32_t e2) {
+    constexpr int MB = 14 * P, DB = 6 * P;
+    const uint32_t x = funnel_r(mw[MB >> 5], mw[(MB >> 5) + 1], MB & 31);
+    const uint32_t m2 = (x & 0x7Fu) | ((x << 9) & 0x7F0000u);
+    const uint32_t y = funnel_r(dw[DB >> 5], dw[(DB >> 5) + 1], DB & 31);
+    const uint32_t d2 = (y & 7u) | ((y << 13) & 0x70000u);
+    const uint32_t ex = ((e2 - d2) << 7) & 0x7F807F80u;
+    const uint32_t s2 = (((sw >> (2 * P)) << 15) & 0x8000u) | ((sw << (30 - 2 * P)) & 0x80000000u);
+    return s2 | ex | m2;
+}
+
+template <int P>
+__device__ __forceinline__ void decode_flat_pairs(uint32_t sw, const uint32_t (&mw)[8], const uint32_t (&dw)[4],
+                                                  uint32_t e2a, uint32_t e2b, uint32_t (&pairs)[16]) {
+    pairs[P] = decode_flat_pair<P>(sw, mw, dw, P < 8 ? e2a : e2b);
+    if constexpr (P + 1 < 16) decode_flat_pairs<P + 1>(sw, mw, dw, e2a, e2b, pairs);
+}
+
 // bf16 bits of the 32 elements of one group from its words.
 __device__ __forceinline__ void decode_group32(uint32_t sw, const uint32_t (&mw)[8], const uint32_t (&dw)[4],
                                                uint32_t eb0, uint32_t eb1, uint32_t (&pairs)[16]) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const uint32_t s = (sw >> i) & 1u;
-        const uint32_t mb = 7 * i, db = 3 * i;
-        const uint32_t m = funnel_r(mw[mb >> 5], mw[(mb >> 5) + 1], mb & 31) & 0x7Fu;
-        const uint32_t d = funnel_r(dw[db >> 5], dw[(db >> 5) + 1], db & 31) & 0x7u;
-        const uint32_t e = i < 16 ? eb0 : eb1;
-        const uint32_t b = (s << 15) | (((e - d) & 0xFFu) << 7) | m;
-        if (i & 1) pairs[i >> 1] |= b << 16; else pairs[i >> 1] = b;
-    }
+    decode_flat_pairs<0>(sw, mw, dw, eb0 * 0x00010001u + 0x100u, eb1 * 0x00010001u + 0x100u, pairs);
 }
 
 __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm)
