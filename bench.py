@@ -318,7 +318,7 @@ def _l2_flusher(dev):
     acc = torch.empty((), dtype=torch.int64, device=dev)
 
     def flush():
-        torch.sum(buf, dtype=torch.int64, out=acc)
+        torch.sum(buf, dim=0, dtype=torch.int64, out=acc)
     return flush
 
 
