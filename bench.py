@@ -455,7 +455,7 @@ def run_ours(args):
     collective_note = None
     if tp and args.collective == "peer":
         from bfloat16x_b200.peer import PeerGroup
-        heap = sum(2 * (B * o * 4 + 256) for o, _ in shapes) + (1 << 20)
+        heap = sum(B * o * 8 + 256 for o, _ in shapes) + (1 << 20)
         try:
             peers = PeerGroup(None, dev, heap_bytes=heap)
         except _lib.Bf16xError as e:        # raised on every rank alike
@@ -478,8 +478,8 @@ def run_ours(args):
         L = dict(rw=rw, x=x, w=wb, rows=rows, r0=r0, out_f=out_f, in_f=in_f,
                  nbytes=workload_bytes(rw.nbytes(), rows, in_f, B))
         if peers is not None:
-            L["yoff"] = peers.alloc(B * out_f * 2)
-            L["y"] = peers.local(L["yoff"], (B, out_f), torch.bfloat16)
+            L["lloff"] = peers.alloc(B * out_f * 8)          # exchange words of this layer
+            L["y"] = torch.empty((B, out_f), dtype=torch.bfloat16, device=dev)
         elif tp:
             rmax = max(h - l for l, h in (shard_bounds(out_f, world, q, 16) for q in range(world)))
             L["y"] = torch.empty((B, rmax), dtype=torch.bfloat16, device=dev)
@@ -492,7 +492,7 @@ def run_ours(args):
     def run_layer(L, x=None):
         x = L["x"] if x is None else x
         if peers is not None:
-            L["rw"].gemv_peers(x, peers, L["yoff"], L["out_f"], L["r0"])
+            L["rw"].gemv_peers(x, peers, L["lloff"], L["out_f"], L["y"], mode=0, row0=L["r0"])
         elif tp:
             L["rw"].gemv(x, out=L["y"][:, :L["rows"]])
             dist.all_gather_into_tensor(L["yall"], L["y"])
@@ -647,7 +647,7 @@ def run_ours(args):
         e2e = {"value": round(total_bytes / (e_max / 1e3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": sum(t.numel() * 2 for t in hx) * world,
                "d2h_bytes_per_step": sum(t.numel() * 2 for t in hy) * world,
-               "path": ("ResidentWeight.gemv_peers (row shards, in-kernel all-gather)" if peers is not None else
+               "path": ("ResidentWeight.gemv_peers (row shards, all-gather inside the kernel)" if peers is not None else
                         "ResidentWeight.gemv (module forward path)") +
                        ": pinned x -> H2D, fused kernel, D2H y, every rank",
                "ms_per_step": round(e_max / args.steps, 4)}
@@ -734,7 +734,8 @@ def bench_config(args, shapes, world):
     """The workload description, identical in both arms."""
     tp = world > 1 and args.scaling == "strong"
     par = (f"row-sharded tensor parallel x{world}, all-gather of y "
-           + ("inside the GEMV kernel (NVLink peer stores)" if args.collective == "peer" else "by NCCL")
+           + ("inside the GEMV kernel (epoch-tagged 64-bit stores to every GPU over NVLink)"
+              if args.collective == "peer" else "by NCCL")
            if tp else f"row-shard x{world} (weak: independent replicas)" if world > 1 else "1 GPU")
     return {"workload": workload_name(args, shapes), "batch": args.batch, "format": args.format,
             "parallelism": par, "l2": "inputs larger than L2 (~1 GB of compressed weights per step)"}

@@ -109,14 +109,17 @@ struct GemvParams {
     int64_t ldy;
     int32_t *tile_cnt;  // n_tiles counters, zero between launches
     float *partials;    // scratch: W x 2 x [16][8]
-    // Collective epilogue (nranks > 1): every output is stored to ydst[q] for
-    // each rank q (peer memory over NVLink, ydst[rank] is this GPU's), then the
-    // last warp to finish posts this launch's epoch to flags[q][rank] of every
-    // rank and waits until its own flags[rank][*] all carry it.  state: this
-    // GPU's [finished warps, epoch] words.
-    int nranks, rank;
-    void *ydst[kMaxRanks];
-    uint32_t *flags[kMaxRanks];
+    // Collective epilogue (bf16x_gemv_peers, nranks > 1).  Every output is
+    // sent as one 64-bit word (fp32 bits | launch epoch << 32) to ll[q] of
+    // every rank q: mode 0 (gather) at [b][row0 + row] -- this rank's rows of
+    // the whole [batch][out_total] output; mode 1 (reduce) at
+    // [rank][b][row] -- this rank's partial sums of all out_total rows.  Each
+    // GPU then waits for the words of its own ll[rank] that carry this
+    // launch's epoch and writes y from them (mode 1: the sum over ranks, in
+    // rank order).  state: this GPU's [finished CTAs, epoch of the last launch].
+    int nranks, rank, mode;
+    uint64_t *ll[kMaxRanks];
+    int64_t ll_ld, out_total, row0;
     uint32_t *state;
 };
 
@@ -272,38 +275,64 @@ __device__ __forceinline__ void half_mma2(const StepFrag (&f)[8], const uint16_t
     if constexpr (J + 1 < 8) half_mma2<J + 1>(f, xq, xq2, ce, co, de, dd);
 }
 
-// One output value to every destination: this GPU's y, and with the
-// collective epilogue the same position of every other rank's y.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+
+// One output value (b, row of this launch's rows): into y, or with the
+// collective epilogue into every rank's exchange buffer as one 64-bit word
+// whose high half is the launch epoch -- a single-copy-atomic store, so a
+// reader that sees the epoch sees the value with it, and no fence is needed.
 template <bool COLL>
-__device__ __forceinline__ void store_y(const GemvParams &p, int64_t idx, float o) {
+__device__ __forceinline__ void store_y(const GemvParams &p, int b, int64_t row, float o, uint32_t epoch) {
     if constexpr (!COLL) {
+        const int64_t idx = (int64_t)b * p.ldy + row;
         if (p.y_f32) reinterpret_cast<float *>(p.y)[idx] = o;
         else reinterpret_cast<uint16_t *>(p.y)[idx] = f32_to_bf16_bits_rn(o);
-    } else if (p.y_f32) {
-        for (int q = 0; q < p.nranks; ++q) reinterpret_cast<float *>(p.ydst[q])[idx] = o;
     } else {
-        const uint16_t v = f32_to_bf16_bits_rn(o);
-        for (int q = 0; q < p.nranks; ++q) reinterpret_cast<uint16_t *>(p.ydst[q])[idx] = v;
+        const int64_t w = p.mode == 0 ? (int64_t)b * p.ll_ld + p.row0 + row
+                                      : ((int64_t)p.rank * p.batch + b) * p.ll_ld + row;
+        const uint64_t v = (uint64_t)epoch << 32 | __float_as_uint(o);
+        for (int q = 0; q < p.nranks; ++q) st_relaxed_sys_u64(p.ll[q] + w, v);
     }
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
-}
-
-// End of the collective epilogue, run by every warp of every CTA once its
-// outputs are stored (their peer stores included), the warps that had no
-// items too.  Within the CTA the warps count themselves on a shared-memory
-// word after a CTA-scope fence; the CTA's last warp then makes the CTA's
-// stores visible system-wide (fence.sc.sys, cumulative over what the count
-// ordered before it) and counts the CTA on this GPU's state word.  The grid's
-// last CTA resets the count, advances the epoch, posts it to every rank's
-// flag word for this rank (release at system scope) and waits, bounded,
-// until every rank has posted the same epoch here.  Only then does the kernel
-// complete, so the next kernel of the stream sees all ranks' rows.  A warp
-// that gave up on a wait never counts itself: its CTA never finishes, and the
-// peers' bounded waits time out and report it.
-__device__ __forceinline__ void collective_finish(const GemvParams &p, uint32_t *cta_done, int n_warps, int lane) {
+// End of the collective epilogue, run by every warp of every CTA once it has
+// sent its outputs, the warps that had no items too.  The [batch][out_total]
+// outputs are dealt to all warps of the grid in equal contiguous ranges; a
+// warp waits (bounded) for the words of its range in this GPU's exchange
+// buffer to carry this launch's epoch and writes y from them.  Nothing here
+// waits for anything but words that other warps send unconditionally, so no
+// wait can close a cycle.  The warps then count themselves per CTA and the
+// CTAs per GPU; the GPU's last CTA records the epoch for the next launch
+// (read after griddepcontrol.wait, i.e. after this kernel has completed).
+// A warp that gave up on a wait never counts itself, so the epoch does not
+// advance and the following launches report timeouts until the caller resets
+// the state.
+template <int NW>
+__device__ __forceinline__ void collective_finish(const GemvParams &p, uint32_t *cta_done, int warp, int lane,
+                                                  uint32_t epoch) {
+    const int64_t n_out = (int64_t)p.batch * p.out_total;
+    const int64_t tw = (int64_t)gridDim.x * NW, wi = (int64_t)blockIdx.x * NW + warp;
+    const int64_t o_lo = n_out * wi / tw, o_hi = n_out * (wi + 1) / tw;
+    const uint64_t *mine = p.ll[p.rank];
+    const int nsrc = p.mode == 0 ? 1 : p.nranks;
+    bool ok = true;
+    for (int64_t o = o_lo + lane; o < o_hi; o += 32) {
+        const int b = (int)(o / p.out_total);
+        const int64_t r = o - (int64_t)b * p.out_total;
+        float acc = 0.f;
+        for (int q = 0; q < nsrc; ++q) {
+            const int64_t w = p.mode == 0 ? (int64_t)b * p.ll_ld + r : ((int64_t)q * p.batch + b) * p.ll_ld + r;
+            uint32_t bits = 0;
+            ok = ll_wait(mine + w, epoch, bits) && ok;
+            acc += __uint_as_float(bits);
+        }
+        const int64_t idx = (int64_t)b * p.ldy + r;
+        if (p.y_f32) reinterpret_cast<float *>(p.y)[idx] = acc;
+        else reinterpret_cast<uint16_t *>(p.y)[idx] = f32_to_bf16_bits_rn(acc);
+    }
+    if (!__all_sync(0xffffffffu, ok)) return;
     __syncwarp();
     uint32_t old = 0;
     if (lane == 0) {
@@ -311,22 +340,11 @@ __device__ __forceinline__ void collective_finish(const GemvParams &p, uint32_t 
         old = atomicAdd(cta_done, 1u);
     }
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + 1 != (uint32_t)n_warps) return;
-    uint32_t last = 0;
-    if (lane == 0) {
-        __threadfence_system();
-        last = atomicAdd(p.state, 1u) + 1 == gridDim.x;
-    }
-    if (!__shfl_sync(0xffffffffu, last, 0)) return;
-    __threadfence_system();
-    const uint32_t epoch = p.state[1] + 1u;
-    if (lane == 0) {
+    if (old + 1 != (uint32_t)NW) return;
+    if (lane == 0 && atomicAdd(p.state, 1u) + 1 == gridDim.x) {
         p.state[0] = 0u;
         p.state[1] = epoch;
     }
-    if (lane < p.nranks) st_release_sys(p.flags[lane] + p.rank, epoch);
-    if (lane < p.nranks) peer_flag_wait(p.flags[p.rank] + lane, epoch);
-    __syncwarp();
 }
 
 // Warp w of the partition owns items [T*w/W, T*(w+1)/W); item i belongs to
@@ -359,7 +377,10 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
     const int64_t gw = (int64_t)blockIdx.x * C::kWarps + warp;
     uint32_t *cta_done = reinterpret_cast<uint32_t *>(smem + C::kCtaOff);           // warps of the CTA finished
     if (gw >= p.W) {
-        if constexpr (COLL) collective_finish(p, cta_done, C::kWarps, lane);
+        if constexpr (COLL) {
+            griddep_wait();
+            collective_finish<C::kWarps>(p, cta_done, warp, lane, *reinterpret_cast<volatile uint32_t *>(p.state + 1) + 1u);
+        }
         return;
     }
     if (lane == 0) {
@@ -391,6 +412,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
     int64_t i_it = lo, i_tile = first_tile;
     int i_c = (int)(lo - first_tile * p.nch);
     int32_t nxt_off = 0, nxt_end = 0;
+    uint32_t epoch = 0;                           // collective epilogue only
     auto load_rec = [&]() {
         if (i_it < hi) {
             nxt_off = __ldg(p.ptile_off + i_it);
@@ -424,6 +446,8 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
             if (++cc == p.nch) { cc = 0; ++tl; }
         }
         griddep_wait();
+        // this launch's epoch (the previous launch on this GPU recorded its own)
+        if constexpr (COLL) epoch = *reinterpret_cast<volatile uint32_t *>(p.state + 1) + 1u;
         if constexpr (XRES) {
             if (warp == 0 && lane == 0) {
                 mbar_arrive_expect_tx(xbar, (uint32_t)(p.nch * BMAX * kXRowBytes));
@@ -505,7 +529,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
             const int64_t row = row0 + rr;
             if (b < p.batch && row < p.rows) {
                 if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
-                store_y<COLL>(p, b * p.ldy + row, o);
+                store_y<COLL>(p, b, row, o, epoch);
             }
         }
         if (lane == 0) p.tile_cnt[tl] = 0;
@@ -614,7 +638,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
                     if (b < p.batch && row < p.rows) {
                         float o = v[k];
                         if (p.bias) o += bf16_bits_to_f32(__ldg(p.bias + row));
-                        store_y<COLL>(p, b * p.ldy + row, o);
+                        store_y<COLL>(p, b, row, o, epoch);
                     }
                 }
             } else {
@@ -644,7 +668,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
         if (++s == S) { s = 0; parity ^= 1u; }
         if (++c == p.nch) { c = 0; ++tile; }
     }
-    if constexpr (COLL) collective_finish(p, cta_done, C::kWarps, lane);
+    if constexpr (COLL) collective_finish<C::kWarps>(p, cta_done, warp, lane, epoch);
 }
 
 struct GemvLaunch {
@@ -794,9 +818,9 @@ namespace bf16x {
 // Destinations of the collective epilogue (bf16x_gemv_peers); none for the
 // plain GEMV.
 struct PeerArgs {
-    int nranks, rank;
-    void *const *ydst;
-    uint32_t *const *flags;
+    int nranks, rank, mode;
+    uint64_t *const *ll;
+    int64_t ll_ld, out_total, row0;
     uint32_t *state;
 };
 
@@ -818,17 +842,28 @@ extern "C" int bf16x_gemv(const uint8_t *layout, const int32_t *ptile_off, const
 
 extern "C" int bf16x_gemv_peers(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
                                 int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
-                                const uint16_t *bias, void *const *ydst, int nranks, int rank, int y_dtype,
-                                int64_t ldy, uint32_t *const *flags, uint32_t *state, int32_t *tile_counters,
-                                void *scratch, int64_t scratch_bytes, void *stream) {
-    if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks)
-        return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: need 1 <= nranks <= %d and 0 <= rank < nranks", kMaxRanks);
-    if (!ydst || !flags || !state) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: null destination table");
-    for (int q = 0; q < nranks; ++q)
-        if (!ydst[q] || !flags[q]) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: null pointer for rank %d", q);
-    if (rows <= 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: every rank needs rows (its peers wait for it)");
-    const PeerArgs pa{nranks, rank, ydst, flags, state};
-    return gemv_impl(layout, ptile_off, precs, rows, in_f, x, batch, ldx, bias, ydst[rank], y_dtype, ldy,
+                                const uint16_t *bias, int mode, uint64_t *const *ll, int64_t ll_ld,
+                                int64_t out_total, int64_t row0, int nranks, int rank, void *y, int y_dtype,
+                                int64_t ldy, uint32_t *state, int32_t *tile_counters, void *scratch,
+                                int64_t scratch_bytes, void *stream) {
+    if (nranks < 2 || nranks > kMaxRanks || rank < 0 || rank >= nranks)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: need 2 <= nranks <= %d and 0 <= rank < nranks", kMaxRanks);
+    if (mode != 0 && mode != 1) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: mode must be 0 (gather) or 1 (reduce)");
+    if (!ll || !state || !y) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: null exchange table, state or y");
+    for (int q = 0; q < nranks; ++q) {
+        if (!ll[q]) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: null exchange buffer for rank %d", q);
+        if (reinterpret_cast<uintptr_t>(ll[q]) & 7u)
+            return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: exchange buffers must be 8-byte aligned");
+    }
+    if (rows <= 0) return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: every rank needs rows (its peers wait for its words)");
+    if (mode == 0 && (row0 < 0 || row0 + rows > out_total))
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: rows [row0, row0+rows) outside 0..out_total");
+    if (mode == 1 && (rows != out_total || row0 != 0))
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: reduce mode takes every output row (rows == out_total, row0 == 0)");
+    if (ll_ld < out_total || ldy < out_total)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gemv_peers: ll_ld and ldy must be >= out_total");
+    const PeerArgs pa{nranks, rank, mode, ll, ll_ld, out_total, row0, state};
+    return gemv_impl(layout, ptile_off, precs, rows, in_f, x, batch, ldx, bias, y, y_dtype, ldy,
                      tile_counters, scratch, scratch_bytes, stream, &pa);
 }
 
@@ -851,7 +886,7 @@ static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: ldx must be a multiple of 8 and >= %lld (zero padded)", (long long)in_pad);
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(layout) | reinterpret_cast<uintptr_t>(precs)) & 15u)
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: x, layout and records must be 16-byte aligned");
-    if (ldy < rows) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: ldy < rows");
+    if (ldy < rows && !peers) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: ldy < rows");
     const int nw = warps_for(batch, rows, in_f);
     const GemvLaunch L = plan_gemv(rows, in_f, nw);
     if (!tile_counters) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: tile_counters (ceil(rows/16) zeroed int32) missing");
@@ -878,15 +913,15 @@ static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint
     p.partials = static_cast<float *>(scratch);
     p.nranks = 1;
     p.rank = 0;
-    p.ydst[0] = y;
     p.state = nullptr;
     if (peers) {
         p.nranks = peers->nranks;
         p.rank = peers->rank;
-        for (int q = 0; q < peers->nranks; ++q) {
-            p.ydst[q] = peers->ydst[q];
-            p.flags[q] = peers->flags[q];
-        }
+        p.mode = peers->mode;
+        for (int q = 0; q < peers->nranks; ++q) p.ll[q] = peers->ll[q];
+        p.ll_ld = peers->ll_ld;
+        p.out_total = peers->out_total;
+        p.row0 = peers->row0;
         p.state = peers->state;
     }
     cudaStream_t st = (cudaStream_t)stream;

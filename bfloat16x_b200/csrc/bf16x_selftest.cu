@@ -12,8 +12,9 @@ namespace bf16x {
 
 // which: 0 = mbar_wait (the GEMV's ring slots), 1 = role_wait (the tcgen05
 // GEMMs' warp roles), 2 = counter_wait (the slab GEMM's cross-CTA counters),
-// 3 = peer_flag_wait (the collective GEMV epilogue).  The mbarrier is fresh,
-// so its phase 0 never completes; the flag is `*flag`, waited on to reach 1.
+// 3 = ll_wait (the collective GEMV epilogue's exchange words).  The mbarrier
+// is fresh, so its phase 0 never completes; 2 waits for the u32 `*flag` to
+// reach 1, 3 for the 64-bit word at `flag` to carry epoch 1 in its high half.
 // result[0] = 1 if the wait gave up, result[1] = the abort flag afterwards,
 // result[2] = microseconds spent waiting.
 __global__ void selftest_wait_kernel(int which, uint64_t limit_ns, const uint32_t *flag, int32_t *result) {
@@ -31,7 +32,10 @@ __global__ void selftest_wait_kernel(int which, uint64_t limit_ns, const uint32_
     if (which == 0) ok = mbar_wait(&bar, 0u, &g_status, limit_ns);
     else if (which == 1) ok = role_wait(&bar, 0u, &abort_flag, limit_ns);
     else if (which == 2) ok = counter_wait(flag, 1u, &abort_flag, limit_ns);
-    else ok = peer_flag_wait(flag, 1u, limit_ns);
+    else {
+        uint32_t data = 0;
+        ok = ll_wait(reinterpret_cast<const uint64_t *>(flag), 1u, data, limit_ns);
+    }
     result[0] = ok ? 0 : 1;
     result[1] = abort_flag;
     result[2] = (int32_t)((globaltimer_ns() - t0) / 1000u);

@@ -70,15 +70,27 @@ __device__ __forceinline__ bool counter_wait(const uint32_t *ctr, uint32_t targe
     }
 }
 
-// The same for a flag another GPU writes over NVLink (system scope).
-__device__ __forceinline__ bool peer_flag_wait(const uint32_t *flag, uint32_t target, uint64_t limit_ns = kWaitLimitNs) {
-    if ((int32_t)(ld_acquire_sys(flag) - target) >= 0) return true;
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Wait until the 64-bit exchange word *w (written by this or another GPU in
+// one single-copy-atomic store: data in the low half, launch epoch in the
+// high half) carries `epoch`; *data gets its low half.  Bounded like the others.
+__device__ __forceinline__ bool ll_wait(const uint64_t *w, uint32_t epoch, uint32_t &data,
+                                        uint64_t limit_ns = kWaitLimitNs) {
+    uint64_t v = ld_relaxed_sys_u64(w);
+    if ((uint32_t)(v >> 32) == epoch) { data = (uint32_t)v; return true; }
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         __nanosleep(32);
-        if ((int32_t)(ld_acquire_sys(flag) - target) >= 0) return true;
+        v = ld_relaxed_sys_u64(w);
+        if ((uint32_t)(v >> 32) == epoch) { data = (uint32_t)v; return true; }
         if ((i & 15u) == 0 && globaltimer_ns() - t0 > limit_ns) {
             atomicOr(&g_status, kErrWaitTimeout);
+            data = 0u;
             return false;
         }
     }

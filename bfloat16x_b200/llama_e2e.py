@@ -94,9 +94,9 @@ class ColumnShard(nn.Module):
     """The input-column slice of a linear: this rank's partial outputs,
     summed over the group.  By default an fp32 NCCL all-reduce; once packed
     and given a PeerGroup (``use_peer_collectives``), up to 16 tokens take the
-    fused decode+GEMV that stores the fp32 partials into this rank's slot of
-    every rank's slot array over NVLink, and the slots are summed in rank
-    order (the same sum on every rank)."""
+    fused decode+GEMV that sends the fp32 partials to this rank's slot of
+    every rank's exchange buffer over NVLink and sums the slots in rank order
+    (the same sum on every rank) inside the same kernel."""
 
     def __init__(self, lin: nn.Module, group=None, tp: int = 1):
         super().__init__()
@@ -107,18 +107,14 @@ class ColumnShard(nn.Module):
         self.peers = peers
         self.max_batch = max_batch
         self.out_f = self.lin.out_features
-        self._slot = max_batch * self.out_f * 4
-        self._soff = peers.alloc(peers.world * self._slot)
+        self._lloff = peers.alloc(peers.world * max_batch * self.out_f * 8)
+        self._y = torch.empty((max_batch, self.out_f), dtype=torch.bfloat16, device=peers.device)
 
     def forward(self, x):
         if self.peers is not None and x.numel() // x.shape[-1] <= self.max_batch:
             x2 = x.reshape(-1, x.shape[-1])
-            B = x2.shape[0]
-            pg = self.peers
-            self.lin.rw.gemv_peers(x2, pg, self._soff + pg.rank * self._slot, self.out_f, 0,
-                                   out_dtype=torch.float32)
-            slots = pg.local(self._soff, (pg.world, self.max_batch, self.out_f), torch.float32)[:, :B]
-            return slots.sum(0).to(x.dtype).reshape(*x.shape[:-1], self.out_f)
+            y = self.lin.rw.gemv_peers(x2, self.peers, self._lloff, self.out_f, self._y, mode=1)
+            return y.to(x.dtype).reshape(*x.shape[:-1], self.out_f)
         y = self.lin(x)
         if self.tp == 1:
             return y
@@ -141,14 +137,14 @@ class VocabShard(nn.Module):
         stored into every rank's logits buffer over NVLink)."""
         self.peers = peers
         self.max_batch = max_batch
-        self._off = peers.alloc(max_batch * self.vocab * 2)
+        self._lloff = peers.alloc(max_batch * self.vocab * 8)
+        self._y = torch.empty((max_batch, self.vocab), dtype=torch.bfloat16, device=peers.device)
 
     def forward(self, x):
         if self.peers is not None and x.numel() // x.shape[-1] <= self.max_batch:
             x2 = x.reshape(-1, x.shape[-1])
             pg = self.peers
-            self.lin.rw.gemv_peers(x2, pg, self._off, self.vocab, pg.rank * self.piece)
-            y = pg.local(self._off, (self.max_batch, self.vocab), torch.bfloat16)[:x2.shape[0]]
+            y = self.lin.rw.gemv_peers(x2, pg, self._lloff, self.vocab, self._y, mode=0, row0=pg.rank * self.piece)
             return y.reshape(*x.shape[:-1], self.vocab)
         y = self.lin(x)
         if self.tp == 1:
@@ -334,8 +330,8 @@ def use_peer_collectives(model: LlamaModel, peers) -> None:
 def peer_heap_bytes(model: LlamaModel) -> int:
     """PeerGroup heap that use_peer_collectives carves for ``model``."""
     cfg, B, tp = model.cfg, max(model.batch, 1), model.tp
-    per_layer = 2 * (tp * B * cfg.hidden * 4 + 256)
-    return cfg.layers * per_layer + B * cfg.vocab * 2 + (1 << 20)
+    per_layer = 2 * (tp * B * cfg.hidden * 8 + 256)
+    return cfg.layers * per_layer + B * cfg.vocab * 8 + (1 << 20)
 
 
 class GraphDecoder:

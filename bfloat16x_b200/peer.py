@@ -1,16 +1,16 @@
 """Device memory shared over NVLink by the ranks of one node, for the fused
-decode+GEMV whose epilogue stores every output row straight into every
-rank's output buffer (``bf16x_gemv_peers``): the row-sharded layer's
-all-gather happens inside the kernel instead of in a separate NCCL call.
+decode+GEMV whose epilogue sends every output straight into every rank's
+exchange buffer (``bf16x_gemv_peers``): the row-sharded layer's all-gather,
+or the column-sharded layer's all-reduce, happens inside the kernel instead
+of in a separate NCCL call.
 
 ``PeerGroup`` is collective: every rank of the process group builds one with
 the same heap size.  Each rank allocates one device buffer, exports it
 (CUDA IPC), exchanges the handles over the process group's host side
 (``all_gather_object``) and maps every peer's buffer.  The buffer holds a
-header -- this rank's launch state (finished-warp count, epoch) and one flag
-word per rank, written by the peers -- followed by a heap carved out by
-``alloc`` at the same offsets on every rank, so an offset names "the same"
-buffer everywhere.
+header -- this rank's launch state (finished-CTA count, epoch of the last
+launch) -- followed by a zeroed heap carved out by ``alloc`` at the same
+offsets on every rank, so an offset names "the same" buffer everywhere.
 
 Rules the kernels rely on (each stated where it is enforced):
 * the collective GEMVs of one group run in the same order on every rank, on
@@ -19,7 +19,7 @@ Rules the kernels rely on (each stated where it is enforced):
   very next one (consecutive layers use different buffers), so a rank that
   runs ahead never overwrites rows another rank is still reading;
 * after a device error (a timed-out wait), ``reset`` clears the state and
-  flags on every rank before the group is used again.
+  the heap on every rank before the group is used again.
 """
 from __future__ import annotations
 
@@ -31,8 +31,7 @@ import torch.distributed as dist
 from . import _lib
 from ._lib import call
 
-HEADER_BYTES = 4096          # state (2 words) at 0, flags (one word per rank) at FLAGS_OFF
-FLAGS_OFF = 256
+HEADER_BYTES = 4096          # state (2 words) at 0
 ALIGN = 256
 MAX_RANKS = 8
 
@@ -83,7 +82,6 @@ class PeerGroup:
             self._imported = []
             raise _lib.Bf16xError(f"PeerGroup: a rank could not map its peers' buffers: {next(e for e in errs if e)}")
         self._next = HEADER_BYTES
-        self._flag_table = (ctypes.c_void_p * self.world)(*[p + FLAGS_OFF for p in self.ptrs])
         self._sync()
         dist.barrier(group=group)
 
@@ -135,19 +133,15 @@ class PeerGroup:
         return (ctypes.c_void_p * self.world)(*[p + offset for p in self.ptrs])
 
     @property
-    def flag_table(self):
-        return self._flag_table
-
-    @property
     def state_ptr(self) -> int:
         return self.ptrs[self.rank]
 
     # ---- lifetime ----------------------------------------------------------
     def reset(self) -> None:
-        """Zero this rank's state and flags, collectively (after a device error)."""
+        """Zero this rank's state and heap, collectively (after a device error)."""
         self._sync()
         dist.barrier(group=self.group)
-        self.buf[:HEADER_BYTES].zero_()
+        self.buf.zero_()
         self._sync()
         dist.barrier(group=self.group)
 
@@ -162,4 +156,4 @@ class PeerGroup:
         dist.barrier(group=self.group)
 
 
-__all__ = ["PeerGroup", "HEADER_BYTES", "FLAGS_OFF"]
+__all__ = ["PeerGroup", "HEADER_BYTES"]

@@ -236,35 +236,42 @@ class ResidentWeight:
                  self._stream())
         return out
 
-    def gemv_peers(self, x: torch.Tensor, peers, offset: int, ldy: int, col0: int,
-                   bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16) -> None:
-        """The fused decode+GEMV of this rank's rows whose epilogue stores
-        every output straight into every rank's copy of the PeerGroup heap
-        buffer at ``offset`` ([batch][ldy] of out_dtype, this shard's rows at
-        columns col0..col0+rows): the row-sharded layer's all-gather happens
-        inside the kernel, over NVLink.  The kernel completes once every
-        rank's rows have arrived here."""
+    def gemv_peers(self, x: torch.Tensor, peers, ll_offset: int, out_total: int, y: torch.Tensor,
+                   mode: int = 0, row0: int = 0, bias: torch.Tensor | None = None) -> torch.Tensor:
+        """The fused decode+GEMV of this rank's weight whose epilogue does the
+        tensor-parallel exchange over NVLink (``bf16x_gemv_peers``): every
+        output goes, tagged with the launch's epoch, to the PeerGroup heap
+        buffer at ``ll_offset`` of every rank, and each GPU builds ``y``
+        ([batch, >= out_total], bf16 or fp32, this GPU's) from the words of
+        its own copy.  mode 0: this weight is rows [row0, row0 + rows) of an
+        out_total-row weight and y gets all rows (all-gather); mode 1: this
+        weight is an input-column slice with every row (rows == out_total)
+        and y gets the sum of all ranks' partials (all-reduce).  The heap
+        buffer holds batch * out_total 64-bit words (mode 1: world times
+        that); consecutive calls of a group must use different buffers."""
         _lib.require_cuda(x, "x")
         x2 = x.reshape(-1, self.in_f)
         B = x2.shape[0]
         if B < 1 or B > GEMV_MAX_BATCH:
             raise ValueError(f"gemv takes 1..{GEMV_MAX_BATCH} rows of activations, got {B}")
+        if y.dim() != 2 or y.shape[0] < B or y.shape[1] < out_total or y.stride(1) != 1:
+            raise ValueError(f"y must be [>= {B}, >= {out_total}] with unit column stride")
         xp = self._prep_x(x2)
-        ydt = {torch.bfloat16: BF16X_DTYPE_BF16, torch.float32: BF16X_DTYPE_F32}[out_dtype]
-        esize = 2 if out_dtype == torch.bfloat16 else 4
+        ydt = {torch.bfloat16: BF16X_DTYPE_BF16, torch.float32: BF16X_DTYPE_F32}[y.dtype]
         b = None if bias is None else bias.to(device=self.device, dtype=torch.bfloat16).contiguous()
-        key = (offset, col0, esize)
         tables = getattr(self, "_peer_tables", None)
-        if tables is None or tables[0] != (id(peers), key):
-            tables = ((id(peers), key), peers.table(offset + col0 * esize))
+        if tables is None or tables[0] != (id(peers), ll_offset):
+            tables = ((id(peers), ll_offset), peers.table(ll_offset))
             self._peer_tables = tables
         with torch.cuda.device(self.device):
             if self._scratch_need is None:
                 self._scratch_need = int(_lib.lib().bf16x_gemv_scratch_bytes(self.rows, self.in_f))
             ws = gemv_scratch(self.device, self._scratch_need)
             call("bf16x_gemv_peers", ptr(self.layout), ptr(self.ptile_off), ptr(self.precs), self.rows, self.in_f,
-                 ptr(xp), B, xp.stride(0), ptr(b), tables[1], peers.world, peers.rank, ydt, int(ldy),
-                 peers.flag_table, peers.state_ptr, ptr(self.tile_counters), ptr(ws), ws.numel(), self._stream())
+                 ptr(xp), B, xp.stride(0), ptr(b), int(mode), tables[1], int(out_total), int(out_total), int(row0),
+                 peers.world, peers.rank, ptr(y), ydt, y.stride(0), peers.state_ptr, ptr(self.tile_counters),
+                 ptr(ws), ws.numel(), self._stream())
+        return y[:B]
 
     def gemm(self, x: torch.Tensor, bias: torch.Tensor | None = None,
              out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -103,11 +103,10 @@ class RowParallelBf16x(RowParallel):
     """Rows [r0, r1) of a BF16X dict resident on this rank's GPU.
 
     With ``peers`` (a PeerGroup over the same ranks), up to 16 rows of
-    activations take the fused decode+GEMV whose epilogue stores each rank's
-    output rows into every rank's output buffer over NVLink
-    (``ResidentWeight.gemv_peers``): no separate all-gather.  The result is
-    then a view of this rank's copy of that buffer, valid until the layer's
-    next call; more rows take the GEMM and NCCL."""
+    activations take the fused decode+GEMV whose epilogue sends each rank's
+    output rows to every rank over NVLink and assembles the full output on
+    each (``ResidentWeight.gemv_peers``, mode 0): no separate all-gather.
+    More rows take the GEMM and NCCL."""
 
     def __init__(self, packed: dict, bias: torch.Tensor | None = None, group=None, gather: bool = True,
                  device=None, peers=None, max_batch: int = 16):
@@ -135,9 +134,9 @@ class RowParallelBf16x(RowParallel):
             if any(h <= l for l, h in self.bounds):
                 raise ValueError("the in-kernel all-gather needs rows on every rank (out_f >= 16 * world)")
             self.max_batch = int(max_batch)
-            # two buffers used alternately: a call never rewrites the rows the
-            # previous call of this layer returned while a peer may read them
-            self._yoff = [peers.alloc(self.max_batch * out_f * 4) for _ in range(2)]
+            # two exchange buffers used alternately, so consecutive calls of
+            # this layer never share one (the rule of bf16x_gemv_peers)
+            self._lloff = [peers.alloc(self.max_batch * out_f * 8) for _ in range(2)]
             self._turn = 0
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -148,10 +147,11 @@ class RowParallelBf16x(RowParallel):
         if B > self.max_batch:
             return super().forward(x)
         od = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.bfloat16
-        off = self._yoff[self._turn]
+        off = self._lloff[self._turn]
         self._turn ^= 1
-        self.resident.gemv_peers(x2, self.peers, off, self.out_f, self.rows[0], bias=self._bias, out_dtype=od)
-        return self.peers.local(off, (B, self.out_f), od).reshape(*x.shape[:-1], self.out_f)
+        y = torch.empty((B, self.out_f), dtype=od, device=x.device)
+        self.resident.gemv_peers(x2, self.peers, off, self.out_f, y, mode=0, row0=self.rows[0], bias=self._bias)
+        return y.reshape(*x.shape[:-1], self.out_f)
 
 
 class ColumnParallelBf16x(ColumnParallel):
@@ -159,10 +159,10 @@ class ColumnParallelBf16x(ColumnParallel):
     The bias, if any, is added once after the reduction.
 
     With ``peers``, up to 16 rows of activations take the fused decode+GEMV
-    whose epilogue stores this rank's fp32 partial outputs into its slot of
-    every rank's slot array over NVLink; the kernel completes once all
-    partials are in, and the sum over the slots (rank order, the same on
-    every rank) replaces the NCCL all-reduce."""
+    whose epilogue sends this rank's fp32 partial outputs to its slot of every
+    rank's exchange buffer over NVLink, and each rank sums the slots in rank
+    order (the same sum everywhere) inside the same kernel: no NCCL
+    all-reduce (``ResidentWeight.gemv_peers``, mode 1)."""
 
     def __init__(self, weight: torch.Tensor, bias: torch.Tensor | None = None, group=None,
                  input_is_sharded: bool = False, device=None, peers=None, max_batch: int = 16):
@@ -186,20 +186,18 @@ class ColumnParallelBf16x(ColumnParallel):
         if self.peers is not None:
             self.max_batch = int(max_batch)
             self.out_f = int(weight.shape[0])
-            self._slot = self.max_batch * self.out_f * 4
-            self._soff = [peers.alloc(world * self._slot) for _ in range(2)]
+            self._lloff = [peers.alloc(world * self.max_batch * self.out_f * 8) for _ in range(2)]
             self._turn = 0
 
     def _peer_sum(self, x: torch.Tensor) -> torch.Tensor:
         xs = x if self.input_is_sharded else x[..., self.c0:self.c1]
         x2 = xs.reshape(-1, xs.shape[-1]).contiguous()
         B = x2.shape[0]
-        off = self._soff[self._turn]
+        off = self._lloff[self._turn]
         self._turn ^= 1
-        self.resident.gemv_peers(x2, self.peers, off + self.rank * self._slot, self.out_f, 0,
-                                 out_dtype=torch.float32)
-        slots = self.peers.local(off, (self.world, self.max_batch, self.out_f), torch.float32)[:, :B]
-        return slots.sum(0).reshape(*x.shape[:-1], self.out_f)
+        y = torch.empty((B, self.out_f), dtype=torch.float32, device=x2.device)
+        self.resident.gemv_peers(x2, self.peers, off, self.out_f, y, mode=1)
+        return y.reshape(*x.shape[:-1], self.out_f)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.peers is not None and x.numel() // x.shape[-1] <= self.max_batch:

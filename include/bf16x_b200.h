@@ -171,27 +171,36 @@ int bf16x_gemv_noalloc(const uint8_t *layout, const int32_t *ptile_off, const ui
                        const uint16_t *x, int64_t batch, int64_t ldx,
                        const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *stream);
 
-/* ---- tensor parallel over NVLink: GEMV with the all-gather inside -------- */
-/* The row-sharded layer of tensor parallelism (each of nranks GPUs of one
- * node holds rows of the weight) needs every rank's output rows on
- * every rank.  The reference has no multi-GPU path; this replaces
- * bf16x_fused_gemv (bf16x_fused.py:114-127) + a separate all-gather.
- * bf16x_gemv_peers is bf16x_gemv whose epilogue stores each output to
- * ydst[q] + b*ldy + row for every rank q (ydst: host array of nranks device
- * pointers, ydst[rank] on this GPU, the others peer memory mapped with
- * bf16x_peer_import), then the last warp posts the launch's epoch to
- * flags[q][rank] for every q and waits (bounded) until flags[rank][0..nranks)
- * all carry it: the kernel completes only once every rank's rows are here.
- * state: this GPU's two zeroed u32 words (finished warps, epoch), shared by
- * the collective GEMVs of one group, which must run in the same order on
- * every rank, on one stream each.  flags: host array of nranks device
- * pointers to each rank's nranks zeroed u32 flag words.  nranks <= 8,
- * rows >= 1 on every rank. */
+/* ---- tensor parallel over NVLink: GEMV with the exchange inside -------- */
+/* Tensor parallelism over the nranks GPUs of one node (2..8).  The reference
+ * has no multi-GPU path; this replaces bf16x_fused_gemv
+ * (bf16x_fused.py:114-127) followed by a separate all-gather or all-reduce.
+ * bf16x_gemv_peers is bf16x_gemv whose epilogue sends every output, as one
+ * 64-bit word (fp32 bits | launch epoch << 32, a single-copy-atomic store, so
+ * no fence or flag is needed), to ll[q] of every rank q (ll: host array of
+ * nranks device pointers, 8-byte aligned, ll[rank] on this GPU, the others
+ * peer memory mapped with bf16x_peer_import):
+ *   mode 0 (gather, row-sharded weight): this rank holds rows
+ *     [row0, row0 + rows) of an out_total-row weight; words go to
+ *     ll[q][b * ll_ld + row0 + row];
+ *   mode 1 (reduce, column-sharded weight): rows == out_total, row0 == 0;
+ *     this rank's partial sums go to ll[q][(rank * batch + b) * ll_ld + row].
+ * Every GPU then waits (bounded) for the words of its own ll[rank] that carry
+ * this launch's epoch and writes y [batch][ldy] (y_dtype, ldy >= out_total):
+ * the gathered rows, or the sum of the partials in rank order.  The kernel
+ * completes once y is whole.  The exchange buffers must start zeroed
+ * (batch * ll_ld words, mode 1: nranks * batch * ll_ld); the launch epoch
+ * lives in state (this GPU's two zeroed u32 words), shared by the collective
+ * GEMVs of one group, which must run in the same order on every rank, on one
+ * stream each; a buffer used by one launch must not be used by the next one.
+ * Every rank needs rows >= 1.  bias applies to this rank's rows (give NULL in
+ * mode 1 and add it once after). */
 int bf16x_gemv_peers(const uint8_t *layout, const int32_t *ptile_off, const uint32_t *precs,
                      int64_t rows, int64_t in_f, const uint16_t *x, int64_t batch, int64_t ldx,
-                     const uint16_t *bias, void *const *ydst, int nranks, int rank, int y_dtype,
-                     int64_t ldy, uint32_t *const *flags, uint32_t *state, int32_t *tile_counters,
-                     void *scratch, int64_t scratch_bytes, void *stream);
+                     const uint16_t *bias, int mode, uint64_t *const *ll, int64_t ll_ld,
+                     int64_t out_total, int64_t row0, int nranks, int rank, void *y, int y_dtype,
+                     int64_t ldy, uint32_t *state, int32_t *tile_counters, void *scratch,
+                     int64_t scratch_bytes, void *stream);
 
 /* CUDA IPC plumbing for the peer pointers above (no counterpart in the
  * reference).  bf16x_peer_export: the IPC handle (bf16x_peer_handle_bytes()
@@ -260,9 +269,11 @@ int bf16x_gguf_apply_ovf(void *y, int y_dtype, int64_t rows, int64_t cols, const
 /* ---- self-test of the bounded waits ------------------------------------- */
 /* No counterpart in the reference.  Runs one of the library's bounded device
  * waits -- which: 0 the GEMV's mbarrier wait, 1 the tcgen05 GEMM roles' wait,
- * 2 the slab GEMM's cross-CTA counter wait, 3 the collective GEMV's peer-flag
- * wait -- against a fresh mbarrier that nothing completes (0, 1) or until
- * *flag (device u32) reaches 1, with a limit of limit_ns (1 us .. 100 ms).
+ * 2 the slab GEMM's cross-CTA counter wait, 3 the collective GEMV's wait for
+ * its exchange words -- against a fresh mbarrier that nothing completes (0, 1), until the
+ * u32 *flag reaches 1 (2), or until the 64-bit word at flag (8-byte aligned)
+ * carries epoch 1 in its high half (3), with a limit of limit_ns (1 us ..
+ * 100 ms).
  * result (device int32[3]): gave up (1/0), abort flag raised (1/0),
  * microseconds waited.  A wait that gives up sets the wait-timeout bit read by
  * bf16x_device_status; the kernel returns and the context stays usable. */

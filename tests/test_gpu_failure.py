@@ -1,7 +1,8 @@
 """Failure path of the bounded device waits, without faulting or hanging the
 GPU: each of the library's waits (the GEMV's mbarrier wait, the tcgen05 GEMM
 roles' wait, the slab GEMM's cross-CTA counter wait, the collective GEMV's
-peer-flag wait) is run by bf16x_selftest_wait against a barrier or flag that
+wait for its exchange words) is run by bf16x_selftest_wait against a barrier,
+flag or word that
 nothing completes, with a 100 us limit.  The wait must give up, the kernel
 must return, the wait-timeout bit must reach bf16x_device_status, and the
 next fused GEMV on the same context must be correct."""
@@ -20,7 +21,9 @@ WAIT_TIMEOUT_BIT = 1
 
 
 def _run(which, flag_value):
-    flag = torch.full((1,), flag_value, dtype=torch.int32, device="cuda")
+    # words 0..1: the u32 flag of wait 2, and the 64-bit exchange word of wait
+    # 3 whose high half is the epoch it waits for (1)
+    flag = torch.tensor([flag_value, flag_value], dtype=torch.int32, device="cuda")
     res = torch.full((3,), -1, dtype=torch.int32, device="cuda")
     call("bf16x_selftest_wait", which, LIMIT_NS, ptr(flag), ptr(res), torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()

@@ -115,6 +115,7 @@ def _peer_worker(rank, world, port, q):
         import torch.distributed as dist
 
         from bfloat16x_b200 import _lib
+        from bfloat16x_b200.opqk_linear import bf16x_quantize
         from bfloat16x_b200.peer import PeerGroup
         from bfloat16x_b200.resident import ResidentWeight
         from bfloat16x_b200.synthetic import synthetic_activation, synthetic_weight
@@ -127,27 +128,38 @@ def _peer_worker(rank, world, port, q):
         os.environ["NCCL_NVLS_ENABLE"] = "0"
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=dev)
-        pg = PeerGroup(None, dev, heap_bytes=8 << 20)
+        pg = PeerGroup(None, dev, heap_bytes=32 << 20)
         res = []
+        # mode 0: row shards, every rank assembles all rows
         for (out_f, in_f), B, dt in [((1000, 2048), 1, torch.float32), ((4096, 4096), 8, torch.bfloat16),
-                                     ((300, 1536), 3, torch.float32)]:
+                                     ((300, 1536), 3, torch.float32), ((2048, 1024), 16, torch.bfloat16)]:
             w = synthetic_weight(out_f, in_f, seed=out_f)
-            wb = bits_of(w)
             r0, r1 = shard_bounds(out_f, world, rank, 16)
-            rw = ResidentWeight.from_packed(oracle_dict(wb), device=dev, row_range=(r0, r1))
-            off = [pg.alloc(B * out_f * 4), pg.alloc(B * out_f * 4)]      # two buffers, used alternately
-            ref = (x_ := synthetic_activation(B, in_f, seed=B)).float() @ w.float().T
+            rw = ResidentWeight.from_packed(oracle_dict(bits_of(w)), device=dev, row_range=(r0, r1))
+            bufs = [pg.alloc(B * out_f * 8) for _ in range(2)]       # used alternately
+            x = synthetic_activation(B, in_f, seed=B)
+            ref = x.float() @ w.float().T
+            ref_c = ref if dt == torch.float32 else ref.to(torch.bfloat16).float()
             for it in range(4):
-                buf = off[it % 2]
-                yv = pg.local(buf, (B, out_f), dt)
-                yv.fill_(float("nan"))
-                dist.barrier()
-                rw.gemv_peers(x_.to(dev), pg, buf, out_f, r0, out_dtype=dt)
+                y = torch.full((B, out_f), float("nan"), dtype=dt, device=dev)
+                rw.gemv_peers(x.to(dev), pg, bufs[it % 2], out_f, y, mode=0, row0=r0)
                 torch.cuda.synchronize()
-                ref_c = ref if dt == torch.float32 else ref.to(torch.bfloat16).float()
-                got = yv.float().cpu()
+                got = y.float().cpu()
                 res.append(bool(torch.isfinite(got).all()) and rel_l2(got.numpy(), ref_c.numpy()) < 1e-3)
-                dist.barrier()
+            _lib.check_device_status(rank)
+        # mode 1: column shards, every rank gets the sum of all partials
+        for (out_f, in_f), B in [((1000, 2048), 1), ((4096, 4096), 5)]:
+            w = synthetic_weight(out_f, in_f, seed=in_f + 1)
+            c0, c1 = shard_bounds(in_f, world, rank, 256)
+            rw = ResidentWeight.from_packed(bf16x_quantize(w[:, c0:c1].contiguous().to(dev), device=dev), device=dev)
+            bufs = [pg.alloc(world * B * out_f * 8) for _ in range(2)]
+            x = synthetic_activation(B, in_f, seed=B + 3)
+            ref = x.float() @ w.float().T
+            for it in range(3):
+                y = torch.empty((B, out_f), dtype=torch.float32, device=dev)
+                rw.gemv_peers(x[:, c0:c1].contiguous().to(dev), pg, bufs[it % 2], out_f, y, mode=1)
+                torch.cuda.synchronize()
+                res.append(rel_l2(y.cpu().numpy(), ref.numpy()) < 1e-3)
             _lib.check_device_status(rank)
         # the same launches captured in a CUDA graph and replayed: the epoch
         # lives in device memory, so replays keep the ranks in step
@@ -156,46 +168,44 @@ def _peer_worker(rank, world, port, q):
         r0, r1 = shard_bounds(out_f, world, rank, 16)
         rw = ResidentWeight.from_packed(oracle_dict(bits_of(w)), device=dev, row_range=(r0, r1))
         x = synthetic_activation(B, in_f, seed=5).to(dev)
-        bufs = [pg.alloc(B * out_f * 2) for _ in range(2)]
+        bufs = [pg.alloc(B * out_f * 8) for _ in range(2)]
+        ys = [torch.zeros((B, out_f), dtype=torch.bfloat16, device=dev) for _ in range(2)]
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
-            for bo in bufs:
-                rw.gemv_peers(x, pg, bo, out_f, r0)
+            for bo, yo in zip(bufs, ys):
+                rw.gemv_peers(x, pg, bo, out_f, yo, mode=0, row0=r0)
             torch.cuda.synchronize(dev)
             dist.barrier()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=s):
-                for bo in bufs:
-                    rw.gemv_peers(x, pg, bo, out_f, r0)
+                for bo, yo in zip(bufs, ys):
+                    rw.gemv_peers(x, pg, bo, out_f, yo, mode=0, row0=r0)
         torch.cuda.synchronize(dev)
         dist.barrier()
         ref = (x.float().cpu() @ w.float().T).to(torch.bfloat16).float()
         for _ in range(5):
-            for bo in bufs:
-                pg.local(bo, (B, out_f), torch.bfloat16).zero_()
+            for yo in ys:
+                yo.zero_()
             torch.cuda.synchronize(dev)
-            dist.barrier()
             g.replay()
             torch.cuda.synchronize(dev)
-            for bo in bufs:
-                got = pg.local(bo, (B, out_f), torch.bfloat16).float().cpu()
-                res.append(rel_l2(got.numpy(), ref.numpy()) < 1e-3)
-            dist.barrier()
+            for yo in ys:
+                res.append(rel_l2(yo.float().cpu().numpy(), ref.numpy()) < 1e-3)
         _lib.check_device_status(rank)
         del g
         pg.close()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, all(res), res))
-    except Exception as e:
+    except Exception:
         import traceback
         q.put((rank, False, traceback.format_exc()))
 
 
-# The row-sharded GEMV whose epilogue writes every rank's output rows into
-# every rank's buffer over NVLink (bf16x_gemv_peers): the full output on each
-# rank against the unsharded product, eager and replayed from a CUDA graph.
+# The GEMV whose epilogue exchanges outputs over NVLink (bf16x_gemv_peers):
+# row shards gathered and column-shard partials summed on every rank, against
+# the unsharded product, eager and replayed from a CUDA graph.
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_gemv_peers_allgather_2gpu():
     world = 2

@@ -76,7 +76,7 @@ def _peer_worker(rank, world, port, q, fail_rank):
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world)
         from bfloat16x_b200 import _lib
-        from bfloat16x_b200.peer import FLAGS_OFF, HEADER_BYTES, PeerGroup
+        from bfloat16x_b200.peer import HEADER_BYTES, PeerGroup
 
         closed = []
 
@@ -100,7 +100,7 @@ def _peer_worker(rank, world, port, q, fail_rank):
         a, b = pg.alloc(100), pg.alloc(3000)
         ok += [a == HEADER_BYTES, b == HEADER_BYTES + 256, b % 256 == 0]
         t = pg.table(b)
-        ok += [t[rank] == pg.buf.data_ptr() + b, list(pg.flag_table)[rank] == pg.buf.data_ptr() + FLAGS_OFF]
+        ok += [t[rank] == pg.buf.data_ptr() + b, pg.state_ptr == pg.buf.data_ptr()]
         # every rank's view of every buffer: its base (+ the stand-in mapping) + the same offset
         bases = [None] * world
         dist.all_gather_object(bases, pg.buf.data_ptr())
