@@ -61,6 +61,9 @@ _SIGS = {
     "bf16x_selftest_wait": (_i32, [_i32, _i64, _p, _p, _p]),
     "bf16x_gemv_peers": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _i32, _p, _i64, _i64, _i64, _i32, _i32,
                                 _p, _i32, _i64, _p, _p, _p, _i64, _p]),
+    "bf16x_add_rmsnorm": (_i32, [_p, _p, _p, ctypes.c_float, _i64, _i64, _p, _p, _p]),
+    "bf16x_rope_qkv": (_i32, [_p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _i64, _i64, _p]),
+    "bf16x_silu_mul": (_i32, [_p, _i64, _i64, _p, _p]),
     "bf16x_peer_handle_bytes": (_i64, []),
     "bf16x_peer_export": (_i32, [_p, _p, _p]),
     "bf16x_peer_import": (_i32, [_p, _p]),
@@ -115,7 +118,7 @@ def check_device_status(device: int | None = None) -> None:
         from .resident import reset_workspaces
         reset_workspaces()
         names = {1: "wait timeout", 2: "overflow index not ascending", 4: "overflow index out of range",
-                 8: "bad resident layout"}
+                 8: "bad resident layout", 16: "device-side index out of range"}
         what = ", ".join(v for k, v in names.items() if f & k) or hex(f)
         raise Bf16xError(f"device reported: {what} (flags {f:#x})")
 

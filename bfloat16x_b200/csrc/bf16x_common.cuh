@@ -21,6 +21,7 @@ enum : uint32_t {
     kErrOvfUnsorted   = 1u << 1,   // overflow index not strictly ascending
     kErrOvfRange      = 1u << 2,   // overflow index outside [0, N)
     kErrBadLayout     = 1u << 3,   // resident layout inconsistent with its arguments
+    kErrBadIndex      = 1u << 4,   // a device-side index (a decoder position) out of range
 };
 
 // Upper bound for one mbarrier wait, in nanoseconds of %globaltimer.

@@ -27,6 +27,8 @@ import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import _lib
+
 
 @dataclass
 class LlamaConfig:
@@ -51,6 +53,10 @@ CONFIGS = {
 }
 
 
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
 class RMSNorm(nn.Module):
     def __init__(self, n: int, eps: float):
         super().__init__()
@@ -58,9 +64,26 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x):
+        if x.is_cuda:
+            return self.add_forward(x, None)[1]
         xf = x.float()
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
         return (y * self.weight.float()).to(x.dtype)
+
+    def add_forward(self, x, delta):
+        """(h, norm(h)) with h = x + delta (delta may be None): one kernel on
+        the GPU (bf16x_add_rmsnorm), the framework ops on the CPU."""
+        if not x.is_cuda:
+            h = x if delta is None else x + delta
+            return h, self.forward(h)
+        x = x.contiguous()
+        n = x.shape[-1]
+        y = torch.empty_like(x)
+        h = x if delta is None else torch.empty_like(x)
+        d = None if delta is None else delta.to(x.dtype).contiguous()
+        _lib.call("bf16x_add_rmsnorm", x.data_ptr(), None if d is None else d.data_ptr(), self.weight.data_ptr(),
+                  float(self.eps), x.numel() // n, n, None if d is None else h.data_ptr(), y.data_ptr(), _stream(x))
+        return h, y
 
 
 def _rope_tables(head_dim: int, max_pos: int, theta: float, device):
@@ -180,18 +203,27 @@ class Attention(nn.Module):
         w = _rand_weight(cfg.hidden, H * d, seed + 1000 * layer + 2, device)
         self.o_proj = ColumnShard(_linear_from(w[:, rank * self.h * d:(rank + 1) * self.h * d]), group, tp)
 
-    def forward(self, x, pos0, cache_k, cache_v, cos, sin, mask):
+    def forward(self, x, pos0, cache_k, cache_v, cos, sin, mask, tables=None):
         B, T, _ = x.shape
         qkv = self.qkv_proj(x)
         nq, nk = self.h * self.d, self.kvh * self.d
-        q = qkv[..., :nq].reshape(B, T, self.h, self.d)
-        k = qkv[..., nq:nq + nk].reshape(B, T, self.kvh, self.d)
-        v = qkv[..., nq + nk:].reshape(B, T, self.kvh, self.d)
-        q, k = _apply_rope(q, cos, sin), _apply_rope(k, cos, sin)
-        # write this step's keys/values at positions pos0 .. pos0+T-1
-        idx = pos0 + torch.arange(T, device=x.device)
-        cache_k.index_copy_(1, idx, k)
-        cache_v.index_copy_(1, idx, v)
+        if x.is_cuda and tables is not None:
+            # rotary embedding of q and k and the cache write of k and v: one kernel
+            qkv = qkv.contiguous()
+            q = torch.empty((B, T, self.h, self.d), dtype=qkv.dtype, device=x.device)
+            cos_t, sin_t = tables
+            _lib.call("bf16x_rope_qkv", qkv.data_ptr(), B * T, T, self.h, self.kvh, self.d, pos0.data_ptr(),
+                      cos_t.data_ptr(), sin_t.data_ptr(), q.data_ptr(), cache_k.data_ptr(), cache_v.data_ptr(),
+                      cache_k.stride(0), cache_k.shape[1], _stream(x))
+        else:
+            q = qkv[..., :nq].reshape(B, T, self.h, self.d)
+            k = qkv[..., nq:nq + nk].reshape(B, T, self.kvh, self.d)
+            v = qkv[..., nq + nk:].reshape(B, T, self.kvh, self.d)
+            q, k = _apply_rope(q, cos, sin), _apply_rope(k, cos, sin)
+            # write this step's keys/values at positions pos0 .. pos0+T-1
+            idx = pos0 + torch.arange(T, device=x.device)
+            cache_k.index_copy_(1, idx, k)
+            cache_v.index_copy_(1, idx, v)
         # grouped-query attention over the whole static cache (masked)
         o = F.scaled_dot_product_attention(q.transpose(1, 2), cache_k.transpose(1, 2), cache_v.transpose(1, 2),
                                            attn_mask=mask, enable_gqa=True)
@@ -214,6 +246,12 @@ class MLP(nn.Module):
 
     def forward(self, x):
         gu = self.gate_up_proj(x)
+        if gu.is_cuda:
+            gu = gu.contiguous()
+            act = torch.empty((*gu.shape[:-1], self.ffn), dtype=gu.dtype, device=gu.device)
+            _lib.call("bf16x_silu_mul", gu.data_ptr(), gu.numel() // (2 * self.ffn), self.ffn, act.data_ptr(),
+                      _stream(gu))
+            return self.down_proj(act)
         return self.down_proj(F.silu(gu[..., :self.ffn]) * gu[..., self.ffn:])
 
 
@@ -268,12 +306,24 @@ class LlamaModel(nn.Module):
         T = ids.shape[1]
         x = self.embed_tokens(ids)
         pos = pos0 + torch.arange(T, device=ids.device)
-        cos, sin = self.cos[pos], self.sin[pos]
         keys = torch.arange(self.max_seq, device=ids.device)
         mask = (keys[None, :] <= pos[:, None])[None, None]              # [1, 1, T, S]
+        if not x.is_cuda:
+            cos, sin = self.cos[pos], self.sin[pos]
+            for i, blk in enumerate(self.layers):
+                x = blk(x, pos0, self.cache_k[i], self.cache_v[i], cos, sin, mask)
+            h = self.norm(x[:, -1:, :])
+            return self.lm_head(h).float().reshape(ids.shape[0], -1)
+        # the GPU path: each residual add fused with the norm that follows it
+        tables = (self.cos, self.sin)
+        delta = None
         for i, blk in enumerate(self.layers):
-            x = blk(x, pos0, self.cache_k[i], self.cache_v[i], cos, sin, mask)
-        h = self.norm(x[:, -1:, :])
+            x, n1 = blk.input_layernorm.add_forward(x, delta)
+            a = blk.self_attn(n1, pos0, self.cache_k[i], self.cache_v[i], None, None, mask, tables)
+            x, n2 = blk.post_attention_layernorm.add_forward(x, a)
+            delta = blk.mlp(n2)
+        last = x[:, -1:, :].contiguous()
+        _, h = self.norm.add_forward(last, delta[:, -1:, :].contiguous())
         return self.lm_head(h).float().reshape(ids.shape[0], -1)
 
 

@@ -266,6 +266,28 @@ int bf16x_gguf_ovf_pack(const void *x, int x_dtype, int64_t rows, int64_t cols, 
 int bf16x_gguf_apply_ovf(void *y, int y_dtype, int64_t rows, int64_t cols, const uint32_t *row_off,
                          const uint16_t *ecols, const uint16_t *ebits, int64_t n_entries, void *stream);
 
+/* ---- decoder glue --------------------------------------------------------- */
+/* No counterpart in the reference (it has no decoder of its own).  The
+ * element-wise steps between the projections of the end-to-end Llama-style
+ * decoder that measures the hot path in a model, one kernel each instead of a
+ * few dozen framework kernels per layer (bf16 in and out, fp32 arithmetic).
+ * bf16x_add_rmsnorm: per row of n, h = x + delta (delta may be NULL: h = x,
+ *   h_out unused), y = h * rsqrt(mean(h^2) + eps) * w.
+ * bf16x_rope_qkv: qkv [tokens][(H + 2 KV) * D] of batch rows of T tokens at
+ *   positions *pos0 .. *pos0 + T - 1 (device int64): q and k heads rotated
+ *   pairwise (cos/sin tables fp32 [positions][D/2]), q to q_out [tokens][H][D],
+ *   k and v to cache_k / cache_v at [b][position] (batch stride cache_ld_b
+ *   elements, KV * D per position).  Positions must lie in [0, max_pos) (the
+ *   cache's and the tables' length); a token outside is skipped and sets a
+ *   status bit (bf16x_device_status).
+ * bf16x_silu_mul: out [rows][F] = silu(gu[r][i]) * gu[r][F + i]. */
+int bf16x_add_rmsnorm(const uint16_t *x, const uint16_t *delta, const uint16_t *w, float eps, int64_t rows,
+                      int64_t n, uint16_t *h_out, uint16_t *y, void *stream);
+int bf16x_rope_qkv(const uint16_t *qkv, int64_t tokens, int T, int H, int KV, int D, const int64_t *pos0,
+                   const float *cos_t, const float *sin_t, uint16_t *q_out, uint16_t *cache_k,
+                   uint16_t *cache_v, int64_t cache_ld_b, int64_t max_pos, void *stream);
+int bf16x_silu_mul(const uint16_t *gu, int64_t rows, int64_t F, uint16_t *out, void *stream);
+
 /* ---- self-test of the bounded waits ------------------------------------- */
 /* No counterpart in the reference.  Runs one of the library's bounded device
  * waits -- which: 0 the GEMV's mbarrier wait, 1 the tcgen05 GEMM roles' wait,
