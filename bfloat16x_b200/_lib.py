@@ -59,7 +59,6 @@ _SIGS = {
     "bf16x_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "bf16x_gemm_ws": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p, _i64, _p]),
     "bf16x_selftest_wait": (_i32, [_i32, _i64, _p, _p, _p]),
-    "bf16x_gemm_slab_cooperative": (_i32, [_i32]),
     "bf16x_gemv_peers": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _i32, _p, _i64, _i64, _i64, _i32, _i32,
                                 _p, _i32, _i64, _p, _p, _p, _i64, _p]),
     "bf16x_add_rmsnorm": (_i32, [_p, _p, _p, ctypes.c_float, _i64, _i64, _p, _p, _p]),

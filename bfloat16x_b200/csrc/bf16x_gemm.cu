@@ -1418,10 +1418,6 @@ static SlabPlan plan_slab(int64_t rows, int64_t in_f, int64_t M, int sms) {
     return s;
 }
 
-// Per device: 0 no slab launch yet, 1 launched cooperatively, -1 the driver
-// refused a cooperative launch with a cluster dimension.
-static int g_slab_coop[64] = {};
-
 static int launch_gemm_slab(const SlabPlan &pl, const uint8_t *layout, const int32_t *ptile_off,
                             const uint32_t *precs, int64_t rows, int64_t in_f, const uint16_t *x, int64_t M,
                             int64_t ldx, const uint16_t *bias, void *y, int y_dtype, int64_t ldy, void *ws,
@@ -1506,35 +1502,16 @@ static int launch_gemm_slab(const SlabPlan &pl, const uint8_t *layout, const int
     cfg.blockDim = dim3((unsigned)threads);
     cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = st;
-    // A cooperative launch makes the runtime guarantee that every CTA of the
-    // grid is resident at once (or refuse the launch), which is what the
-    // ready/release waits need; where the driver does not take it together
-    // with a cluster dimension, the occupancy cap above is the guarantee.
-    int *coop_ok = g_slab_coop;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeCooperative;
-    attr[1].val.cooperative = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = coop_ok[dev] >= 0 ? 2 : 1;
+    cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, p);
-    if (e != cudaSuccess && cfg.numAttrs == 2 && coop_ok[dev] == 0 &&
-        (e == cudaErrorNotSupported || e == cudaErrorInvalidValue || e == cudaErrorInvalidConfiguration)) {
-        cudaGetLastError();                           // a refused launch configuration, not a device error
-        coop_ok[dev] = -1;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kern, p);
-    }
     if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemm: slab launch: %s", cudaGetErrorString(e));
-    if (cfg.numAttrs == 2) coop_ok[dev] = 1;
     return check_launch("bf16x_gemm");
-}
-
-extern "C" int bf16x_gemm_slab_cooperative(int device) {
-    return (device >= 0 && device < 64) ? g_slab_coop[device] : 0;
 }
 
 }  // namespace bf16x

@@ -240,13 +240,6 @@ int bf16x_gemm_ws(const uint8_t *layout, const int32_t *ptile_off, const uint32_
                   const uint16_t *x, int64_t M, int64_t ldx,
                   const uint16_t *bias, void *y, int y_dtype, int64_t ldy,
                   void *workspace, int64_t workspace_bytes, void *stream);
-/* No counterpart in the reference.  The slab kernel's CTAs wait on one
- * another, so it is launched cooperatively (every CTA resident at once, or
- * the launch is refused) where the driver takes a cooperative launch with a
- * cluster dimension; otherwise the grid is capped at the clusters the device
- * can hold at once.  Returns for `device`: 1 cooperative, -1 the driver
- * refused it (the cap alone applies), 0 no slab launch yet. */
-int bf16x_gemm_slab_cooperative(int device);
 
 /* ---- GGUF BF16X block format (llama.cpp GGML_TYPE_BF16X) --------------- */
 /* 32 weights per 46-byte block: emax[2] (per 16-weight half, floored at 7),

@@ -211,21 +211,3 @@ def test_gemm_slab_wide_ragged_vs_torch():
     assert float((y - ref).norm() / ref.norm()) < GATE
     assert torch.equal(y, rw.gemm(x, bias=bias, out_dtype=torch.float32))
     _lib.check_device_status()
-
-
-def test_slab_launch_cooperative_or_capped():
-    """The slab kernel's CTAs wait on one another: its launch is cooperative
-    (all CTAs resident, or refused) where the driver takes that together with
-    the 2-CTA cluster, else capped at the resident clusters; either way the
-    result is right."""
-    rows, in_f, M = 4096, 1024, 2048
-    assert int(_lib.lib().bf16x_gemm_workspace_bytes(rows, in_f, M)) > 0     # the slab kernel runs
-    w = synthetic_weight(rows, in_f, seed=31, device="cuda")
-    rw = ResidentWeight.from_packed(oracle_dict(bits_of(w)), device="cuda")
-    x = synthetic_activation(M, in_f, seed=37, device="cuda")
-    y = rw.gemm(x, out_dtype=torch.float32)
-    ref = x.float() @ w.float().T
-    assert float((y - ref).norm() / ref.norm()) < GATE
-    state = int(_lib.lib().bf16x_gemm_slab_cooperative(torch.cuda.current_device()))
-    assert state in (1, -1), state
-    _lib.check_device_status()
