@@ -68,9 +68,11 @@ def parse_args():
     ap.add_argument("--new", type=int, default=128, help="generated tokens for --mode e2e")
     ap.add_argument("--seqs", type=int, default=1, help="sequences decoded together for --mode e2e (batch)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill tokens M for --mode gemm")
-    ap.add_argument("--format", choices=["flat", "gguf", "gguf-lossless"], default="flat",
+    ap.add_argument("--format", choices=["flat", "gguf", "gguf-lossless", "gguf-blocks", "gguf-blocks-lossless"],
+                    default="flat",
                     help="weight source: the bf16x_quantize dict (flat), the 11.5-bpw GGUF blocks "
-                         "(zero marker, lossy) or GGUF blocks + side table (exact)")
+                         "(zero marker, lossy) or GGUF blocks + side table (exact), re-encoded into the "
+                         "resident layout; gguf-blocks*: the GEMV reads the GGUF blocks in place")
     return ap.parse_args()
 
 
@@ -94,6 +96,9 @@ def make_resident(w, fmt, dev):
     if fmt == "flat":
         return ResidentWeight.from_packed(bf16x_quantize(w, device=dev), device=dev)
     from bfloat16x_b200.bf16x_gguf_block import GgufWeight
+    if fmt.startswith("gguf-blocks"):
+        # the GEMV reads the 46-byte blocks in place (prefill: resident layout)
+        return GgufWeight.from_float(w, lossless=(fmt == "gguf-blocks-lossless"), native=True)
     return GgufWeight.from_float(w, lossless=(fmt == "gguf-lossless")).resident()
 
 
@@ -476,7 +481,7 @@ def run_ours(args):
         del w
         x = synthetic_activation(B, in_f, seed=si + 1, device=dev)
         L = dict(rw=rw, x=x, w=wb, rows=rows, r0=r0, out_f=out_f, in_f=in_f,
-                 nbytes=workload_bytes(rw.nbytes(), rows, in_f, B))
+                 nbytes=workload_bytes(getattr(rw, "stream_bytes", rw.nbytes)(), rows, in_f, B))
         if peers is not None:
             L["lloff"] = peers.alloc(B * out_f * 8)          # exchange words of this layer
             L["y"] = torch.empty((B, out_f), dtype=torch.bfloat16, device=dev)
@@ -618,7 +623,8 @@ def run_ours(args):
     Ld = layers[dom]
     achieved = Ld["nbytes"] / (per_layer_ms[dom] / 1e3) / 1e9
     peak, peak_kind = peak_hbm()
-    kernel_key = f"gemv_b{B}_{Ld['rows']}x{Ld['in_f']}"
+    kernel_key = (f"gemv_b{B}_{Ld['rows']}x{Ld['in_f']}" if args.format == "flat"
+                  else f"gemv_{args.format}_b{B}_{Ld['rows']}x{Ld['in_f']}")
 
     # ---------------- end-to-end through the public API, host buffers ---------
     e2e = None
@@ -701,14 +707,15 @@ def run_ours(args):
             "data": "synthetic (seeded N(0,0.02) weights with 0.5% x 2^U{4..8} outliers, bf16 N(0,1) activations)",
             "config": bench_config(args, shapes, world),
             "collective_note": collective_note,
-            "resident_bpw": round(8 * sum(L['rw'].nbytes() for L in layers) /
+            "resident_bpw": round(8 * sum(getattr(L['rw'], "stream_bytes", L['rw'].nbytes)() for L in layers) /
                                   sum(L['rows'] * L['in_f'] for L in layers), 3),
             "frac_of_8TBs": round(value / world / 8000.0, 4),
             "tok_s": round(B / (ms_step / 1e3), 1),
             "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per_layer_ms[i], 4) for i, L in enumerate(layers)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "kernel": f"gemv_kernel (fused decode+GEMV) {Ld['rows']}x{Ld['in_f']} batch {B}",
+                         "kernel": f"gemv_kernel{' (GGUF blocks in place)' if args.format.startswith('gguf-blocks') else ''} "
+                                   f"(fused decode+GEMV) {Ld['rows']}x{Ld['in_f']} batch {B}",
                          "traffic": traffic_from_profile(kernel_key) if world == 1 else None},
             "gpu_launches": args.steps * len(layers),
             "timing": "CUDA-graph replay of the step; per_shape_ms from the same launch replayed back to back",

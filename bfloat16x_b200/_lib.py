@@ -55,6 +55,10 @@ _SIGS = {
     "bf16x_gguf_ovf_count": (_i32, [_p, _i32, _i64, _i64, _p, _p]),
     "bf16x_gguf_ovf_pack": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _p]),
     "bf16x_gguf_apply_ovf": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i64, _p]),
+    "bf16x_gguf_side_index_count": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p]),
+    "bf16x_gguf_side_index": (_i32, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _p]),
+    "bf16x_gguf_gemv_scratch_bytes": (_i64, [_i64, _i64]),
+    "bf16x_gguf_gemv": (_i32, [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _i32, _i64, _p, _p, _i64, _p]),
     "bf16x_gemm": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p]),
     "bf16x_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "bf16x_gemm_ws": (_i32, [_p, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _i32, _i64, _p, _i64, _p]),

@@ -5,9 +5,10 @@ GPU through the C ABI.
 Same names and semantics as bf16x_gguf_block.py: numpy arrays in give numpy
 arrays out (the work runs on the current CUDA device); CUDA tensors in give
 CUDA tensors out with no host copies.  ``GgufWeight`` adds what the reference
-leaves to llama.cpp: a device-resident GGUF weight that feeds the fused
-decode+GEMV / decode+GEMM kernels (the 11.5-bpw GGUF-block variant of the
-matmul path), exact when the side table is given.
+leaves to llama.cpp: a device-resident GGUF weight whose GEMV reads the
+46-byte blocks in place (the 11.5-bpw GGUF-block variant of the matmul
+path, exact when the side table is given) and whose larger batches run on
+the tensor-core GEMM.
 
 Block (46 bytes per 32 weights): emax[2] (per 16-weight half, floored at 7),
 sign[4], mant[28], delta[12], all LSB-first; delta 7 is the zero marker.
@@ -20,7 +21,8 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import BF16X_DTYPE_BF16, BF16X_DTYPE_F32, BF16X_DTYPE_F32_TRUNC, call, ptr
+from ._lib import (BF16X_DTYPE_BF16, BF16X_DTYPE_F32, BF16X_DTYPE_F32_TRUNC, Bf16xError, call, check_device_status,
+                   lib, ptr)
 
 QK_BF16X = 32
 BLOCK_BYTES = 46
@@ -231,31 +233,46 @@ def ovf_stats(x):
 class GgufWeight:
     """A (out_f, in_f) weight in GGUF BF16X blocks on the device, with an
     optional lossless side table.  ``dequantize()`` gives bf16 bits through
-    the GPU kernels; ``resident()`` re-encodes those exact values once into
-    the kernel layout so the fused decode+GEMV / decode+GEMM kernels consume
-    the GGUF variant (its zero-marked and side-table weights become patches)."""
+    the GPU kernels.  ``gemv()`` multiplies 1..16 rows of activations either
+    by the blocks in place (``bf16x_gguf_gemv``: 11.5 bits per weight
+    streamed, the side table's exact values stored over the decoded weights;
+    in_f a multiple of 256) or through ``resident()``, the exact values
+    re-encoded once into the kernel layout (its zero-marked and side-table
+    weights become patches), which the tensor-core GEMM always uses.
 
-    def __init__(self, blocks: torch.Tensor, out_f: int, in_f: int, side=None):
+    ``native=None`` picks the faster GEMV for the weight: the blocks in place
+    without a side table (the lossy 11.5-bpw format), the resident layout with
+    one (a table's entries, a few percent of the weights, cost the in-place
+    kernel more than the resident layout's few patches); True or False forces
+    either."""
+
+    def __init__(self, blocks: torch.Tensor, out_f: int, in_f: int, side=None, native: bool | None = None):
         if in_f % QK_BF16X:
             raise ValueError(f"in_f {in_f} not divisible by {QK_BF16X}")
         self.blocks = blocks.contiguous()
         self.out_f, self.in_f = int(out_f), int(in_f)
         self.side = side                       # (row_off, cols, bits) device tensors or None
+        self.native = native
         self._resident = None
+        self._items = None                     # side table as per-item records (block GEMV)
+        self._tile_counters = None
+        self._scratch_need = None
+        self._stream_bytes = None
 
     @classmethod
     @torch.no_grad()
-    def from_float(cls, w, lossless: bool = True) -> "GgufWeight":
+    def from_float(cls, w, lossless: bool = True, native: bool | None = None) -> "GgufWeight":
         t, mode = _values_on_device(w)
         out_f, in_f = t.shape
         blocks = torch.empty(out_f * in_f // QK_BF16X * BLOCK_BYTES, dtype=torch.uint8, device=t.device)
         with torch.cuda.device(t.device):
             call("bf16x_gguf_quantize", ptr(t), mode, t.numel(), ptr(blocks), _stream(t.device))
         side = _pack_ovf_dev(t, mode, out_f, in_f) if lossless else None
-        return cls(blocks, out_f, in_f, side)
+        return cls(blocks, out_f, in_f, side, native=native)
 
     @classmethod
-    def from_blocks(cls, blocks, out_f: int, in_f: int, blob: bytes | None = None) -> "GgufWeight":
+    def from_blocks(cls, blocks, out_f: int, in_f: int, blob: bytes | None = None,
+                    native: bool | None = None) -> "GgufWeight":
         dev = _device()
         b = torch.from_numpy(np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1)).to(dev) \
             if not isinstance(blocks, torch.Tensor) else blocks.reshape(-1).to(dev)
@@ -265,7 +282,7 @@ class GgufWeight:
             if rows != out_f:
                 raise ValueError(f"side table has {rows} rows, weight {out_f}")
             side = (ro, ec, eb)
-        return cls(b, out_f, in_f, side)
+        return cls(b, out_f, in_f, side, native=native)
 
     @property
     def device(self) -> torch.device:
@@ -299,7 +316,104 @@ class GgufWeight:
             self._resident = ResidentWeight.from_packed(p, device=self.device)
         return self._resident
 
+    @property
+    def blocks_native(self) -> bool:
+        """True when the block GEMV can read this weight in place (in_f % 256 == 0)."""
+        return self.in_f % 256 == 0 and self.in_f <= 65536
+
+    @property
+    def gemv_in_place(self) -> bool:
+        """True when gemv() runs on the blocks in place (see ``native``)."""
+        if not self.blocks_native:
+            return False
+        if self.native is not None:
+            return bool(self.native)
+        return self.side is None or self.side[1].numel() == 0
+
+    def _stream(self) -> int:
+        return _stream(self.device)
+
+    @torch.no_grad()
+    def side_records(self):
+        """(item_off, item_recs): the side table re-indexed into one record per
+        (16-row tile, 256-column chunk) for the block GEMV, built once on the
+        GPU; (None, None) without a table or entries."""
+        if self._items is None:
+            if self.side is None or self.side[1].numel() == 0:
+                self._items = (None, None)
+            else:
+                ro, ec, eb = self.side
+                dev = self.device
+                T = (self.out_f + 15) // 16 * (self.in_f // 256)
+                item_off = torch.empty(T + 1, dtype=torch.int32, device=dev)
+                with torch.cuda.device(dev):
+                    call("bf16x_gguf_side_index_count", ptr(ro), ptr(ec), self.out_f, self.in_f, ec.numel(),
+                         ptr(item_off), self._stream())
+                    check_device_status(dev.index)
+                    words = int(item_off[-1].item())
+                    recs = torch.empty(max(words, 4), dtype=torch.int32, device=dev)
+                    call("bf16x_gguf_side_index", ptr(ro), ptr(ec), ptr(eb), self.out_f, self.in_f, ec.numel(),
+                         ptr(item_off), ptr(recs), self._stream())
+                self._items = (item_off, recs)
+        return self._items
+
+    def gemv(self, x: torch.Tensor, bias: torch.Tensor | None = None,
+             out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y[b, n] = sum_k W[n, k] x[b, k] (+ bias) for 1..16 rows of
+        activations, decoded from the blocks in place (side table applied)."""
+        from .resident import GEMV_MAX_BATCH, gemv_scratch
+        if not self.gemv_in_place:
+            return self.resident().gemv(x, bias, out_dtype=out_dtype, out=out)
+        if not x.is_cuda:
+            raise Bf16xError("x must be a CUDA tensor (bfloat16x_b200 runs on the GPU only)")
+        x2 = x.reshape(-1, self.in_f).to(torch.bfloat16)
+        B = x2.shape[0]
+        if B < 1 or B > GEMV_MAX_BATCH:
+            raise ValueError(f"gemv takes 1..{GEMV_MAX_BATCH} rows of activations, got {B}")
+        if not (x2.is_contiguous() and x2.data_ptr() % 16 == 0):
+            x2 = x2.contiguous().clone()
+        if out is None:
+            out = torch.empty((B, self.out_f), dtype=out_dtype, device=self.device)
+        ydt = BF16X_DTYPE_F32 if out.dtype == torch.float32 else BF16X_DTYPE_BF16
+        b = None if bias is None else bias.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        item_off, recs = self.side_records()
+        with torch.cuda.device(self.device):
+            if self._tile_counters is None:
+                self._tile_counters = torch.zeros((self.out_f + 15) // 16 + 1, dtype=torch.int32, device=self.device)
+                self._scratch_need = int(lib().bf16x_gguf_gemv_scratch_bytes(self.out_f, self.in_f))
+            ws = gemv_scratch(self.device, self._scratch_need)
+            call("bf16x_gguf_gemv", ptr(self.blocks), self.out_f, self.in_f, ptr(item_off), ptr(recs), ptr(x2), B,
+                 x2.stride(0), ptr(b), ptr(out), ydt, out.stride(0), ptr(self._tile_counters), ptr(ws), ws.numel(),
+                 self._stream())
+        return out
+
+    def stream_bytes(self) -> int:
+        """Bytes one gemv() reads for the weight: in place, the blocks plus the
+        side-table records and their offsets when there are entries; else the
+        resident layout's."""
+        if not self.gemv_in_place:
+            return self.resident().nbytes()
+        if self._stream_bytes is None:
+            n = self.blocks.numel()
+            item_off, recs = self.side_records()
+            if recs is not None:
+                n += 4 * item_off.numel() + 4 * int(item_off[-1].item())
+            self._stream_bytes = n
+        return self._stream_bytes
+
+    def gemm(self, x: torch.Tensor, bias: torch.Tensor | None = None,
+             out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Any number of rows on the tensor-core GEMM (resident layout)."""
+        return self.resident().gemm(x, bias, out_dtype=out_dtype, out=out)
+
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None, out_dtype=None) -> torch.Tensor:
+        """x[..., in_f] -> [..., out_f]: the block GEMV for up to 16 rows of
+        activations, the resident tensor-core GEMM above that."""
+        from .resident import GEMV_MAX_BATCH
+        x2 = x.reshape(-1, self.in_f)
+        if x2.shape[0] <= GEMV_MAX_BATCH and self.gemv_in_place:
+            od = out_dtype or (x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.bfloat16)
+            return self.gemv(x2, bias, out_dtype=od).reshape(*x.shape[:-1], self.out_f)
         return self.resident().linear(x, bias, out_dtype)
 
 

@@ -40,6 +40,7 @@
 #include <cuda_runtime.h>
 
 #include "bf16x_common.cuh"
+#include "bf16x_gguf.cuh"
 #include "bf16x_resident.cuh"
 #include "bf16x_status.cuh"
 #include "bf16x_tmap.h"
@@ -63,11 +64,20 @@ constexpr int kXRowBytes = kChunkElems * 2;
 // there, instead of copying a 4 KB slice into its slot; with records staged
 // to 160 words (126 entries) the slots then shrink enough for 12 warps per SM.
 constexpr int kXResChunks = 16;      // in_f <= 4096
-template <int BMAX, int NW, bool XRES = false>
+//
+// FMT selects the weight format: kFmtResident (the resident layout) or
+// kFmtGguf (GGUF blocks in place, bf16x_gguf.cuh: 16 rows x 368 bytes per
+// item, no swizzle, records of side-table entries only).
+constexpr int kFmtResident = 0;
+constexpr int kFmtGguf = 1;
+
+template <int BMAX, int NW, bool XRES = false, int FMT = kFmtResident>
 struct GemvCfg {
-    static constexpr int kWBytes = kTileRows * kChunkBytes;                 // 6144
+    static constexpr bool kGguf = FMT == kFmtGguf;
+    static constexpr int kWBytes = kGguf ? kTileRows * kGgufChunkBytes : kTileRows * kChunkBytes;  // 5888 / 6144
+    static constexpr int kRecHdrW = kGguf ? kGgufRecHdrWords : kRecHdrWords;   // words before the entries
     static constexpr int kPOff = XRES ? 0 : BMAX * kXRowBytes;              // record after the activations
-    static constexpr int kPcap = XRES ? 160 : kPcapWords;      // XRES: 126 entries staged
+    static constexpr int kPcap = XRES ? 160 : kGguf ? 128 : kPcapWords;   // XRES: 126 entries staged, GGUF: 124
     static constexpr int kXRSlot = kPOff + kPcap * 4;
     static constexpr int kPerSlot = kWBytes + kXRSlot;
     static constexpr int kXCache = XRES ? kXResChunks * BMAX * kXRowBytes : 0;
@@ -85,18 +95,21 @@ struct GemvCfg {
     static constexpr int kCtaOff = kBarOff + kWarps * kStages * 8 + 8;       // after the x barrier: finished warps
     static constexpr int kSmem = kCtaOff + 16 + 1024;                        // + base alignment
     static_assert(kStages >= 2, "ring too shallow for this configuration");
-    static_assert(kWBytes % 1024 == 0 && kXRSlot % 128 == 0 && kPOff % 16 == 0 && kXCOff % 128 == 0,
-                  "slot alignment");
+    static_assert(kWBytes % (kGguf ? 128 : 1024) == 0 && kXRSlot % 128 == 0 && kPOff % 16 == 0 &&
+                      kXCOff % 128 == 0, "slot alignment");
+    static_assert(!(kGguf && XRES), "the GGUF form stages its activations per item");
     static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct GemvParams {
-    CUtensorMap wmap;   // resident layout [rows][chunks][3 lines], box 16 rows x 1 chunk, 128B swizzle
+    CUtensorMap wmap;   // resident layout [rows][chunks][3 lines], box 16 rows x 1 chunk, 128B swizzle;
+                        // GGUF: blocks as [rows][row_bytes / 4] u32, box 16 rows x 92 words
     CUtensorMap xmap;   // activations [batch][in_pad] bf16, box BMAX rows x 256 columns
     const uint8_t *layout;
     const int32_t *ptile_off;
     const uint32_t *precs;
     int64_t rows, row_bytes;
+    int has_rec;        // GGUF: side-table records given (the resident layout always has records)
     int nch, n_tiles;
     int64_t T;          // items = n_tiles * nch
     int64_t W;          // warps taking part in the partition (<= T)
@@ -163,8 +176,9 @@ struct ItemPatches {
     const uint32_t *precs;
     const int64_t *rof;
     int cap;                                  // record words staged in shared memory
+    int hdr;                                  // record words before the first entry
     __device__ __forceinline__ uint32_t entry(int j) const {
-        return kRecHdrWords + j < cap ? rec[kRecHdrWords + j] : __ldg(precs + *rof + kRecHdrWords + j);
+        return hdr + j < cap ? rec[hdr + j] : __ldg(precs + *rof + hdr + j);
     }
 };
 
@@ -275,6 +289,24 @@ __device__ __forceinline__ void half_mma2(const StepFrag (&f)[8], const uint16_t
     if constexpr (J + 1 < 8) half_mma2<J + 1>(f, xq, xq2, ce, co, de, dd);
 }
 
+// GGUF form: an item's activation rows (those below the batch) rewritten in
+// place in the pair order of the decoded registers: word P of each
+// 32-column group = (x[P], x[P + 16]).  Lane l handles words 4 (l % 4) .. +3
+// of group l / 4; every lane loads before any stores.  Called by the warp.
+template <int BMAX>
+__device__ __forceinline__ void gguf_pair_order_x(uint16_t *xs, int batch, int lane) {
+    const int q = lane >> 2, u = lane & 3;
+    for (int b = 0; b < BMAX && b < batch; ++b) {
+        uint16_t *grp = xs + b * kChunkElems + 32 * q;
+        const uint2 lo = *reinterpret_cast<const uint2 *>(grp + 4 * u);
+        const uint2 hi = *reinterpret_cast<const uint2 *>(grp + 16 + 4 * u);
+        __syncwarp();
+        *reinterpret_cast<uint4 *>(grp + 8 * u) = make_uint4(prmt(lo.x, hi.x, 0x5410u), prmt(lo.x, hi.x, 0x7632u),
+                                                             prmt(lo.y, hi.y, 0x5410u), prmt(lo.y, hi.y, 0x7632u));
+    }
+    __syncwarp();
+}
+
 __device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
 }
@@ -352,10 +384,11 @@ __device__ __forceinline__ void collective_finish(const GemvParams &p, uint32_t 
 __device__ __forceinline__ int64_t item_lo(int64_t w, int64_t T, int64_t W) { return T * w / W; }
 __device__ __forceinline__ int64_t item_owner(int64_t i, int64_t T, int64_t W) { return ((i + 1) * W - 1) / T; }
 
-template <int BMAX, int NW, bool XRES, bool COLL>
-__global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
+template <int BMAX, int NW, bool XRES, bool COLL, int FMT = kFmtResident>
+__global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES, FMT>::kWarps * 32, 1)
     gemv_kernel(const __grid_constant__ GemvParams p) {
-    using C = GemvCfg<BMAX, NW, XRES>;
+    using C = GemvCfg<BMAX, NW, XRES, FMT>;
+    constexpr bool GG = C::kGguf;
     constexpr int S = C::kStages;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the weight slots want a 1024-byte-aligned base (128-byte swizzle)
@@ -397,13 +430,14 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
     // three TMA operations (16 weight rows, the activation slice, the record)
     auto issue = [&](int64_t tile, int c, int s, int32_t r_off, int32_t r_end) {
         if (lane == 0) {
-            const int staged = min(r_end - r_off, C::kPcap);
+            const int staged = GG && !p.has_rec ? 0 : min(r_end - r_off, C::kPcap);
             uint8_t *xr = xrs + s * C::kXRSlot;
             rec_of[s] = r_off;
             mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + (XRES ? 0 : BMAX * kXRowBytes) + staged * 4));
-            tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, c, (int)(tile * kTileRows), &bars[s]);
+            if constexpr (GG) tma_load_2d(wsm + s * C::kWBytes, &p.wmap, c * kGgufChunkWords, (int)(tile * kTileRows), &bars[s]);
+            else tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, c, (int)(tile * kTileRows), &bars[s]);
             if constexpr (!XRES) tma_load_2d(xr, &p.xmap, c * kChunkElems, 0, &bars[s]);
-            bulk_g2s(xr + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
+            if (staged > 0) bulk_g2s(xr + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
         }
     };
 
@@ -413,8 +447,9 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
     int i_c = (int)(lo - first_tile * p.nch);
     int32_t nxt_off = 0, nxt_end = 0;
     uint32_t epoch = 0;                           // collective epilogue only
+    const bool has_rec = !GG || p.has_rec;
     auto load_rec = [&]() {
-        if (i_it < hi) {
+        if (i_it < hi && has_rec) {
             nxt_off = __ldg(p.ptile_off + i_it);
             nxt_end = __ldg(p.ptile_off + i_it + 1);
         }
@@ -430,7 +465,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
         // outputs and the scratch are touched only after it.  Each slot's
         // expected bytes are raised without arriving; the activation copy's
         // arrival completes the phase.
-        const int32_t v = (lane <= S + 1 && lo + lane <= p.T) ? __ldg(p.ptile_off + lo + lane) : 0;
+        const int32_t v = (has_rec && lane <= S + 1 && lo + lane <= p.T) ? __ldg(p.ptile_off + lo + lane) : 0;
         int64_t tl = i_tile;
         int cc = i_c;
         for (int s = 0; s < S && lo + s < hi; ++s) {
@@ -440,8 +475,9 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
                 rec_of[s] = r_off;
                 if constexpr (XRES) mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
                 else mbar_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
-                tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, cc, (int)(tl * kTileRows), &bars[s]);
-                bulk_g2s(xrs + s * C::kXRSlot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
+                if constexpr (GG) tma_load_2d(wsm + s * C::kWBytes, &p.wmap, cc * kGgufChunkWords, (int)(tl * kTileRows), &bars[s]);
+                else tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, cc, (int)(tl * kTileRows), &bars[s]);
+                if (staged > 0) bulk_g2s(xrs + s * C::kXRSlot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
             }
             if (++cc == p.nch) { cc = 0; ++tl; }
         }
@@ -540,7 +576,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
         const uint8_t *wsl = wsm + s * C::kWBytes;
         const uint8_t *xr = xrs + s * C::kXRSlot;
         const uint16_t *xs = reinterpret_cast<const uint16_t *>(XRES ? smem + C::kXCOff + c * BMAX * kXRowBytes : xr);
-        {
+        if constexpr (!GG) {
             const uint32_t *rec = reinterpret_cast<const uint32_t *>(xr + C::kPOff);
             const uint32_t hdr = rec[kRecHdr];
             const uint2 ewA = *reinterpret_cast<const uint2 *>(rec + 2 * g);        // emax of row g, groups 0..7
@@ -554,7 +590,7 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
                 load_group_sw(wsl, go[h], smA[h], dA[h]);
                 load_group_sw(wsl + kRowB, go[h], smB[h], dB[h]);
             }
-            const ItemPatches ip{rec, p.precs, rec_of + s, C::kPcap};
+            const ItemPatches ip{rec, p.precs, rec_of + s, C::kPcap, C::kRecHdrW};
             const int n_low = (int)(hdr & 0xFFFFu), n_all = (int)(hdr >> 16);
             // Few entries (the usual case): the patched weights enter the
             // products with their saturated value, and (exact - saturated) * x
@@ -609,6 +645,65 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES>::kWarps * 32, 1)
             // shared-memory writes of the generic proxy before the slot's
             // refill by the TMA engine (async proxy)
             if (dense) fence_proxy_async_smem();
+        } else {
+            // GGUF blocks: the activations into the decoded pair order, the
+            // four 12-word windows of the lane's blocks (rows g and g + 8,
+            // blocks 2t and 2t + 1 of the chunk) into registers, then per
+            // half: decode, side-table values (dense), multiply.
+            gguf_pair_order_x<BMAX>(reinterpret_cast<uint16_t *>(const_cast<uint8_t *>(xr)), p.batch, lane);
+            const uint32_t *rec = reinterpret_cast<const uint32_t *>(xr + C::kPOff);
+            const uint32_t hdr = p.has_rec ? rec[0] : 0u;
+            const uint16_t *xg = g < BMAX ? xs + g * kChunkElems : zero_x;
+            const uint32_t *wv = reinterpret_cast<const uint32_t *>(wsl);
+            uint32_t wA[2][12], wB[2][12];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int i = 0; i < 12; ++i) {
+                    wA[h][i] = wv[g * kGgufChunkWords + 23 * t + 11 * h + i];
+                    wB[h][i] = wv[(g + 8) * kGgufChunkWords + 23 * t + 11 * h + i];
+                }
+            // blocks with an emax below 7 (never written by the packer, and
+            // the zero rows past the end of the weight) take the exact
+            // per-lane form, for the whole warp
+            const uint32_t emin = min(min(gguf_min_emax<0>(wA[0]), gguf_min_emax<0>(wB[0])),
+                                      min(gguf_min_emax<1>(wA[1]), gguf_min_emax<1>(wB[1])));
+            const bool exact_form = __any_sync(0xffffffffu, emin < 7u);
+            const ItemPatches ip{rec, p.precs, rec_of + s, C::kPcap, C::kRecHdrW};
+            const int n_low = (int)(hdr & 0xFFFFu), n_all = (int)(hdr >> 16);
+            auto half = [&](auto h_tag, auto fast_tag) {
+                constexpr int h = decltype(h_tag)::value;
+                constexpr bool kFast = decltype(fast_tag)::value;
+                uint32_t pa[16], pb[16];
+                gguf_pairs_from<0, kFast>(gguf_load_block<h>(wA[h]), pa);
+                gguf_pairs_from<0, kFast>(gguf_load_block<h>(wB[h]), pb);
+                StepFrag f[8];
+#pragma unroll
+                for (int J = 0; J < 8; ++J) f[J] = StepFrag{pa[2 * J], pb[2 * J], pa[2 * J + 1], pb[2 * J + 1]};
+                // the windows are in registers, so the weight slot serves as
+                // the fragment buffer of the side-table values
+                if (n_all > 0)
+                    patch_half_dense(f, reinterpret_cast<uint4 *>(const_cast<uint8_t *>(wsl)), ip, h ? n_low : 0,
+                                     h ? n_all : n_low, lane);
+                const int q = 2 * t + h;
+                if constexpr (BMAX > 8) {
+                    half_mma2<0>(f, xg + 32 * q, xs + (8 + g) * kChunkElems + 32 * q, ce, co, de, dd);
+                } else {
+                    half_mma<0>(f, xg + 32 * q, g < BMAX, ce, co);
+                }
+            };
+            using I0 = std::integral_constant<int, 0>;
+            using I1 = std::integral_constant<int, 1>;
+            if (exact_form) {
+                half(I0{}, std::false_type{});
+                half(I1{}, std::false_type{});
+            } else {
+                half(I0{}, std::true_type{});
+                half(I1{}, std::true_type{});
+            }
+            // the permuted activations and side-table values were written
+            // with generic stores before the slot's refill by the TMA engine
+            fence_proxy_async_smem();
         }
 
         // ---- refill this slot S items ahead
@@ -763,18 +858,30 @@ static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
     return GemvCfg<16, 8>::kWarps;
 }
 
+// The GGUF form: the same choice without the CTA activation block.
+static int warps_for_gguf(int64_t batch, int64_t rows, int64_t in_f) {
+    const int64_t nch = (in_f + kChunkElems - 1) / kChunkElems;
+    const int64_t T = (rows + kTileRows - 1) / kTileRows * nch;
+    const bool wide = T * 8 >= nch * (int64_t)device_sms() * 12;
+    if (batch == 1) return wide ? GemvCfg<1, 16, false, kFmtGguf>::kWarps : GemvCfg<1, 8, false, kFmtGguf>::kWarps;
+    if (batch == 2) return wide ? GemvCfg<2, 12, false, kFmtGguf>::kWarps : GemvCfg<2, 8, false, kFmtGguf>::kWarps;
+    if (batch <= 4) return wide ? GemvCfg<4, 12, false, kFmtGguf>::kWarps : GemvCfg<4, 8, false, kFmtGguf>::kWarps;
+    if (batch <= 8) return wide ? GemvCfg<8, 10, false, kFmtGguf>::kWarps : GemvCfg<8, 8, false, kFmtGguf>::kWarps;
+    return GemvCfg<16, 8, false, kFmtGguf>::kWarps;
+}
+
 // partial sums: per unit two [16][8] (batch <= 8) or [16][16] fp32 slots
 static int64_t scratch_need(const GemvLaunch &L, int64_t batch) { return L.W * 2 * 16 * (batch > 8 ? 16 : 8) * 4; }
 
-template <int BMAX, int NW, bool XRES, bool COLL>
+template <int BMAX, int NW, bool XRES, bool COLL, int FMT = kFmtResident>
 static int launch_gemv_as(const GemvParams &p, const GemvLaunch &L, cudaStream_t st) {
-    using C = GemvCfg<BMAX, NW, XRES>;
+    using C = GemvCfg<BMAX, NW, XRES, FMT>;
     int dev = 0;
     cudaGetDevice(&dev);
     static bool attr_set[64] = {false};
     if (dev < 0 || dev >= 64) return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gemv: device index %d", dev);
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BMAX, NW, XRES, COLL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BMAX, NW, XRES, COLL, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
         if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: smem attribute: %s", cudaGetErrorString(e));
         attr_set[dev] = true;
     }
@@ -790,7 +897,7 @@ static int launch_gemv_as(const GemvParams &p, const GemvLaunch &L, cudaStream_t
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<BMAX, NW, XRES, COLL>, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<BMAX, NW, XRES, COLL, FMT>, p);
     if (e != cudaSuccess) return set_error(BF16X_ERR_CUDA, "bf16x_gemv: launch: %s", cudaGetErrorString(e));
     return check_launch("bf16x_gemv");
 }
@@ -906,6 +1013,7 @@ static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint
     }
     p.layout = layout; p.ptile_off = ptile_off; p.precs = precs;
     p.rows = rows; p.row_bytes = resident_row_bytes(in_f);
+    p.has_rec = 1;
     p.nch = L.nch; p.n_tiles = L.n_tiles; p.T = L.T; p.W = L.W;
     p.x = x; p.ldx = ldx; p.batch = (int)batch;
     p.bias = bias; p.y = y; p.y_f32 = y_dtype == BF16X_DTYPE_F32; p.ldy = ldy;
@@ -936,6 +1044,82 @@ static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint
 }
 
 }  // namespace bf16x
+
+// ------------------------------------------------------- GGUF-block GEMV
+namespace bf16x {
+
+static bool make_gguf_map(CUtensorMap *m, const MapKey &k) {   // a = rows, b = in_f
+    const int64_t rb = gguf_row_bytes(k.b);
+    const cuuint64_t dims[2] = {(cuuint64_t)(rb / 4), (cuuint64_t)k.a};
+    const cuuint64_t strides[1] = {(cuuint64_t)rb};
+    const cuuint32_t box[2] = {(cuuint32_t)kGgufChunkWords, (cuuint32_t)kTileRows};
+    return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, k.ptr, dims, strides, box);
+}
+
+}  // namespace bf16x
+
+extern "C" int64_t bf16x_gguf_gemv_scratch_bytes(int64_t rows, int64_t in_f) {
+    if (rows <= 0 || in_f <= 0) return 0;
+    int64_t need = 0;
+    for (int b : {1, 2, 4, 8, 16})
+        need = std::max(need, scratch_need(plan_gemv(rows, in_f, warps_for_gguf(b, rows, in_f)), b));
+    return need;
+}
+
+extern "C" int bf16x_gguf_gemv(const uint8_t *blocks, int64_t rows, int64_t in_f, const int32_t *item_off,
+                               const uint32_t *item_recs, const uint16_t *x, int64_t batch, int64_t ldx,
+                               const uint16_t *bias, void *y, int y_dtype, int64_t ldy, int32_t *tile_counters,
+                               void *scratch, int64_t scratch_bytes, void *stream) {
+    if (rows < 0 || in_f <= 0) return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: bad shape");
+    if (in_f % kChunkElems != 0 || in_f > 65536)
+        return set_error(BF16X_ERR_UNSUPPORTED, "bf16x_gguf_gemv: in_f must be a multiple of 256 and <= 65536 (got %lld)",
+                         (long long)in_f);
+    if (batch < 1 || batch > 16) return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: batch must be 1..16 (got %lld)", (long long)batch);
+    if (y_dtype != BF16X_DTYPE_BF16 && y_dtype != BF16X_DTYPE_F32)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: bad y_dtype");
+    if ((item_off == nullptr) != (item_recs == nullptr))
+        return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: side-table offsets and records go together");
+    if (rows == 0) return BF16X_OK;
+    if (!blocks || !x || !y) return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: null pointer");
+    if (ldx < in_f || (ldx % 8) != 0)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: ldx must be a multiple of 8 and >= in_f");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(blocks) | reinterpret_cast<uintptr_t>(item_recs)) & 15u)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: x, blocks and records must be 16-byte aligned");
+    if (ldy < rows) return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: ldy < rows");
+    const int nw = warps_for_gguf(batch, rows, in_f);
+    const GemvLaunch L = plan_gemv(rows, in_f, nw);
+    if (!tile_counters) return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: tile_counters (ceil(rows/16) zeroed int32) missing");
+    if (!scratch || scratch_bytes < scratch_need(L, batch))
+        return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: scratch of %lld bytes needed", (long long)scratch_need(L, batch));
+    if (reinterpret_cast<uintptr_t>(scratch) & 15u)
+        return set_error(BF16X_ERR_INVALID, "bf16x_gguf_gemv: scratch must be 16-byte aligned");
+    GemvParams p = {};
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int64_t bmax = batch == 1 ? 1 : batch == 2 ? 2 : batch <= 4 ? 4 : batch <= 8 ? 8 : 16;
+        if (!cached_map(&p.wmap, MapKey{blocks, rows, in_f, 1, dev}, make_gguf_map))
+            return set_error(BF16X_ERR_CUDA, "bf16x_gguf_gemv: block tensor map");
+        if (!cached_map(&p.xmap, MapKey{x, in_f, batch, ldx | (bmax << 40), dev}, make_xmap))
+            return set_error(BF16X_ERR_CUDA, "bf16x_gguf_gemv: activation tensor map");
+    }
+    p.layout = blocks; p.ptile_off = item_off; p.precs = item_recs;
+    p.has_rec = item_off != nullptr;
+    p.rows = rows; p.row_bytes = gguf_row_bytes(in_f);
+    p.nch = L.nch; p.n_tiles = L.n_tiles; p.T = L.T; p.W = L.W;
+    p.x = x; p.ldx = ldx; p.batch = (int)batch;
+    p.bias = bias; p.y = y; p.y_f32 = y_dtype == BF16X_DTYPE_F32; p.ldy = ldy;
+    p.tile_cnt = tile_counters;
+    p.partials = static_cast<float *>(scratch);
+    p.nranks = 1;
+    cudaStream_t st = (cudaStream_t)stream;
+    constexpr int G = kFmtGguf;
+    if (batch == 1) return nw > 8 ? launch_gemv_as<1, 16, false, false, G>(p, L, st) : launch_gemv_as<1, 8, false, false, G>(p, L, st);
+    if (batch == 2) return nw > 8 ? launch_gemv_as<2, 12, false, false, G>(p, L, st) : launch_gemv_as<2, 8, false, false, G>(p, L, st);
+    if (batch <= 4) return nw > 8 ? launch_gemv_as<4, 12, false, false, G>(p, L, st) : launch_gemv_as<4, 8, false, false, G>(p, L, st);
+    if (batch <= 8) return nw > 8 ? launch_gemv_as<8, 10, false, false, G>(p, L, st) : launch_gemv_as<8, 8, false, false, G>(p, L, st);
+    return launch_gemv_as<16, 8, false, false, G>(p, L, st);
+}
 
 // ------------------------------------------------ no-allocation GEMV entry
 // bf16x_gemv_noalloc serves callers that cannot hand this library device

@@ -18,6 +18,8 @@
 #include <cuda_runtime.h>
 
 #include "bf16x_common.cuh"
+#include "bf16x_gguf.cuh"
+#include "bf16x_resident.cuh"
 #include "bf16x_status.cuh"
 
 namespace bf16x {
@@ -276,6 +278,99 @@ __global__ void gguf_apply_ovf_kernel(void *y, int y_f32, int64_t rows, int64_t 
     }
 }
 
+// ------------------------------------------ side table -> per-item records
+// The records the GGUF-block GEMV stages with each (16-row tile, 256-column
+// chunk) item (bf16x_gguf.cuh).  One CTA per tile, threads strided over the
+// tile's (row, chunk) pairs: a row's entries are sorted by column, so those
+// of one chunk are a contiguous range, found by binary search and counted
+// per half (block parity).  WRITE = false stores each item's record size in
+// words (scanned into offsets afterwards); WRITE = true fills the records,
+// entries of half 0 first, each half by row then column, deterministically.
+// Row offsets are clamped to [0, n_entries] and columns at or past in_f
+// fall in no chunk, so both kernels see the same (possibly clipped) table
+// and the writes stay inside the records the counts sized; the counting
+// pass reports any such table through the status word.
+__device__ __forceinline__ int64_t col_lower_bound(const uint16_t *cols, int64_t lo, int64_t hi, uint32_t v) {
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if ((uint32_t)cols[mid] < v) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+template <bool WRITE>
+__global__ void __launch_bounds__(256) gguf_side_kernel(const uint32_t *row_off, const uint16_t *cols,
+                                                        const uint16_t *bits, int64_t rows, int64_t in_f,
+                                                        int64_t n_entries, int nch, int32_t *item_off,
+                                                        uint32_t *recs) {
+    extern __shared__ int32_t side_sh[];
+    int32_t *cnt = side_sh;                 // [(c * 16 + r) * 2 + half]
+    int32_t *first = side_sh + nch * 32;    // [c * 16 + r]: the range's first entry
+    const int64_t r0 = (int64_t)blockIdx.x * kTileRows;
+    const int nr = (int)(rows - r0 < kTileRows ? rows - r0 : kTileRows);
+    if constexpr (!WRITE) {
+        if (blockIdx.x == 0 && threadIdx.x == 0 && (row_off[0] != 0u || (int64_t)row_off[rows] != n_entries))
+            atomicOr(&g_status, kErrOvfRange);
+        for (int r = threadIdx.x; r < nr; r += blockDim.x) {
+            const int64_t b = row_off[r0 + r], e = row_off[r0 + r + 1];
+            if (e < b || e > n_entries) { atomicOr(&g_status, kErrOvfRange); continue; }
+            for (int64_t k = b; k < e; ++k) {
+                if ((int64_t)cols[k] >= in_f) atomicOr(&g_status, kErrOvfRange);
+                if (k > b && cols[k - 1] >= cols[k]) atomicOr(&g_status, kErrOvfUnsorted);
+            }
+        }
+    }
+    for (int i = threadIdx.x; i < nch * kTileRows; i += blockDim.x) {
+        const int c = i >> 4, r = i & 15;
+        int32_t n0 = 0, n1 = 0;
+        int64_t a = 0;
+        if (r < nr) {
+            const int64_t e = ::min((int64_t)row_off[r0 + r + 1], n_entries);
+            const int64_t b = ::min((int64_t)row_off[r0 + r], e);
+            a = col_lower_bound(cols, b, e, 256u * c);
+            const int64_t z = col_lower_bound(cols, a, e, 256u * (c + 1));
+            for (int64_t k = a; k < z; ++k) {
+                if ((cols[k] >> 5) & 1u) ++n1; else ++n0;
+            }
+        }
+        cnt[2 * i] = n0;
+        cnt[2 * i + 1] = n1;
+        first[i] = (int32_t)a;
+    }
+    __syncthreads();
+    if constexpr (!WRITE) {
+        for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+            int32_t n = 0;
+            for (int r = 0; r < kTileRows; ++r) n += cnt[2 * (c * 16 + r)] + cnt[2 * (c * 16 + r) + 1];
+            item_off[(int64_t)blockIdx.x * nch + c] = (int32_t)gguf_rec_words(n);
+        }
+    } else {
+        for (int i = threadIdx.x; i < nch * kTileRows; i += blockDim.x) {
+            const int c = i >> 4, r = i & 15;
+            int32_t base0 = 0, base1 = 0, n_low = 0, n_all = 0;
+            for (int rr = 0; rr < kTileRows; ++rr) {
+                const int32_t a0 = cnt[2 * (c * 16 + rr)], a1 = cnt[2 * (c * 16 + rr) + 1];
+                if (rr < r) { base0 += a0; base1 += a1; }
+                n_low += a0;
+                n_all += a0 + a1;
+            }
+            base1 += n_low;
+            uint32_t *rec = recs + item_off[(int64_t)blockIdx.x * nch + c];
+            if (r == 0) {
+                rec[0] = (uint32_t)n_low | ((uint32_t)n_all << 16);
+                rec[1] = rec[2] = rec[3] = 0u;
+                for (int64_t w = kGgufRecHdrWords + n_all; w < gguf_rec_words(n_all); ++w) rec[w] = 0u;
+            }
+            const int64_t a = first[i], z = a + cnt[2 * i] + cnt[2 * i + 1];
+            for (int64_t k = a; k < z; ++k) {
+                const uint32_t col = (uint32_t)cols[k] & 255u, h = (col >> 5) & 1u;
+                const int32_t pos = h ? base1++ : base0++;
+                rec[kGgufRecHdrWords + pos] = gguf_frag_index((uint32_t)r, col) | (h << 11) | ((uint32_t)bits[k] << 16);
+            }
+        }
+    }
+}
+
 static int grid_for(int64_t n, int per) {
     const int64_t g = (n + per - 1) / per;
     return (int)std::min<int64_t>(g, 1 << 30);
@@ -349,4 +444,49 @@ extern "C" int bf16x_gguf_apply_ovf(void *y, int y_dtype, int64_t rows, int64_t 
     gguf_apply_ovf_kernel<<<grid_for(n_entries, 256), 256, 0, (cudaStream_t)stream>>>(
         y, y_dtype == BF16X_DTYPE_F32, rows, cols, row_off, ecols, ebits, n_entries);
     return check_launch("bf16x_gguf_apply_ovf");
+}
+
+static int side_args(const char *who, const uint32_t *row_off, const uint16_t *cols, int64_t rows, int64_t in_f,
+                     int64_t n_entries) {
+    if (rows < 0 || n_entries < 0) return set_error(BF16X_ERR_INVALID, "%s: bad size", who);
+    if (in_f <= 0 || in_f % 256 || in_f > 65536)
+        return set_error(BF16X_ERR_UNSUPPORTED, "%s: in_f must be a multiple of 256 and <= 65536", who);
+    if (rows > 0 && !row_off) return set_error(BF16X_ERR_INVALID, "%s: null row_off", who);
+    if (n_entries > 0 && !cols) return set_error(BF16X_ERR_INVALID, "%s: null columns", who);
+    if (n_entries >= (1ll << 30)) return set_error(BF16X_ERR_UNSUPPORTED, "%s: too many entries", who);
+    return BF16X_OK;
+}
+
+extern "C" int bf16x_gguf_side_index_count(const uint32_t *row_off, const uint16_t *cols, int64_t rows, int64_t in_f,
+                                           int64_t n_entries, int32_t *item_off, void *stream) {
+    if (int rc = side_args("bf16x_gguf_side_index_count", row_off, cols, rows, in_f, n_entries)) return rc;
+    if (!item_off) return set_error(BF16X_ERR_INVALID, "bf16x_gguf_side_index_count: null item_off");
+    const int nch = (int)(in_f / 256);
+    const int64_t n_tiles = (rows + kTileRows - 1) / kTileRows;
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t sh = (size_t)nch * kTileRows * 3 * sizeof(int32_t);
+    if (n_tiles > 0) {
+        cudaFuncSetAttribute(gguf_side_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh);
+        gguf_side_kernel<false><<<(unsigned)n_tiles, 256, sh, st>>>(row_off, cols, nullptr, rows, in_f, n_entries, nch,
+                                                                   item_off, nullptr);
+        if (int rc = check_launch("bf16x_gguf_side_index_count")) return rc;
+    }
+    gguf_scan_kernel<<<1, 1024, 0, st>>>(reinterpret_cast<uint32_t *>(item_off), n_tiles * nch);
+    return check_launch("bf16x_gguf_side_index_count scan");
+}
+
+extern "C" int bf16x_gguf_side_index(const uint32_t *row_off, const uint16_t *cols, const uint16_t *bits, int64_t rows,
+                                     int64_t in_f, int64_t n_entries, const int32_t *item_off, uint32_t *item_recs,
+                                     void *stream) {
+    if (int rc = side_args("bf16x_gguf_side_index", row_off, cols, rows, in_f, n_entries)) return rc;
+    if (rows == 0) return BF16X_OK;
+    if (!item_off || !item_recs || (n_entries > 0 && !bits))
+        return set_error(BF16X_ERR_INVALID, "bf16x_gguf_side_index: null pointer");
+    const int nch = (int)(in_f / 256);
+    const int64_t n_tiles = (rows + kTileRows - 1) / kTileRows;
+    const size_t sh = (size_t)nch * kTileRows * 3 * sizeof(int32_t);
+    cudaFuncSetAttribute(gguf_side_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh);
+    gguf_side_kernel<true><<<(unsigned)n_tiles, 256, sh, (cudaStream_t)stream>>>(
+        row_off, cols, bits, rows, in_f, n_entries, nch, const_cast<int32_t *>(item_off), item_recs);
+    return check_launch("bf16x_gguf_side_index");
 }

@@ -266,6 +266,36 @@ int bf16x_gguf_ovf_pack(const void *x, int x_dtype, int64_t rows, int64_t cols, 
 int bf16x_gguf_apply_ovf(void *y, int y_dtype, int64_t rows, int64_t cols, const uint32_t *row_off,
                          const uint16_t *ecols, const uint16_t *ebits, int64_t n_entries, void *stream);
 
+/* ---- GEMV on the GGUF blocks in place ------------------------------------ */
+/* The decode+GEMV of llama.cpp's BF16X matmul with the lossless side table
+ * applied (GGML_OP_SPARSE_MM, README.md:311-318; block decode
+ * bf16x_gguf_block.py:84-95, table bf16x_gguf_block.py:107-181) reading the
+ * 46-byte blocks themselves: y[b][n] = sum_k W[n][k] x[b][k] (+ bias[n]) for
+ * batch 1..16, W the blocks (rows x in_f/32 blocks, row-major, 16-byte
+ * aligned; in_f a multiple of 256, <= 65536) decoded exactly, with the side
+ * table's values where it has entries.  The side table is first re-indexed
+ * into one record per (16-row tile, 256-column chunk):
+ * bf16x_gguf_side_index_count writes item_off[0..T] (T = ceil(rows/16) *
+ * in_f/256, int32 word offsets, item_off[T] = words of records), then
+ * bf16x_gguf_side_index fills item_recs (item_off[T] uint32, 16-byte
+ * aligned) from the table (row_off: rows+1 u32; cols, bits: u16 per entry,
+ * sorted by row then column).  A table with bad offsets, unsorted columns or
+ * columns >= in_f is reported through the device status.  Without a table
+ * (the lossy format) item_off and item_recs are both NULL.  x: [batch][ldx]
+ * bf16 bits (ldx >= in_f, multiple of 8, 16-byte aligned); tile_counters:
+ * ceil(rows/16) int32 zeroed once (the kernel leaves them zero); scratch:
+ * bf16x_gguf_gemv_scratch_bytes(rows, in_f) bytes, 16-byte aligned. */
+int bf16x_gguf_side_index_count(const uint32_t *row_off, const uint16_t *cols, int64_t rows, int64_t in_f,
+                                int64_t n_entries, int32_t *item_off, void *stream);
+int bf16x_gguf_side_index(const uint32_t *row_off, const uint16_t *cols, const uint16_t *bits, int64_t rows,
+                          int64_t in_f, int64_t n_entries, const int32_t *item_off, uint32_t *item_recs,
+                          void *stream);
+int64_t bf16x_gguf_gemv_scratch_bytes(int64_t rows, int64_t in_f);
+int bf16x_gguf_gemv(const uint8_t *blocks, int64_t rows, int64_t in_f, const int32_t *item_off,
+                    const uint32_t *item_recs, const uint16_t *x, int64_t batch, int64_t ldx,
+                    const uint16_t *bias, void *y, int y_dtype, int64_t ldy, int32_t *tile_counters,
+                    void *scratch, int64_t scratch_bytes, void *stream);
+
 /* ---- decoder glue --------------------------------------------------------- */
 /* No counterpart in the reference (it has no decoder of its own).  The
  * element-wise steps between the projections of the end-to-end Llama-style
