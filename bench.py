@@ -389,6 +389,85 @@ def prefill_record(layers, dev, steps, warmup, with_cublas):
     return out
 
 
+def gguf_record(layers, dev, steps, batch):
+    """The same four weights quantized to the 11.5-bpw GGUF blocks (lossy:
+    zero marker, no side table) and multiplied in place by bf16x_gguf_gemv:
+    the step as one CUDA graph, each launch replayed back to back, the
+    dominant launch's fraction of the measured HBM copy bandwidth
+    (algorithmic bytes: 46 B per 32 weights + x + y)."""
+    import torch
+
+    from bfloat16x_b200.bf16x_gguf_block import GgufWeight
+    if any(L.get("w") is None for L in layers) or any(L["in_f"] % 256 for L in layers):
+        return None
+    peak, kind = peak_hbm()
+    gws = [GgufWeight.from_float(L["w"], lossless=False, native=True) for L in layers]
+    ys = [torch.empty((batch, L["rows"]), dtype=torch.bfloat16, device=dev) for L in layers]
+
+    def run(i):
+        gws[i].gemv(layers[i]["x"], out=ys[i])
+
+    def step():
+        for i in range(len(layers)):
+            run(i)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            step()                                  # scratch and counters exist before the capture
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step()
+        gl = []
+        for i in range(len(layers)):
+            h = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(h, stream=s):
+                run(i)
+            gl.append(h)
+    torch.cuda.synchronize(dev)
+    for _ in range(3):
+        g.replay()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / steps
+    per = []
+    for h in gl:
+        h.replay()
+        a.record()
+        for _ in range(steps):
+            h.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        per.append(a.elapsed_time(b) / steps)
+    nbytes = [gw.stream_bytes() + 2 * batch * (L["in_f"] + L["rows"]) for gw, L in zip(gws, layers)]
+    dom = max(range(len(layers)), key=lambda i: per[i])
+    ach = nbytes[dom] / (per[dom] / 1e3) / 1e9
+    key = f"gemv_gguf-blocks_b{batch}_{layers[dom]['rows']}x{layers[dom]['in_f']}"
+    out = {"format": "GGUF BF16X blocks, lossy (11.5 bits per weight), GEMV on the blocks in place",
+           "ms_per_step": round(ms, 4), "GB/s": round(sum(nbytes) / (ms / 1e3) / 1e9, 1),
+           "bits_per_weight": round(8 * sum(gw.stream_bytes() for gw in gws) /
+                                    sum(L["rows"] * L["in_f"] for L in layers), 3),
+           "per_shape_ms": {f"{L['rows']}x{L['in_f']}": round(per[i], 4) for i, L in enumerate(layers)},
+           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(ach / peak, 4), "peak_source": kind,
+                        "kernel": f"gemv_kernel (GGUF blocks in place) {layers[dom]['rows']}x{layers[dom]['in_f']}",
+                        "traffic": traffic_from_profile(key)},
+           "gpu_launches": steps * len(layers)}
+    _lib_check(dev)
+    del g, gl, gws, ys
+    return out
+
+
+def _lib_check(dev):
+    from bfloat16x_b200 import _lib
+    _lib.check_device_status(dev.index)
+
+
 def decode_record(dev, reps=20):
     """Stand-alone flat decode + overflow fix (bf16x_decode_triton) on 2048x1536
     and 4096x4096: bytes = 1.4375 B/weight of streams + 5 B per overflow entry
@@ -685,10 +764,12 @@ def run_ours(args):
                   "note": "torch F.linear (cuBLAS) on the uncompressed bf16 weights (this rank's rows, no "
                           "all-gather), same shapes, CUDA graph"}
 
-    prefill = decode = None
+    prefill = decode = gguf = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_record(layers, dev, min(args.steps, 10), args.warmup, not args.no_cublas)
         decode = decode_record(dev)
+        if args.format == "flat":
+            gguf = gguf_record(layers, dev, args.steps, B)
 
     # ---------------- CPU baseline (rank 0, N=1) ---------------------------------
     cpu = None
@@ -725,6 +806,7 @@ def run_ours(args):
             "allgather_nccl": nccl_cmp,
             "prefill": prefill,
             "decode": decode,
+            "gguf": gguf,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
