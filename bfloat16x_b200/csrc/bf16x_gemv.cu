@@ -464,22 +464,29 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES, FMT>::kWarps * 32, 1)
         // the end of the previous kernel of the stream; the activations, the
         // outputs and the scratch are touched only after it.  Each slot's
         // expected bytes are raised without arriving; the activation copy's
-        // arrival completes the phase.
-        const int32_t v = (has_rec && lane <= S + 1 && lo + lane <= p.T) ? __ldg(p.ptile_off + lo + lane) : 0;
+        // arrival completes the phase.  The weight rows go first: they need
+        // no record offset, so their copies are in flight while the offsets
+        // load.
         int64_t tl = i_tile;
         int cc = i_c;
+        for (int s = 0; s < S && lo + s < hi; ++s) {
+            if (lane == 0) {
+                mbar_expect_tx(&bars[s], (uint32_t)C::kWBytes);
+                if constexpr (GG) tma_load_2d(wsm + s * C::kWBytes, &p.wmap, cc * kGgufChunkWords, (int)(tl * kTileRows), &bars[s]);
+                else tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, cc, (int)(tl * kTileRows), &bars[s]);
+            }
+            if (++cc == p.nch) { cc = 0; ++tl; }
+        }
+        const int32_t v = (has_rec && lane <= S + 1 && lo + lane <= p.T) ? __ldg(p.ptile_off + lo + lane) : 0;
         for (int s = 0; s < S && lo + s < hi; ++s) {
             const int32_t r_off = __shfl_sync(0xffffffffu, v, s), r_end = __shfl_sync(0xffffffffu, v, s + 1);
             if (lane == 0) {
                 const int staged = min(r_end - r_off, C::kPcap);
                 rec_of[s] = r_off;
-                if constexpr (XRES) mbar_arrive_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
-                else mbar_expect_tx(&bars[s], (uint32_t)(C::kWBytes + staged * 4));
-                if constexpr (GG) tma_load_2d(wsm + s * C::kWBytes, &p.wmap, cc * kGgufChunkWords, (int)(tl * kTileRows), &bars[s]);
-                else tma_load_4d(wsm + s * C::kWBytes, &p.wmap, 0, 0, cc, (int)(tl * kTileRows), &bars[s]);
+                if constexpr (XRES) mbar_arrive_expect_tx(&bars[s], (uint32_t)(staged * 4));
+                else if (staged > 0) mbar_expect_tx(&bars[s], (uint32_t)(staged * 4));
                 if (staged > 0) bulk_g2s(xrs + s * C::kXRSlot + C::kPOff, p.precs + r_off, (uint32_t)staged * 4, &bars[s]);
             }
-            if (++cc == p.nch) { cc = 0; ++tl; }
         }
         griddep_wait();
         // this launch's epoch (the previous launch on this GPU recorded its own)
