@@ -535,7 +535,6 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES, FMT>::kWarps * 32, 1)
         return (int)(item_owner(tl * p.nch + p.nch - 1, p.T, p.W) - item_owner(tl * p.nch, p.T, p.W));
     };
     auto reduce_split = [&](int64_t tl) {
-        __threadfence();
         const int64_t w_first = item_owner(tl * p.nch, p.T, p.W);
         const int64_t w_last = item_owner(tl * p.nch + p.nch - 1, p.T, p.W);
         // w_first's piece is in its slot 1 when its range began in an earlier
@@ -747,21 +746,24 @@ __global__ void __launch_bounds__(GemvCfg<BMAX, NW, XRES, FMT>::kWarps * 32, 1)
                 // partial tile: publish this piece, the last arriving warp reduces
                 const int pslot = tile == first_tile ? 0 : 1;
                 float *mine = p.partials + (gw * 2 + pslot) * PW;
-                mine[g * BW + 2 * t] = c0;
-                mine[g * BW + 2 * t + 1] = c1;
-                mine[(g + 8) * BW + 2 * t] = c2;
-                mine[(g + 8) * BW + 2 * t + 1] = c3;
+                *reinterpret_cast<float2 *>(mine + g * BW + 2 * t) = make_float2(c0, c1);
+                *reinterpret_cast<float2 *>(mine + (g + 8) * BW + 2 * t) = make_float2(c2, c3);
                 if constexpr (BMAX > 8) {
-                    mine[g * BW + 8 + 2 * t] = d0;
-                    mine[g * BW + 8 + 2 * t + 1] = d1;
-                    mine[(g + 8) * BW + 8 + 2 * t] = d2;
-                    mine[(g + 8) * BW + 8 + 2 * t + 1] = d3;
+                    *reinterpret_cast<float2 *>(mine + g * BW + 8 + 2 * t) = make_float2(d0, d1);
+                    *reinterpret_cast<float2 *>(mine + (g + 8) * BW + 8 + 2 * t) = make_float2(d2, d3);
                 }
-                __threadfence();
+                // the warp's stores, then one acquire-release count: it publishes
+                // them to whichever warp arrives last and, for that warp,
+                // orders its reads of the other pieces after the count
                 __syncwarp();
                 int old = 0;
-                if (lane == 0) old = atomicAdd(p.tile_cnt + tile, 1);
-                if (__shfl_sync(0xffffffffu, old, 0) == pieces_before(tile)) reduce_split(tile);
+                if (lane == 0)
+                    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.tile_cnt + tile) : "memory");
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == pieces_before(tile)) {
+                    __syncwarp();
+                    reduce_split(tile);
+                }
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) ce[k] = co[k] = de[k] = dd[k] = pc[k] = pd[k] = 0.f;
