@@ -1,6 +1,7 @@
 """Host-side logic of the drop-in modules (no GPU): the per-row overflow CSR
 that the reference's Bf16xFused builds (bf16x_fused.py:165-179) converts back
-to the flat overflow table the kernels read."""
+to the flat overflow table the kernels read; the resident-layout cache; the
+GEMV path a GGUF weight takes."""
 import numpy as np
 import torch
 
@@ -90,3 +91,23 @@ def test_resident_cache_keys_on_live_objects():
     gc.collect()
     assert key not in bf._RESIDENT_CACHE          # evicted when its first stream died
     bf.clear_cache()
+
+
+def test_gguf_weight_gemv_path_choice():
+    """GgufWeight reads the blocks in place for the lossy format and takes the
+    resident layout when a side table has entries, unless told otherwise;
+    in_f that is not a multiple of 256 always takes the resident layout."""
+    import torch
+
+    from bfloat16x_b200.bf16x_gguf_block import GgufWeight
+    blocks = torch.zeros(64 * 512 // 32 * 46, dtype=torch.uint8)
+    ro = torch.zeros(65, dtype=torch.int32)
+    empty = (ro, torch.zeros(0, dtype=torch.int16), torch.zeros(0, dtype=torch.int16))
+    some = (ro.clone().fill_(0), torch.zeros(3, dtype=torch.int16), torch.zeros(3, dtype=torch.int16))
+    assert GgufWeight(blocks, 64, 512).gemv_in_place
+    assert GgufWeight(blocks, 64, 512, side=empty).gemv_in_place
+    assert not GgufWeight(blocks, 64, 512, side=some).gemv_in_place
+    assert GgufWeight(blocks, 64, 512, side=some, native=True).gemv_in_place
+    assert not GgufWeight(blocks, 64, 512, native=False).gemv_in_place
+    odd = torch.zeros(64 * 288 // 32 * 46, dtype=torch.uint8)
+    assert not GgufWeight(odd, 64, 288, native=True).gemv_in_place
