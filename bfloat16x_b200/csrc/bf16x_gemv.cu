@@ -860,17 +860,17 @@ static GemvLaunch plan_gemv(int64_t rows, int64_t in_f, int nw) {
 // its sibling and starts fetching its weights (programmatic dependent launch)
 // while this launch's last pieces finish: the chain of small launches in a
 // decode step overlaps (1B decoder 1.607 -> 1.570 ms per token; the 4-shape
-// bench step unchanged).
+// bench step unchanged).  The collective epilogue keeps one CTA of 12.
 // 5..8 rows: 12 with the CTA's activation block (in_f <= 4096 and enough
 // items to repay its copy), else 10, else 8; above 8 rows always 8 (their
 // activation slots fill shared memory).
 static bool xres_for(int64_t T, int64_t nch) { return nch <= kXResChunks && T >= 8192; }
 
-static int warps_for(int64_t batch, int64_t rows, int64_t in_f) {
+static int warps_for(int64_t batch, int64_t rows, int64_t in_f, bool coll = false) {
     const int64_t nch = (in_f + kChunkElems - 1) / kChunkElems;
     const int64_t T = (rows + kTileRows - 1) / kTileRows * nch;
     const bool wide = T * 8 >= nch * (int64_t)device_sms() * 12;
-    if (batch == 1) return wide ? (T < 32768 ? GemvCfg<1, 6>::kWarps : GemvCfg<1, 12>::kWarps) : GemvCfg<1, 8>::kWarps;
+    if (batch == 1) return wide ? (T < 32768 && !coll ? GemvCfg<1, 6>::kWarps : GemvCfg<1, 12>::kWarps) : GemvCfg<1, 8>::kWarps;
     if (batch == 2) return wide ? GemvCfg<2, 12>::kWarps : GemvCfg<2, 8>::kWarps;
     if (batch <= 4) return wide ? GemvCfg<4, 12>::kWarps : GemvCfg<4, 8>::kWarps;
     if (batch <= 8)
@@ -1014,7 +1014,7 @@ static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(layout) | reinterpret_cast<uintptr_t>(precs)) & 15u)
         return set_error(BF16X_ERR_INVALID, "bf16x_gemv: x, layout and records must be 16-byte aligned");
     if (ldy < rows && !peers) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: ldy < rows");
-    const int nw = warps_for(batch, rows, in_f);
+    const int nw = warps_for(batch, rows, in_f, peers != nullptr);
     const GemvLaunch L = plan_gemv(rows, in_f, nw);
     if (!tile_counters) return set_error(BF16X_ERR_INVALID, "bf16x_gemv: tile_counters (ceil(rows/16) zeroed int32) missing");
     if (!scratch || scratch_bytes < scratch_need(L, batch))
