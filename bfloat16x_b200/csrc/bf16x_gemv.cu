@@ -860,7 +860,8 @@ static GemvLaunch plan_gemv(int64_t rows, int64_t in_f, int nw) {
 // its sibling and starts fetching its weights (programmatic dependent launch)
 // while this launch's last pieces finish: the chain of small launches in a
 // decode step overlaps (1B decoder 1.607 -> 1.570 ms per token; the 4-shape
-// bench step unchanged).  The collective epilogue keeps one CTA of 12.
+// bench step unchanged).  The collective epilogue keeps one CTA of 12, and
+// above 8 rows its activation slots.
 // 5..8 rows: 12 with the CTA's activation block (in_f <= 4096 and enough
 // items to repay its copy), else 10, else 8; above 8 rows 8 (7 fit), with the
 // CTA's activation block under the same condition (128256x4096 at 16 rows:
@@ -876,7 +877,7 @@ static int warps_for(int64_t batch, int64_t rows, int64_t in_f, bool coll = fals
     if (batch <= 4) return wide ? GemvCfg<4, 12>::kWarps : GemvCfg<4, 8>::kWarps;
     if (batch <= 8)
         return wide ? (xres_for(T, nch) ? GemvCfg<8, 12, true>::kWarps : GemvCfg<8, 10>::kWarps) : GemvCfg<8, 8>::kWarps;
-    return xres_for(T, nch) ? GemvCfg<16, 8, true>::kWarps : GemvCfg<16, 8>::kWarps;
+    return xres_for(T, nch) && !coll ? GemvCfg<16, 8, true>::kWarps : GemvCfg<16, 8>::kWarps;
 }
 
 // The GGUF form: the same choice without the CTA activation block.
@@ -1061,7 +1062,7 @@ static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint
         if (nw <= 8) return launch_gemv<8, 8>(p, L, st);
         return xres_for(L.T, L.nch) ? launch_gemv<8, 12, true>(p, L, st) : launch_gemv<8, 10>(p, L, st);
     }
-    return xres_for(L.T, L.nch) ? launch_gemv<16, 8, true>(p, L, st) : launch_gemv<16, 8>(p, L, st);
+    return xres_for(L.T, L.nch) && p.nranks == 1 ? launch_gemv<16, 8, true>(p, L, st) : launch_gemv<16, 8>(p, L, st);
 }
 
 }  // namespace bf16x
