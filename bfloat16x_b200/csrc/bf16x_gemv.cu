@@ -57,9 +57,10 @@ constexpr int kXRowBytes = kChunkElems * 2;
 // weight slots of all warps first (16 rows x 384 bytes each, 1024-byte
 // aligned for the 128-byte swizzle), then every warp's activation + record
 // slots, zeros, record offsets and mbarriers.  12-warp configurations get
-// 2-slot rings, 8-warp ones 3-slot rings (see warps_for).
+// 2-slot rings, 8-warp ones 3-slot rings (see warps_for); 9..16 rows with the
+// activation block 1-slot rings.
 //
-// XRES (5..8 activation rows, in_f <= 4096): the whole activation block is
+// XRES (5..16 activation rows, in_f <= 4096): the whole activation block is
 // copied once per CTA into shared memory and every item reads its chunk
 // there, instead of copying a 4 KB slice into its slot; with records staged
 // to 160 words (126 entries) the slots then shrink enough for 12 warps per SM.
@@ -84,7 +85,11 @@ struct GemvCfg {
     // NW = 6: two CTAs per SM (half the shared memory each), see warps_for
     static constexpr int kCtasPerSm = NW == 6 ? 2 : 1;
     static constexpr int kBudget = (kCtasPerSm == 2 ? 110 * 1024 : 224 * 1024) - kXCache;   // slots
-    static constexpr int kWarpsFit = kBudget / (2 * kPerSlot);
+    // 9..16 rows with the CTA's activation block: one slot per warp, so that
+    // 12 warps fit beside the 128 KB block (more warps in flight beat
+    // deeper rings here: 128256x4096 0.203 -> 0.188 ms)
+    static constexpr int kMinStages = (BMAX > 8 && XRES) ? 1 : 2;
+    static constexpr int kWarpsFit = kBudget / (kMinStages * kPerSlot);
     static constexpr int kWarps = NW < kWarpsFit ? NW : kWarpsFit;
     static constexpr int kStagesFit = kBudget / kWarps / kPerSlot;
     static constexpr int kStages = kStagesFit < 3 ? kStagesFit : 3;
@@ -96,7 +101,7 @@ struct GemvCfg {
     static constexpr int kBarOff = kRecOff + kWarps * kStages * 8;
     static constexpr int kCtaOff = kBarOff + kWarps * kStages * 8 + 8;       // after the x barrier: finished warps
     static constexpr int kSmem = kCtaOff + 16 + 1024;                        // + base alignment
-    static_assert(kStages >= 2, "ring too shallow for this configuration");
+    static_assert(kStages >= kMinStages, "ring too shallow for this configuration");
     static_assert(kCtasPerSm == 1 || 2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM must fit");
     static_assert(kWBytes % (kGguf ? 128 : 1024) == 0 && kXRSlot % 128 == 0 && kPOff % 16 == 0 &&
                       kXCOff % 128 == 0, "slot alignment");
@@ -863,9 +868,9 @@ static GemvLaunch plan_gemv(int64_t rows, int64_t in_f, int nw) {
 // bench step unchanged).  The collective epilogue keeps one CTA of 12, and
 // above 8 rows its activation slots.
 // 5..8 rows: 12 with the CTA's activation block (in_f <= 4096 and enough
-// items to repay its copy), else 10, else 8; above 8 rows 8 (7 fit), with the
-// CTA's activation block under the same condition (128256x4096 at 16 rows:
-// 0.209 -> 0.203 ms).
+// items to repay its copy), else 10, else 8; above 8 rows 12 with the CTA's
+// activation block under the same condition (one slot per warp), else 8
+// (7 fit).
 static bool xres_for(int64_t T, int64_t nch) { return nch <= kXResChunks && T >= 8192; }
 
 static int warps_for(int64_t batch, int64_t rows, int64_t in_f, bool coll = false) {
@@ -877,7 +882,7 @@ static int warps_for(int64_t batch, int64_t rows, int64_t in_f, bool coll = fals
     if (batch <= 4) return wide ? GemvCfg<4, 12>::kWarps : GemvCfg<4, 8>::kWarps;
     if (batch <= 8)
         return wide ? (xres_for(T, nch) ? GemvCfg<8, 12, true>::kWarps : GemvCfg<8, 10>::kWarps) : GemvCfg<8, 8>::kWarps;
-    return xres_for(T, nch) && !coll ? GemvCfg<16, 8, true>::kWarps : GemvCfg<16, 8>::kWarps;
+    return xres_for(T, nch) && !coll ? GemvCfg<16, 12, true>::kWarps : GemvCfg<16, 8>::kWarps;
 }
 
 // The GGUF form: the same choice without the CTA activation block.
@@ -1062,7 +1067,7 @@ static int gemv_impl(const uint8_t *layout, const int32_t *ptile_off, const uint
         if (nw <= 8) return launch_gemv<8, 8>(p, L, st);
         return xres_for(L.T, L.nch) ? launch_gemv<8, 12, true>(p, L, st) : launch_gemv<8, 10>(p, L, st);
     }
-    return xres_for(L.T, L.nch) && p.nranks == 1 ? launch_gemv<16, 8, true>(p, L, st) : launch_gemv<16, 8>(p, L, st);
+    return xres_for(L.T, L.nch) && p.nranks == 1 ? launch_gemv<16, 12, true>(p, L, st) : launch_gemv<16, 8>(p, L, st);
 }
 
 }  // namespace bf16x
