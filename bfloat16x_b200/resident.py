@@ -49,12 +49,14 @@ def flat_args(f: dict):
 
 
 _SCRATCH: dict = {}
+_YDT = {torch.bfloat16: BF16X_DTYPE_BF16, torch.float32: BF16X_DTYPE_F32}
 
 
-def gemv_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
-    """GEMV partial-sum scratch for (device, current stream), grown on demand.
-    Its contents never need initialising."""
-    stream = torch.cuda.current_stream(device).cuda_stream
+def gemv_scratch(device: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor:
+    """GEMV partial-sum scratch for (device, stream: default the current one),
+    grown on demand.  Its contents never need initialising."""
+    if stream is None:
+        stream = torch.cuda.current_stream(device).cuda_stream
     key = (device.index, stream)
     ws = _SCRATCH.get(key)
     if ws is None or ws.numel() < nbytes:
@@ -104,6 +106,7 @@ class ResidentWeight:
         self.row0 = int(row0)
         self._n_patches = None
         self._scratch_need = None
+        self._wptrs = None
         # one zeroed counter per 16-row tile, reset by the kernel after use
         self.tile_counters = torch.zeros((self.rows + TILE_ROWS - 1) // TILE_ROWS + 1, dtype=torch.int32,
                                          device=layout.device)
@@ -222,19 +225,31 @@ class ResidentWeight:
         xp = self._prep_x(x2)
         if out is None:
             out = torch.empty((B, self.rows), dtype=out_dtype, device=self.device)
-        ydt = {torch.bfloat16: BF16X_DTYPE_BF16, torch.float32: BF16X_DTYPE_F32}[out.dtype]
+        ydt = _YDT[out.dtype]
         b = None
         if bias is not None:
             b = bias.to(device=self.device, dtype=torch.bfloat16).contiguous()
-        with torch.cuda.device(self.device):
-            if self._scratch_need is None:
-                self._scratch_need = int(_lib.lib().bf16x_gemv_scratch_bytes(self.rows, self.in_f))
-            ws = gemv_scratch(self.device, self._scratch_need)
-            call("bf16x_gemv", ptr(self.layout), ptr(self.ptile_off), ptr(self.precs), self.rows, self.in_f,
-                 ptr(xp), B, xp.stride(0), ptr(b), ptr(out), ydt, out.stride(0), ptr(self.tile_counters),
-                 ptr(ws), ws.numel(),
-                 self._stream())
+        dev = self.device
+        if torch.cuda.current_device() == dev.index:
+            self._launch_gemv(xp, B, b, out, ydt)
+        else:
+            with torch.cuda.device(dev):
+                self._launch_gemv(xp, B, b, out, ydt)
         return out
+
+    def _launch_gemv(self, xp, B, b, out, ydt):
+        """bf16x_gemv on the current device and stream (the per-weight
+        pointers looked up once)."""
+        if self._wptrs is None:
+            self._scratch_need = int(_lib.lib().bf16x_gemv_scratch_bytes(self.rows, self.in_f))
+            self._wptrs = (self.layout.data_ptr(), self.ptile_off.data_ptr(), self.precs.data_ptr(),
+                           self.tile_counters.data_ptr())
+        st = torch.cuda.current_stream().cuda_stream
+        ws = gemv_scratch(self.device, self._scratch_need, st)
+        lay, pto, prc, cnt = self._wptrs
+        _lib.check(_lib.lib().bf16x_gemv(lay, pto, prc, self.rows, self.in_f, xp.data_ptr(), B, xp.stride(0),
+                                         ptr(b), out.data_ptr(), ydt, out.stride(0), cnt, ws.data_ptr(),
+                                         ws.numel(), st), "bf16x_gemv")
 
     def gemv_peers(self, x: torch.Tensor, peers, ll_offset: int, out_total: int, y: torch.Tensor,
                    mode: int = 0, row0: int = 0, bias: torch.Tensor | None = None) -> torch.Tensor:
